@@ -1,0 +1,96 @@
+// hkv_internal.h -- shapes, the page layout and the kernel launch interface
+// shared by the host engine (hkv_engine.cpp) and the kernels (hkv_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hkv {
+
+// The kernels are specialised for the HiggsAudioV3 / Qwen3-4B attention
+// shape: head_dim 128, 4 query heads per KV head, 16-token pages.
+constexpr int kHeadDim = 128;
+constexpr int kGqa = 4;
+constexpr int kPageTokens = 16;
+// One head block: 16 token rows x 128 dims of F16 = 4 KiB, contiguous.
+constexpr int kHeadBlockBytes = kPageTokens * kHeadDim * 2;
+constexpr int kRowBytes = kHeadDim * 2;  // 256 B, 16 chunks of 16 B
+
+// Page layout in HBM (page-major, so a copy-on-write duplicates one
+// contiguous range):
+//   block(page, layer, kv, head) = ((page * n_layers + layer) * 2 + kv) * n_head_kv + head
+//   byte(page, layer, kv, head, row, chunk) =
+//       block * 4096 + row * 256 + (chunk ^ (row & 7)) * 16
+// where kv = 0 for K and 1 for V, row = position % 16 and chunk = dim / 8.
+// The XOR swizzle of the 16-byte chunks makes the eight rows an ldmatrix
+// reads in one phase land in eight different bank groups once a head block
+// has been copied verbatim (TMA bulk copy) into shared memory, while a row
+// stays sixteen 16-byte pieces for the append's vector stores.
+__host__ __device__ inline int64_t head_block_index(int64_t page, int layer, int kv, int head,
+                                                   int n_layers, int n_head_kv) {
+    return ((page * n_layers + layer) * 2 + kv) * n_head_kv + head;
+}
+__host__ __device__ inline int swizzled_chunk(int row, int chunk) { return chunk ^ (row & 7); }
+
+// Device-side error record.  Kernels never trap: a failed bounds check or an
+// expired bounded wait stores its code here (first writer wins) and the
+// kernel returns; hkv_sync_check reads it.
+struct DeviceError {
+    int32_t code;  // 0, kErrBadIndex or kErrTimeout
+    int32_t where; // kernel id
+    int32_t a;
+    int32_t b;
+};
+constexpr int32_t kErrBadIndex = 1;
+constexpr int32_t kErrTimeout = 2;
+
+// Per-batch descriptor, built on the host once per (slot list, lengths) and
+// uploaded in one copy; the pointers below address that device copy.
+struct BatchView {
+    const int32_t *pos;       // [n]   row being appended = rope position (used)
+    const int32_t *ntok;      // [n]   rows attended = used + 1
+    const int32_t *npages;    // [n]   pages covering [0, used]
+    const int32_t *page_off;  // [n+1] prefix sum of npages into pages[]
+    const int32_t *unit_off;  // [n+1] prefix sum of npages * n_head_kv
+    const int32_t *part_off;  // [n*n_head_kv + 1] first partial of each (entry, kv head)
+    const int32_t *pages;     // [page_off[n]] physical pages, entry-major
+    int32_t n;
+    int32_t total_units;      // sum of npages * n_head_kv: one unit = one head block of K and V
+    int32_t units_per_warp;   // stream-K share of one warp
+    int32_t n_parts;
+};
+
+struct PoolView {
+    uint8_t *base;
+    int64_t n_pages;
+    int32_t n_layers;
+    int32_t n_head_kv;
+};
+
+struct RopeView {
+    const float *cos_tab;  // [context][64]
+    const float *sin_tab;
+    int32_t context_length;
+};
+
+// Attention launch geometry (fixed per build).
+constexpr int kAttnWarps = 8;     // consumer warps per CTA, one CTA per SM
+constexpr int kAttnStages = 3;    // TMA ring depth per warp (K+V head block per stage)
+
+void launch_append(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
+                   const float *k, const float *v, bool apply_rope, DeviceError *err,
+                   cudaStream_t stream);
+void launch_append_range(const PoolView &pool, const RopeView &rope, const int32_t *range_pages,
+                         int64_t pos0, int64_t n_tokens, int layer, const float *k, const float *v,
+                         bool apply_rope, DeviceError *err, cudaStream_t stream);
+void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
+                      const float *q, float *part_o, float *part_ml, float scale_log2, int grid,
+                      DeviceError *err, cudaStream_t stream);
+void launch_combine(const BatchView &batch, int n_head_kv, const float *part_o,
+                    const float *part_ml, float *out, cudaStream_t stream);
+void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
+                   int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
+                   cudaStream_t stream);
+size_t attention_smem_bytes();
+
+}  // namespace hkv

@@ -1,0 +1,692 @@
+// hkv_kernels.cu -- sm_100a kernels of the paged KV decode engine.
+//
+//   append_kernel     fused NEOX RoPE (BF16 table) + F32->F16 + row write into
+//                     the row's physical page, one warp per (row, KV head),
+//                     one 16-byte store per lane.
+//   attention_kernel  split-K ("stream-K") flash-decode over all slots of a
+//                     batch: the flattened (slot, KV head, page) unit range is
+//                     cut into equal shares, one per warp; each warp streams
+//                     its head blocks through a private ring of TMA bulk
+//                     copies (cp.async.bulk + mbarrier) and keeps the 4 query
+//                     heads of its KV head together so every K/V byte is read
+//                     from HBM once.  QK^T and PV run on the tensor cores
+//                     (mma.sync m16n8k16, F32 accumulate) with each F32
+//                     operand split into an F16 high part and an F16 residual
+//                     that ride in the otherwise-empty columns of the n=8
+//                     tile, which keeps products at F32 accuracy.  Online
+//                     softmax in base 2 with warp-shuffle reductions; each
+//                     (slot, KV head) share writes a partial (m, l, o).
+//   combine_kernel    log-sum-exp merge of the partials into the head-major
+//                     output.
+//   gather_kernel     logical [pos][kv_head][dim] view of one slot's layer.
+//
+// Waits on mbarriers are bounded (clock64 budget); a kernel that gives up
+// records kErrTimeout in the DeviceError word, drains its own copies (again
+// bounded) and returns.  Bounds checks record kErrBadIndex and skip the
+// access.  No kernel traps.
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "hkv_internal.h"
+
+namespace hkv {
+namespace {
+
+constexpr int kStageBytes = 2 * kHeadBlockBytes;  // K block + V block
+constexpr int kQcStride = 136;                     // halves per staged-query row (272 B)
+constexpr int kQcBytes = 8 * kQcStride * 2;        // 8 rows: 4 heads x {hi, lo}
+constexpr int kPBufBytes = 16 * 16;                // 16 tokens x 8 halves
+constexpr int kWarpSmem = kAttnStages * kStageBytes + kQcBytes + kPBufBytes + 32;
+constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
+constexpr int kWhereAppend = 0;
+constexpr int kWhereAttn = 1;
+constexpr int kWhereGather = 3;
+
+static_assert(kWarpSmem % 16 == 0, "per-warp shared region must keep 16-byte alignment");
+static_assert(kAttnWarps * kWarpSmem <= 227 * 1024, "attention CTA exceeds shared memory");
+
+__device__ __forceinline__ void record_error(DeviceError *err, int code, int where, int a, int b) {
+    if (atomicCAS(&err->code, 0, code) == 0) {
+        err->where = where;
+        err->a = a;
+        err->b = b;
+    }
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------ mbarrier/TMA
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: true when the phase with `parity` completed.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) {
+        return true;
+    }
+    const long long t0 = clock64();
+    while (clock64() - t0 < kWaitBudgetCycles) {
+        if (mbar_try_wait(bar, parity)) {
+            return true;
+        }
+    }
+    return false;
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 1-D bulk copy global -> shared (no tensor map, no multicast), completion
+// reported as transaction bytes on `bar`.  The KV stream is read once per
+// step, so it is marked evict-first in L2.
+__device__ __forceinline__ void tma_load_1d(uint32_t dst, const void *src, uint32_t bytes,
+                                            uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+// ------------------------------------------------------- ldmatrix / mma
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                              uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(addr)
+                 : "memory");
+}
+// D = A(16x16, row) * B(16x8, col) + D, F16 inputs, F32 accumulators.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ float f16_residual(float x) {
+    return __fsub_rn(x, __half2float(__float2half_rn(x)));
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(addr), "r"(0) : "memory");
+}
+
+// NEOX rotation of one (x0, x1) pair with the reference's rounding: two
+// separately rounded products, then a rounded difference / sum (ggml_mul,
+// ggml_sub, ggml_add are separate graph nodes, src/higgs_pipeline.cpp:503-504).
+__device__ __forceinline__ float rope_lo(float x0, float x1, float c, float s) {
+    return __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+}
+__device__ __forceinline__ float rope_hi(float x0, float x1, float c, float s) {
+    return __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+__device__ __forceinline__ void load8(const float *p, float (&x)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(p + 4));
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+// ===================================================================== append
+// One warp per (row, KV head).  Lanes 0-15 write the sixteen 16-byte chunks
+// of the K row, lanes 16-31 those of the V row.
+template <bool kRope, bool kRange>
+__global__ void __launch_bounds__(128) append_kernel(PoolView pool, RopeView rope, BatchView batch,
+                                                     const int32_t *__restrict__ range_pages,
+                                                     int64_t pos0, int64_t n_rows, int layer,
+                                                     const float *__restrict__ k,
+                                                     const float *__restrict__ v,
+                                                     DeviceError *err) {
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int G = pool.n_head_kv;
+    const int64_t row = warp / G;
+    const int head = static_cast<int>(warp - row * G);
+    if (row >= n_rows) {
+        return;
+    }
+    int64_t pos;
+    int64_t page;
+    if (kRange) {
+        pos = pos0 + row;
+        page = range_pages[(pos >> 4) - (pos0 >> 4)];
+    } else {
+        pos = batch.pos[row];
+        page = batch.pages[batch.page_off[row] + (pos >> 4)];
+    }
+    if (page < 0 || page >= pool.n_pages || pos < 0 || pos >= rope.context_length) {
+        if (lane == 0) {
+            record_error(err, kErrBadIndex, kWhereAppend, static_cast<int>(page),
+                         static_cast<int>(pos));
+        }
+        return;
+    }
+    const int r = static_cast<int>(pos & 15);
+    const bool is_v = lane >= 16;
+    const int c = lane & 15;
+    const float *src = (is_v ? v : k) + (row * G + head) * kHeadDim;
+    float y[8];
+    if (is_v || !kRope) {
+        load8(src + c * 8, y);
+    } else {
+        const float *cr = rope.cos_tab + pos * (kHeadDim / 2);
+        const float *sr = rope.sin_tab + pos * (kHeadDim / 2);
+        const int i0 = (c & 7) * 8;  // index into the half
+        float x0[8], x1[8], cs[8], sn[8];
+        load8(src + i0, x0);
+        load8(src + i0 + kHeadDim / 2, x1);
+        load8(cr + i0, cs);
+        load8(sr + i0, sn);
+        if (c < 8) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                y[j] = rope_lo(x0[j], x1[j], cs[j], sn[j]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                y[j] = rope_hi(x0[j], x1[j], cs[j], sn[j]);
+            }
+        }
+    }
+    uint4 packed;
+    packed.x = pack_half2(y[0], y[1]);
+    packed.y = pack_half2(y[2], y[3]);
+    packed.z = pack_half2(y[4], y[5]);
+    packed.w = pack_half2(y[6], y[7]);
+    uint8_t *dst = pool.base +
+                   head_block_index(page, layer, is_v ? 1 : 0, head, pool.n_layers, G) *
+                       kHeadBlockBytes +
+                   r * kRowBytes + swizzled_chunk(r, c) * 16;
+    *reinterpret_cast<uint4 *>(dst) = packed;
+}
+
+// ================================================================== attention
+struct Cursor {
+    int e;      // batch entry
+    int h;      // KV head
+    int i;      // page index within the slot
+    int np;     // pages of entry e
+    int pbase;  // page_off[e]
+};
+
+__device__ __forceinline__ Cursor locate(const BatchView &b, int u) {
+    int lo = 0;
+    int hi = b.n;  // find the last e with unit_off[e] <= u
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (b.unit_off[mid] <= u) {
+            lo = mid;
+        } else {
+            hi = mid;
+        }
+    }
+    Cursor c;
+    c.e = lo;
+    c.np = b.npages[lo];
+    c.pbase = b.page_off[lo];
+    const int rem = u - b.unit_off[lo];
+    c.h = rem / c.np;
+    c.i = rem - c.h * c.np;
+    return c;
+}
+
+__device__ __forceinline__ void advance(const BatchView &b, int G, Cursor &c) {
+    if (++c.i == c.np) {
+        c.i = 0;
+        if (++c.h == G) {
+            c.h = 0;
+            if (++c.e < b.n) {
+                c.np = b.npages[c.e];
+                c.pbase = b.page_off[c.e];
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void issue_unit(const PoolView &pool, const BatchView &b, int layer,
+                                           const Cursor &c, uint32_t stage, uint32_t bar,
+                                           uint64_t policy, DeviceError *err) {
+    int64_t page = b.pages[c.pbase + c.i];
+    if (page < 0 || page >= pool.n_pages) {
+        record_error(err, kErrBadIndex, kWhereAttn, static_cast<int>(page), c.e);
+        page = 0;  // keep the copy in bounds; the result is flagged as invalid
+    }
+    const uint8_t *kb =
+        pool.base +
+        head_block_index(page, layer, 0, c.h, pool.n_layers, pool.n_head_kv) * kHeadBlockBytes;
+    const uint8_t *vb = kb + static_cast<int64_t>(pool.n_head_kv) * kHeadBlockBytes;
+    mbar_arrive_expect_tx(bar, kStageBytes);
+    tma_load_1d(stage, kb, kHeadBlockBytes, bar, policy);
+    tma_load_1d(stage + kHeadBlockBytes, vb, kHeadBlockBytes, bar, policy);
+}
+
+__global__ void __launch_bounds__(kAttnWarps * 32, 1)
+    attention_kernel(PoolView pool, RopeView rope, BatchView batch, int layer,
+                     const float *__restrict__ q, float *__restrict__ part_o,
+                     float *__restrict__ part_ml, float scale_log2, DeviceError *err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int lane = threadIdx.x & 31;
+    const int wid = threadIdx.x >> 5;
+    const int gw = blockIdx.x * kAttnWarps + wid;
+    const int G = pool.n_head_kv;
+    const int Q = batch.units_per_warp;
+    const int u_begin = gw * Q;
+    const int u_end = min(u_begin + Q, batch.total_units);
+    if (u_begin >= u_end) {
+        return;
+    }
+    const uint32_t stage0 = smem_u32(smem + wid * kWarpSmem);
+    const uint32_t qc = stage0 + kAttnStages * kStageBytes;
+    const uint32_t pbuf = qc + kQcBytes;
+    const uint32_t bar0 = pbuf + kPBufBytes;
+    const uint64_t policy = l2_evict_first_policy();
+
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kAttnStages; ++s) {
+            mbar_init(bar0 + 8 * s, 1);
+        }
+        fence_barrier_init();
+    }
+    __syncwarp();
+
+    Cursor cons = locate(batch, u_begin);
+    Cursor prod = cons;
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kAttnStages; ++s) {
+            if (u_begin + s < u_end) {
+                issue_unit(pool, batch, layer, prod, stage0 + s * kStageBytes, bar0 + 8 * s,
+                           policy, err);
+                advance(batch, G, prod);
+            }
+        }
+    }
+
+    const int r7 = lane & 7;
+    const int mi = lane >> 3;
+    // Per-lane byte offsets inside a head block for the ldmatrix row addresses.
+    const int k_row_off = (r7 + ((mi & 1) << 3)) * kRowBytes;
+    const int v_row_off = (r7 + ((mi >> 1) << 3)) * kRowBytes;
+    const int k_chunk_hi = mi >> 1;
+    const int v_chunk_hi = mi & 1;
+    const bool lo_side = (lane & 2) != 0;  // columns 4-7: F16 residual parts
+    const float kNegInf = -INFINITY;
+
+    float o[8][4];
+    uint32_t qb[8][2];
+    float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
+    int part = 0;
+    int ntok = 0;
+
+    auto flush = [&]() {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                o[mt][j] += __shfl_xor_sync(0xffffffffu, o[mt][j], 2);
+            }
+        }
+        l_a += __shfl_xor_sync(0xffffffffu, l_a, 4);
+        l_a += __shfl_xor_sync(0xffffffffu, l_a, 8);
+        l_a += __shfl_xor_sync(0xffffffffu, l_a, 16);
+        l_b += __shfl_xor_sync(0xffffffffu, l_b, 4);
+        l_b += __shfl_xor_sync(0xffffffffu, l_b, 8);
+        l_b += __shfl_xor_sync(0xffffffffu, l_b, 16);
+        if (!lo_side) {
+            const int ha = (lane & 1) * 2;
+            float *po = part_o + static_cast<int64_t>(part) * (kGqa * kHeadDim);
+            const int d0 = lane >> 2;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                po[ha * kHeadDim + 16 * mt + d0] = o[mt][0];
+                po[(ha + 1) * kHeadDim + 16 * mt + d0] = o[mt][1];
+                po[ha * kHeadDim + 16 * mt + d0 + 8] = o[mt][2];
+                po[(ha + 1) * kHeadDim + 16 * mt + d0 + 8] = o[mt][3];
+            }
+            if (d0 == 0) {
+                float *pm = part_ml + static_cast<int64_t>(part) * (2 * kGqa);
+                pm[ha * 2] = m_a;
+                pm[ha * 2 + 1] = l_a;
+                pm[ha * 2 + 2] = m_b;
+                pm[ha * 2 + 3] = l_b;
+            }
+        }
+    };
+
+    for (int u = u_begin, k = 0; u < u_end; ++u, ++k) {
+        const int s = k % kAttnStages;
+        const uint32_t parity = static_cast<uint32_t>(k / kAttnStages) & 1u;
+        if (u == u_begin || cons.i == 0) {
+            if (u != u_begin) {
+                flush();
+            }
+            // ---- new (entry, KV head) share: stage RoPE'd q as F16 hi/lo rows
+            const int e = cons.e;
+            const int h = cons.h;
+            const int pos = batch.pos[e];
+            ntok = batch.ntok[e];
+            const int first_warp = (batch.unit_off[e] + h * cons.np) / Q;
+            part = batch.part_off[e * G + h] + (gw - first_warp);
+            const float *cr = rope.cos_tab + static_cast<int64_t>(pos) * (kHeadDim / 2);
+            const float *sr = rope.sin_tab + static_cast<int64_t>(pos) * (kHeadDim / 2);
+            const float *qe = q + (static_cast<int64_t>(e) * (kGqa * G) + kGqa * h) * kHeadDim;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int i = lane + 32 * half;
+                const float c = __ldg(cr + i);
+                const float sn = __ldg(sr + i);
+#pragma unroll
+                for (int j = 0; j < kGqa; ++j) {
+                    const float x0 = __ldg(qe + j * kHeadDim + i);
+                    const float x1 = __ldg(qe + j * kHeadDim + i + kHeadDim / 2);
+                    const float y0 = rope_lo(x0, x1, c, sn);
+                    const float y1 = rope_hi(x0, x1, c, sn);
+                    const __half h0 = __float2half_rn(y0);
+                    const __half h1 = __float2half_rn(y1);
+                    const __half l0 = __float2half_rn(__fsub_rn(y0, __half2float(h0)));
+                    const __half l1 = __float2half_rn(__fsub_rn(y1, __half2float(h1)));
+                    st_shared_u16(qc + (j * kQcStride + i) * 2, __half_as_ushort(h0));
+                    st_shared_u16(qc + (j * kQcStride + i + 64) * 2, __half_as_ushort(h1));
+                    st_shared_u16(qc + ((j + 4) * kQcStride + i) * 2, __half_as_ushort(l0));
+                    st_shared_u16(qc + ((j + 4) * kQcStride + i + 64) * 2, __half_as_ushort(l1));
+                }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                ldsm_x4(qc + (r7 * kQcStride + jj * 32 + mi * 8) * 2, qb[2 * jj][0],
+                        qb[2 * jj][1], qb[2 * jj + 1][0], qb[2 * jj + 1][1]);
+            }
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    o[mt][j] = 0.f;
+                }
+            }
+            m_a = m_b = kNegInf;
+            l_a = l_b = 0.f;
+        }
+
+        // ---- wait for this unit's K and V head blocks
+        const uint32_t bar = bar0 + 8 * s;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
+        if (!ok) {
+            if (lane == 0) {
+                record_error(err, kErrTimeout, kWhereAttn, u, blockIdx.x);
+            }
+            // Drain the copies this warp still has in flight, then leave.
+            for (int j = 1; j < kAttnStages && u + j < u_end; ++j) {
+                const int kk = k + j;
+                mbar_wait_bounded(bar0 + 8 * (kk % kAttnStages),
+                                  static_cast<uint32_t>(kk / kAttnStages) & 1u);
+            }
+            return;
+        }
+        const uint32_t kt = stage0 + s * kStageBytes;
+        const uint32_t vt = kt + kHeadBlockBytes;
+        const int row0 = cons.i * kPageTokens;
+        const int valid = min(kPageTokens, ntok - row0);
+        if (valid < kPageTokens) {
+            // Rows past the slot's length hold whatever the page had before;
+            // zero them in shared memory so 0 * garbage cannot poison PV.
+            for (int idx = lane; idx < (kPageTokens - valid) * 16; idx += 32) {
+                st_shared_zero16(vt + (valid + (idx >> 4)) * kRowBytes + (idx & 15) * 16);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+        }
+
+        // ---- S^T[token][col] = K[token][:] . Qc[col][:]   (col 0-3 hi, 4-7 lo)
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a0, a1, a2, a3;
+            const int chunk = 2 * ks + k_chunk_hi;
+            ldsm_x4(kt + k_row_off + ((chunk ^ r7) << 4), a0, a1, a2, a3);
+            mma_16816(sc, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], 2);
+        }
+        const int tok = row0 + (lane >> 2);
+        const float s0 = tok < ntok ? sc[0] * scale_log2 : kNegInf;      // head a, row g
+        const float s1 = tok < ntok ? sc[1] * scale_log2 : kNegInf;      // head b, row g
+        const float s2 = tok + 8 < ntok ? sc[2] * scale_log2 : kNegInf;  // head a, row g+8
+        const float s3 = tok + 8 < ntok ? sc[3] * scale_log2 : kNegInf;  // head b, row g+8
+        float mx_a = fmaxf(s0, s2);
+        float mx_b = fmaxf(s1, s3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+        }
+        const float mn_a = fmaxf(m_a, mx_a);
+        const float mn_b = fmaxf(m_b, mx_b);
+        const float alpha_a = exp2f(m_a - mn_a);
+        const float alpha_b = exp2f(m_b - mn_b);
+        const float p0 = exp2f(s0 - mn_a);
+        const float p1 = exp2f(s1 - mn_b);
+        const float p2 = exp2f(s2 - mn_a);
+        const float p3 = exp2f(s3 - mn_b);
+        l_a = l_a * alpha_a + (p0 + p2);
+        l_b = l_b * alpha_b + (p1 + p3);
+        m_a = mn_a;
+        m_b = mn_b;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            o[mt][0] *= alpha_a;
+            o[mt][1] *= alpha_b;
+            o[mt][2] *= alpha_a;
+            o[mt][3] *= alpha_b;
+        }
+        // ---- P^T tile in shared memory: [token][col], hi parts in cols 0-3,
+        // F16 residuals in cols 4-7 (each lane writes its own column pair).
+        const uint32_t w_lo = lo_side ? pack_half2(f16_residual(p0), f16_residual(p1))
+                                      : pack_half2(p0, p1);
+        const uint32_t w_hi = lo_side ? pack_half2(f16_residual(p2), f16_residual(p3))
+                                      : pack_half2(p2, p3);
+        st_shared_u32(pbuf + (lane >> 2) * 16 + (lane & 3) * 4, w_lo);
+        st_shared_u32(pbuf + ((lane >> 2) + 8) * 16 + (lane & 3) * 4, w_hi);
+        __syncwarp();
+        uint32_t pb0, pb1;
+        ldsm_x2_trans(pbuf + (lane & 15) * 16, pb0, pb1);
+
+        // ---- O^T[dim][col] += V^T[dim][token] . P^T[token][col]
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            uint32_t a0, a1, a2, a3;
+            const int chunk = 2 * mt + v_chunk_hi;
+            ldsm_x4_trans(vt + v_row_off + ((chunk ^ r7) << 4), a0, a1, a2, a3);
+            mma_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+        }
+        __syncwarp();
+        if (lane == 0 && u + kAttnStages < u_end) {
+            fence_proxy_async_smem();
+            issue_unit(pool, batch, layer, prod, kt, bar, policy, err);
+            advance(batch, G, prod);
+        }
+        advance(batch, G, cons);
+    }
+    flush();
+}
+
+// ==================================================================== combine
+__global__ void __launch_bounds__(kHeadDim) combine_kernel(BatchView batch, int G,
+                                                           const float *__restrict__ part_o,
+                                                           const float *__restrict__ part_ml,
+                                                           float *__restrict__ out) {
+    const int eh = blockIdx.x;
+    const int e = eh / G;
+    const int h = eh - e * G;
+    const int t = threadIdx.x;
+    const int p0 = batch.part_off[eh];
+    const int p1 = batch.part_off[eh + 1];
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        float mx = -INFINITY;
+        for (int p = p0; p < p1; ++p) {
+            mx = fmaxf(mx, part_ml[p * 2 * kGqa + 2 * j]);
+        }
+        float num = 0.f;
+        float den = 0.f;
+        for (int p = p0; p < p1; ++p) {
+            const float w = exp2f(part_ml[p * 2 * kGqa + 2 * j] - mx);
+            den += w * part_ml[p * 2 * kGqa + 2 * j + 1];
+            num += w * part_o[static_cast<int64_t>(p) * (kGqa * kHeadDim) + j * kHeadDim + t];
+        }
+        out[(static_cast<int64_t>(e) * (kGqa * G) + kGqa * h + j) * kHeadDim + t] = num / den;
+    }
+}
+
+// ===================================================================== gather
+__global__ void gather_kernel(PoolView pool, const int32_t *__restrict__ slot_pages, int64_t pos0,
+                              int64_t n, int layer, uint16_t *__restrict__ k_out,
+                              uint16_t *__restrict__ v_out, DeviceError *err) {
+    const int G = pool.n_head_kv;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t per_row = static_cast<int64_t>(G) * 16;
+    if (idx >= n * per_row) {
+        return;
+    }
+    const int64_t t = idx / per_row;
+    const int rem = static_cast<int>(idx - t * per_row);
+    const int h = rem >> 4;
+    const int c = rem & 15;
+    const int64_t pos = pos0 + t;
+    const int64_t page = slot_pages[pos >> 4];
+    if (page < 0 || page >= pool.n_pages) {
+        record_error(err, kErrBadIndex, kWhereGather, static_cast<int>(page),
+                     static_cast<int>(pos));
+        return;
+    }
+    const int r = static_cast<int>(pos & 15);
+    const int64_t within = r * kRowBytes + swizzled_chunk(r, c) * 16;
+    const uint8_t *kb =
+        pool.base + head_block_index(page, layer, 0, h, pool.n_layers, G) * kHeadBlockBytes;
+    const uint8_t *vb =
+        pool.base + head_block_index(page, layer, 1, h, pool.n_layers, G) * kHeadBlockBytes;
+    const int64_t o = (t * G + h) * kHeadDim + c * 8;
+    *reinterpret_cast<uint4 *>(k_out + o) = *reinterpret_cast<const uint4 *>(kb + within);
+    *reinterpret_cast<uint4 *>(v_out + o) = *reinterpret_cast<const uint4 *>(vb + within);
+}
+
+}  // namespace
+
+size_t attention_smem_bytes() { return static_cast<size_t>(kAttnWarps) * kWarpSmem; }
+
+void launch_append(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
+                   const float *k, const float *v, bool apply_rope, DeviceError *err,
+                   cudaStream_t stream) {
+    const int64_t warps = static_cast<int64_t>(batch.n) * pool.n_head_kv;
+    const int blocks = static_cast<int>((warps + 3) / 4);
+    if (apply_rope) {
+        append_kernel<true, false><<<blocks, 128, 0, stream>>>(pool, rope, batch, nullptr, 0,
+                                                               batch.n, layer, k, v, err);
+    } else {
+        append_kernel<false, false><<<blocks, 128, 0, stream>>>(pool, rope, batch, nullptr, 0,
+                                                                batch.n, layer, k, v, err);
+    }
+}
+
+void launch_append_range(const PoolView &pool, const RopeView &rope, const int32_t *range_pages,
+                         int64_t pos0, int64_t n_tokens, int layer, const float *k, const float *v,
+                         bool apply_rope, DeviceError *err, cudaStream_t stream) {
+    const int64_t warps = n_tokens * pool.n_head_kv;
+    const int blocks = static_cast<int>((warps + 3) / 4);
+    BatchView none{};
+    if (apply_rope) {
+        append_kernel<true, true><<<blocks, 128, 0, stream>>>(pool, rope, none, range_pages, pos0,
+                                                              n_tokens, layer, k, v, err);
+    } else {
+        append_kernel<false, true><<<blocks, 128, 0, stream>>>(pool, rope, none, range_pages,
+                                                               pos0, n_tokens, layer, k, v, err);
+    }
+}
+
+void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
+                      const float *q, float *part_o, float *part_ml, float scale_log2, int grid,
+                      DeviceError *err, cudaStream_t stream) {
+    // The dynamic shared-memory opt-in is per device.
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(attention_smem_bytes()));
+        if (dev >= 0 && dev < 64) {
+            configured[dev] = true;
+        }
+    }
+    attention_kernel<<<grid, kAttnWarps * 32, attention_smem_bytes(), stream>>>(
+        pool, rope, batch, layer, q, part_o, part_ml, scale_log2, err);
+}
+
+void launch_combine(const BatchView &batch, int n_head_kv, const float *part_o,
+                    const float *part_ml, float *out, cudaStream_t stream) {
+    const int blocks = batch.n * n_head_kv;
+    combine_kernel<<<blocks, kHeadDim, 0, stream>>>(batch, n_head_kv, part_o, part_ml, out);
+}
+
+void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
+                   int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
+                   cudaStream_t stream) {
+    const int64_t threads = n * pool.n_head_kv * 16;
+    const int blocks = static_cast<int>((threads + 255) / 256);
+    gather_kernel<<<blocks, 256, 0, stream>>>(pool, slot_pages, pos0, n, layer, k_out, v_out, err);
+}
+
+}  // namespace hkv

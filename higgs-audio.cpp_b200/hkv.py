@@ -1,0 +1,356 @@
+"""ctypes binding of libhkv.so (include/hkv.h) for Python callers and tests.
+
+The binding mirrors the reference's slot API (src/higgs_pipeline.cpp):
+``acquire_backend_kv_cache_slot`` (:1191) -> ``Engine.acquire_backend_kv_cache_slot``
+returning a ``ScopedBackendKvCacheSlot`` context manager whose exit releases
+the slot (:372-403, :1210); engine errors raise ``HkvError`` (a
+``RuntimeError``, as the reference throws ``std::runtime_error``), and
+position errors raise ``HkvRangeError`` (an ``IndexError``, the reference's
+``std::out_of_range`` at :1138-1140).
+
+Compute calls take device pointers (ints, or objects with ``data_ptr()``)
+and a CUDA stream handle (int).  There is no CPU fallback: if the library
+is missing, loading it raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+from pathlib import Path
+from typing import Optional, Sequence
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("HKV_LIB", _PKG / "lib" / "libhkv.so"))
+
+HKV_OK = 0
+HKV_ERR_INVALID = 1
+HKV_ERR_OOM = 2
+HKV_ERR_BAD_SLOT = 3
+HKV_ERR_RANGE = 4
+HKV_ERR_CUDA = 5
+HKV_ERR_TIMEOUT = 6
+HKV_ERR_NO_DEVICE = 7
+HKV_ERR_NOT_FOUND = 8
+HKV_ERR_DEVICE = 9
+
+KERNEL_APPEND = 0
+KERNEL_ATTN = 1
+KERNEL_COMBINE = 2
+KERNEL_GATHER = 3
+KERNEL_STEP = 4
+
+
+class HkvError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class HkvRangeError(HkvError, IndexError):
+    pass
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int32),
+        ("n_head", ctypes.c_int32),
+        ("n_head_kv", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("page_tokens", ctypes.c_int32),
+        ("context_length", ctypes.c_int32),
+        ("rope_freq_base", ctypes.c_float),
+        ("max_slots", ctypes.c_int32),
+        ("n_pages", ctypes.c_int64),
+        ("device", ctypes.c_int32),
+        ("shuffle_seed", ctypes.c_uint32),
+    ]
+
+
+class PrefixKey(ctypes.Structure):
+    _fields_ = [("hash", ctypes.c_uint64), ("n_tokens", ctypes.c_int64)]
+
+
+class PoolStats(ctypes.Structure):
+    _fields_ = [
+        ("n_pages", ctypes.c_int64),
+        ("free_pages", ctypes.c_int64),
+        ("reserved", ctypes.c_int64),
+        ("shared_pages", ctypes.c_int64),
+        ("live_slots", ctypes.c_int32),
+        ("prefixes", ctypes.c_int32),
+        ("page_bytes", ctypes.c_int64),
+        ("cow_copies", ctypes.c_int64),
+    ]
+
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_I32P = ctypes.POINTER(ctypes.c_int32)
+_I64P = ctypes.POINTER(ctypes.c_int64)
+
+# name -> (argtypes, restype); every function declared in include/hkv.h.
+SIGNATURES = {
+    "hkv_abi_version": ([], ctypes.c_int),
+    "hkv_status_string": ([ctypes.c_int], ctypes.c_char_p),
+    "hkv_last_error": ([_P], ctypes.c_char_p),
+    "hkv_config_default": ([ctypes.POINTER(Config)], ctypes.c_int),
+    "hkv_engine_create": ([ctypes.POINTER(Config), ctypes.POINTER(_P)], ctypes.c_int),
+    "hkv_engine_destroy": ([_P], ctypes.c_int),
+    "hkv_slot_acquire": ([_P, _I64, ctypes.POINTER(PrefixKey), _I32P], ctypes.c_int),
+    "hkv_slot_release": ([_P, _I32], ctypes.c_int),
+    "hkv_slot_fork": ([_P, _I32, _I64, _I32P], ctypes.c_int),
+    "hkv_slot_len": ([_P, _I32, _I64P], ctypes.c_int),
+    "hkv_slot_set_len": ([_P, _I32, _I64], ctypes.c_int),
+    "hkv_slot_advance": ([_P, _I32, _I32P, _I64], ctypes.c_int),
+    "hkv_prefix_publish": ([_P, ctypes.POINTER(PrefixKey), _I32], ctypes.c_int),
+    "hkv_prefix_drop": ([_P, ctypes.POINTER(PrefixKey)], ctypes.c_int),
+    "hkv_slot_pages": ([_P, _I32, _I32P, _I64, _I64P], ctypes.c_int),
+    "hkv_pool_stats_get": ([_P, ctypes.POINTER(PoolStats)], ctypes.c_int),
+    "hkv_append": ([_P, _I32, _I32, _I32P, _P, _P, _P], ctypes.c_int),
+    "hkv_rope_append": ([_P, _I32, _I32, _I32P, _P, _P, _P], ctypes.c_int),
+    "hkv_rope_append_range": ([_P, _I32, _I32, _I64, _P, _P, _P], ctypes.c_int),
+    "hkv_decode_attn": ([_P, _I32, _I32, _I32P, _P, _P, _P], ctypes.c_int),
+    "hkv_decode_step": ([_P, _I32, _I32, _I32P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "hkv_gather": ([_P, _I32, _I32, _I64, _I64, _P, _P, _P], ctypes.c_int),
+    "hkv_sync_check": ([_P, _P], ctypes.c_int),
+    "hkv_rope_tables": ([_P, _P, _P], ctypes.c_int),
+    "hkv_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
+    "hkv_profile_reset": ([_P], ctypes.c_int),
+    "hkv_profile_read": ([_P, ctypes.c_int, _I64P, ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+}
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def load_library(path: Optional[os.PathLike] = None) -> ctypes.CDLL:
+    """Loads libhkv.so and declares every entry point; raises if absent."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise ImportError(
+            f"{p} is missing: build it with `python higgs-audio.cpp_b200/hkv_build.py` "
+            "(the engine has no fallback implementation)")
+    lib = ctypes.CDLL(str(p))
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _ptr(x) -> Optional[int]:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return int(x.data_ptr())
+    if isinstance(x, np.ndarray):
+        return int(x.ctypes.data)
+    raise TypeError(f"cannot take a device pointer from {type(x)!r}")
+
+
+def _stream(s) -> Optional[int]:
+    if s is None or s == 0:
+        return None
+    if isinstance(s, int):
+        return s
+    if hasattr(s, "cuda_stream"):
+        return int(s.cuda_stream)
+    raise TypeError(f"cannot take a CUDA stream handle from {type(s)!r}")
+
+
+def _slots_arg(slots: Sequence[int]):
+    arr = (ctypes.c_int32 * len(slots))(*[int(s) for s in slots])
+    return len(slots), arr
+
+
+class ScopedBackendKvCacheSlot:
+    """RAII slot lease (ScopedBackendKvCacheSlot, src/higgs_pipeline.cpp:372-403)."""
+
+    def __init__(self, engine: "Engine", slot: int):
+        self.engine = engine
+        self.slot = slot
+
+    def release(self) -> None:
+        if self.engine is not None and self.slot >= 0:
+            self.engine.release(self.slot)
+        self.engine = None
+        self.slot = -1
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.release()
+        return False
+
+
+class Engine:
+    """One paged KV engine (one page pool on one GPU, or host-only if device=-1)."""
+
+    def __init__(self, n_layers: int = 36, n_head: int = 32, n_head_kv: int = 8,
+                 head_dim: int = 128, page_tokens: int = 16, context_length: int = 32768,
+                 rope_freq_base: float = 1e6, max_slots: int = 256, n_pages: int = 4096,
+                 device: int = 0, shuffle_seed: int = 0, lib: Optional[ctypes.CDLL] = None):
+        self.lib = lib or load_library()
+        self.handle = None
+        self.cfg = Config(n_layers, n_head, n_head_kv, head_dim, page_tokens, context_length,
+                          rope_freq_base, max_slots, n_pages, device, shuffle_seed)
+        h = ctypes.c_void_p()
+        st = self.lib.hkv_engine_create(ctypes.byref(self.cfg), ctypes.byref(h))
+        if st != HKV_OK:
+            raise HkvError(st, f"hkv_engine_create failed: "
+                               f"{self.lib.hkv_status_string(st).decode()}")
+        self.handle = h
+
+    # ---------------------------------------------------------------- misc
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.hkv_engine_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+        return False
+
+    def last_error(self) -> str:
+        return self.lib.hkv_last_error(self.handle).decode()
+
+    def _check(self, st: int) -> None:
+        if st == HKV_OK:
+            return
+        msg = self.last_error()
+        if st == HKV_ERR_RANGE:
+            raise HkvRangeError(st, msg)
+        raise HkvError(st, msg)
+
+    # --------------------------------------------------------------- slots
+    def acquire(self, capacity: int = 0, share: Optional[tuple] = None) -> int:
+        out = ctypes.c_int32()
+        key = PrefixKey(*share) if share is not None else None
+        self._check(self.lib.hkv_slot_acquire(self.handle, capacity,
+                                              ctypes.byref(key) if key else None,
+                                              ctypes.byref(out)))
+        return out.value
+
+    def acquire_backend_kv_cache_slot(self, capacity: int,
+                                      share: Optional[tuple] = None) -> ScopedBackendKvCacheSlot:
+        return ScopedBackendKvCacheSlot(self, self.acquire(capacity, share))
+
+    def release(self, slot: int) -> None:
+        self._check(self.lib.hkv_slot_release(self.handle, slot))
+
+    def fork(self, src: int, n_tokens: int) -> int:
+        out = ctypes.c_int32()
+        self._check(self.lib.hkv_slot_fork(self.handle, src, n_tokens, ctypes.byref(out)))
+        return out.value
+
+    def length(self, slot: int) -> int:
+        out = ctypes.c_int64()
+        self._check(self.lib.hkv_slot_len(self.handle, slot, ctypes.byref(out)))
+        return out.value
+
+    def set_length(self, slot: int, used: int) -> None:
+        self._check(self.lib.hkv_slot_set_len(self.handle, slot, used))
+
+    def advance(self, slots: Sequence[int], n_tokens: int = 1) -> None:
+        n, arr = _slots_arg(slots)
+        self._check(self.lib.hkv_slot_advance(self.handle, n, arr, n_tokens))
+
+    def publish(self, key_hash: int, n_tokens: int, slot: int) -> None:
+        key = PrefixKey(key_hash, n_tokens)
+        self._check(self.lib.hkv_prefix_publish(self.handle, ctypes.byref(key), slot))
+
+    def drop(self, key_hash: int, n_tokens: int) -> None:
+        key = PrefixKey(key_hash, n_tokens)
+        self._check(self.lib.hkv_prefix_drop(self.handle, ctypes.byref(key)))
+
+    def pages(self, slot: int) -> list:
+        n = ctypes.c_int64()
+        self._check(self.lib.hkv_slot_pages(self.handle, slot, None, 0, ctypes.byref(n)))
+        buf = (ctypes.c_int32 * max(1, n.value))()
+        self._check(self.lib.hkv_slot_pages(self.handle, slot, buf, n.value, ctypes.byref(n)))
+        return list(buf[: n.value])
+
+    def stats(self) -> dict:
+        s = PoolStats()
+        self._check(self.lib.hkv_pool_stats_get(self.handle, ctypes.byref(s)))
+        return {f: getattr(s, f) for f, _ in PoolStats._fields_}
+
+    # ------------------------------------------------------------- compute
+    def append(self, layer: int, slots: Sequence[int], k, v, stream=None) -> None:
+        n, arr = _slots_arg(slots)
+        self._check(self.lib.hkv_append(self.handle, layer, n, arr, _ptr(k), _ptr(v),
+                                        _stream(stream)))
+
+    def rope_append(self, layer: int, slots: Sequence[int], k, v, stream=None) -> None:
+        n, arr = _slots_arg(slots)
+        self._check(self.lib.hkv_rope_append(self.handle, layer, n, arr, _ptr(k), _ptr(v),
+                                             _stream(stream)))
+
+    def rope_append_range(self, layer: int, slot: int, n_tokens: int, k, v, stream=None) -> None:
+        self._check(self.lib.hkv_rope_append_range(self.handle, layer, slot, n_tokens, _ptr(k),
+                                                   _ptr(v), _stream(stream)))
+
+    def decode_attn(self, layer: int, slots: Sequence[int], q, out, stream=None) -> None:
+        n, arr = _slots_arg(slots)
+        self._check(self.lib.hkv_decode_attn(self.handle, layer, n, arr, _ptr(q), _ptr(out),
+                                             _stream(stream)))
+
+    def decode_step(self, layer: int, slots: Sequence[int], q, k, v, out, stream=None) -> None:
+        n, arr = _slots_arg(slots)
+        self._check(self.lib.hkv_decode_step(self.handle, layer, n, arr, _ptr(q), _ptr(k),
+                                             _ptr(v), _ptr(out), _stream(stream)))
+
+    def gather(self, slot: int, layer: int, pos0: int, n: int, k_out, v_out, stream=None) -> None:
+        self._check(self.lib.hkv_gather(self.handle, slot, layer, pos0, n, _ptr(k_out),
+                                        _ptr(v_out), _stream(stream)))
+
+    def sync_check(self, stream=None) -> None:
+        self._check(self.lib.hkv_sync_check(self.handle, _stream(stream)))
+
+    def rope_tables(self):
+        half = self.cfg.head_dim // 2
+        cos = np.empty((self.cfg.context_length, half), np.float32)
+        sin = np.empty_like(cos)
+        self._check(self.lib.hkv_rope_tables(self.handle, cos.ctypes.data, sin.ctypes.data))
+        return cos, sin
+
+    # ----------------------------------------------------------- profiling
+    def profile_enable(self, on: bool = True) -> None:
+        self._check(self.lib.hkv_profile_enable(self.handle, 1 if on else 0))
+
+    def profile_reset(self) -> None:
+        self._check(self.lib.hkv_profile_reset(self.handle))
+
+    def profile_read(self, kernel_id: int):
+        n = ctypes.c_int64()
+        ms = ctypes.c_double()
+        self._check(self.lib.hkv_profile_read(self.handle, kernel_id, ctypes.byref(n),
+                                              ctypes.byref(ms)))
+        return n.value, ms.value
+
+
+def header_functions(header: Path) -> list:
+    """Names of the functions a C header declares."""
+    text = Path(header).read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(hkv_[a-z0-9_]+)\s*\(", text)))

@@ -1,0 +1,237 @@
+/*
+ * hkv.h -- C ABI of the B200 paged KV-cache decode engine.
+ *
+ * The engine replaces the per-request KV-slot path of higgs-audio.cpp
+ * (src/higgs_pipeline.cpp): the slot arena (BackendKvCache / BackendRuntime,
+ * :326-403, :1137-1220), the K/V row write into the cache (ggml_set_inplace,
+ * :5748-5749 decode, :6278-6279 window, :6603-6604 prefill), the NEOX RoPE on
+ * the BF16 table (:471-506) and the GQA decode attention chain (:5750-5786).
+ *
+ * Storage model: one page pool per engine (per GPU).  A page holds 16
+ * consecutive token positions of one slot for ALL layers, K and V, all KV
+ * heads, in F16.  Each live slot owns a page list; pages are reference
+ * counted so slots can share a prefix (fork / published prefixes) and are
+ * copied on the first write into a shared page (copy-on-write).
+ *
+ * Conventions:
+ *   * Every function returns an hkv_status; on failure hkv_last_error() holds
+ *     a message and no slot or page state has changed.
+ *   * `slots` arrays are HOST arrays of slot ids.  Tensor arguments of the
+ *     compute calls (q, k, v, out, gather outputs) are DEVICE pointers on the
+ *     engine's GPU, 16-byte aligned; compute calls are ordered on `stream` (a
+ *     cudaStream_t, 0 for the legacy default stream) and return before the
+ *     GPU finishes.
+ *   * Decode step protocol (one new token per slot):
+ *         for layer in [0, n_layers):
+ *             hkv_rope_append(layer, ...)   writes row `used` of each slot
+ *             hkv_decode_attn(layer, ...)   attends rows [0, used]
+ *         hkv_slot_advance(...)             used += 1
+ *     This mirrors the reference's `past = cache.used` for all layers of one
+ *     graph followed by `cache.used += 1` (:5642, :5183).
+ *   * Row layouts follow ggml order: a K/V row is [n_head_kv][head_dim],
+ *     q and the attention output are head-major [n_head][head_dim]; query
+ *     head h reads KV head h / (n_head / n_head_kv) (:441-456).
+ *   * Slot operations are thread-safe (one mutex per engine).  Compute calls
+ *     on one engine share its split-partial buffer: issue them on one stream
+ *     (or order the streams) in the order the GPU should run them.
+ */
+#ifndef HKV_H
+#define HKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HKV_ABI_VERSION 1
+
+typedef enum hkv_status {
+    HKV_OK = 0,
+    HKV_ERR_INVALID = 1,   /* bad argument or unsupported shape              */
+    HKV_ERR_OOM = 2,       /* page pool, reservation or slot table exhausted */
+    HKV_ERR_BAD_SLOT = 3,  /* slot id not live (or released twice)           */
+    HKV_ERR_RANGE = 4,     /* position / length out of range                 */
+    HKV_ERR_CUDA = 5,      /* CUDA runtime error                             */
+    HKV_ERR_TIMEOUT = 6,   /* a bounded device-side wait gave up             */
+    HKV_ERR_NO_DEVICE = 7, /* compute call on a host-only engine             */
+    HKV_ERR_NOT_FOUND = 8, /* unknown prefix key                             */
+    HKV_ERR_DEVICE = 9     /* a kernel's bounds check recorded a bad index   */
+} hkv_status;
+
+typedef struct hkv_engine hkv_engine;
+typedef void *hkv_stream; /* cudaStream_t */
+
+/* Engine shape.  Replaces TextConfig fields the KV path reads
+ * (include/higgs_audio.h:86-100: block_count, head_count, head_count_kv,
+ * key_length, context_length, rope_freq_base) plus pool sizing. */
+typedef struct hkv_config {
+    int32_t n_layers;       /* 36                                              */
+    int32_t n_head;         /* query heads, 32                                 */
+    int32_t n_head_kv;      /* KV heads held by this engine, 8 (or a share)    */
+    int32_t head_dim;       /* 128 (the only value the kernels take)           */
+    int32_t page_tokens;    /* 16 (the only value the kernels take)            */
+    int32_t context_length; /* 32768: RoPE table rows and max positions        */
+    float rope_freq_base;   /* 1e6                                             */
+    int32_t max_slots;      /* slot-table size                                 */
+    int64_t n_pages;        /* pages in the pool                               */
+    int32_t device;         /* CUDA ordinal; -1 = host-only bookkeeping engine */
+    uint32_t shuffle_seed;  /* nonzero: the free list starts in a seeded random
+                               order, so logical pages land on scattered
+                               physical pages (tests, benchmarks)              */
+} hkv_config;
+
+/* Key of a shareable prompt prefix, e.g. a hash of the reference-code cache
+ * key (model, reference wav path, size, mtime: :1545-1551) and the
+ * reference-prompt token count. */
+typedef struct hkv_prefix_key {
+    uint64_t hash;
+    int64_t n_tokens;
+} hkv_prefix_key;
+
+typedef struct hkv_pool_stats {
+    int64_t n_pages;       /* pool size                                       */
+    int64_t free_pages;    /* on the free list                                */
+    int64_t reserved;      /* free pages promised to live slots               */
+    int64_t shared_pages;  /* pages with refcount > 1                         */
+    int32_t live_slots;
+    int32_t prefixes;
+    int64_t page_bytes;    /* bytes of one page (all layers, K and V)         */
+    int64_t cow_copies;    /* pages copied on write since creation            */
+} hkv_pool_stats;
+
+/* Kernel ids for the CUDA-event profiler. */
+typedef enum hkv_kernel_id {
+    HKV_KERNEL_APPEND = 0,
+    HKV_KERNEL_ATTN = 1,
+    HKV_KERNEL_COMBINE = 2,
+    HKV_KERNEL_GATHER = 3,
+    HKV_KERNEL_STEP = 4,
+    HKV_KERNEL_COUNT = 5
+} hkv_kernel_id;
+
+/* ------------------------------------------------------------ engine -- */
+
+/* Qwen3-4B / HiggsAudioV3 backbone shape (docs/spec.md:329-341). */
+int hkv_config_default(hkv_config *cfg);
+
+/* Creates the pool (one device allocation, zero-filled), the BF16 RoPE tables
+ * (make_bf16_rope_table, :475-487, built on the host and uploaded once as in
+ * ensure_backend_kv_rope_tables, :1606-1622) and the split-partial buffer. */
+int hkv_engine_create(const hkv_config *cfg, hkv_engine **out);
+int hkv_engine_destroy(hkv_engine *eng);
+
+/* Message of the last failed call on this engine ("" if none). */
+const char *hkv_last_error(const hkv_engine *eng);
+const char *hkv_status_string(int status);
+int hkv_abi_version(void);
+
+/* ------------------------------------------------------------- slots -- */
+
+/* Rents a slot.  Replaces acquire_backend_kv_cache_slot (:1191-1208).
+ * capacity_hint: positions the request will reach (prompt + steps + 1, as
+ *   the reference's capacity, :4820); the pages it needs beyond a shared
+ *   prefix are reserved so later appends cannot run out (HKV_ERR_OOM here
+ *   instead).  0 reserves nothing.
+ * share: if non-NULL and published, the slot starts with that prefix's pages
+ *   mapped (used = share->n_tokens, copy-on-write); if not published the slot
+ *   starts empty (check hkv_slot_len). */
+int hkv_slot_acquire(hkv_engine *eng, int64_t capacity_hint, const hkv_prefix_key *share,
+                     int32_t *slot_out);
+
+/* Returns a slot.  Replaces ScopedBackendKvCacheSlot::release (:1210-1220).
+ * Drops the slot's page references; a second release is HKV_ERR_BAD_SLOT. */
+int hkv_slot_release(hkv_engine *eng, int32_t slot);
+
+/* New slot sharing the first n_tokens positions of src (copy-on-write).
+ * No reference counterpart (the reference copies whole caches); it is the
+ * primitive behind prefix sharing. */
+int hkv_slot_fork(hkv_engine *eng, int32_t src, int64_t n_tokens, int32_t *dst_out);
+
+/* cache.used of the reference (:340). */
+int hkv_slot_len(const hkv_engine *eng, int32_t slot, int64_t *used_out);
+
+/* Truncates a slot (rollback, e.g. the reference's window refresh that
+ * rewrites rows [start, used), :4837-4842).  used must be <= current. */
+int hkv_slot_set_len(hkv_engine *eng, int32_t slot, int64_t used);
+
+/* used += n_tokens for each slot (the caller's `cache.used += 1`, :5183,
+ * :4925; prefill sets used = P, :4837).  The rows must have been written. */
+int hkv_slot_advance(hkv_engine *eng, int32_t n, const int32_t *slots, int64_t n_tokens);
+
+/* Publishes the first key->n_tokens positions of `slot` under `key`; the
+ * prefix holds its own page references until hkv_prefix_drop. */
+int hkv_prefix_publish(hkv_engine *eng, const hkv_prefix_key *key, int32_t slot);
+int hkv_prefix_drop(hkv_engine *eng, const hkv_prefix_key *key);
+
+/* Physical page ids of a slot (diagnostics and tests). */
+int hkv_slot_pages(const hkv_engine *eng, int32_t slot, int32_t *pages_out, int64_t cap,
+                   int64_t *n_out);
+int hkv_pool_stats_get(const hkv_engine *eng, hkv_pool_stats *out);
+
+/* ----------------------------------------------------------- compute -- */
+
+/* Raw K/V row write at position `used` of each slot, for one layer: the
+ * drop-in for ggml_set_inplace(cache.key, k_cur) / (cache.value, v_cur)
+ * (:5748-5749) when the caller already applied RoPE.  k, v: device
+ * [n][n_head_kv][head_dim] F32, stored as F16 (round to nearest even). */
+int hkv_append(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots, const float *k,
+               const float *v, hkv_stream stream);
+
+/* Fused NEOX RoPE (BF16 table, position `used`, :489-506 / :5735) of the
+ * pre-RoPE k, then the row write of roped k and raw v.  Same shapes. */
+int hkv_rope_append(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
+                    const float *k_prerope, const float *v, hkv_stream stream);
+
+/* Prefill / window writer: positions [used, used + n_tokens) of one slot,
+ * one layer (:6603-6604 prefill at 0, :6278-6279 window at start).
+ * k_prerope, v: device [n_tokens][n_head_kv][head_dim] F32.  Call for every
+ * layer, then hkv_slot_advance(n_tokens). */
+int hkv_rope_append_range(hkv_engine *eng, int32_t layer, int32_t slot, int64_t n_tokens,
+                          const float *k_prerope, const float *v, hkv_stream stream);
+
+/* GQA decode attention of one new token per slot over rows [0, used]
+ * (used + 1 rows, the last one written by this step's append), for one
+ * layer.  Replaces repeat_kv_3d + mul_mat + scale(1/sqrt(head_dim)) +
+ * soft_max + mul_mat + permute/cont (:5750-5786).  q_prerope: device
+ * [n][n_head][head_dim] F32 before RoPE (RoPE at position `used` is applied
+ * inside, :5734).  out: device [n][n_head * head_dim] F32, head-major. */
+int hkv_decode_attn(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
+                    const float *q_prerope, float *out, hkv_stream stream);
+
+/* hkv_rope_append followed by hkv_decode_attn for one layer, in one call
+ * (one descriptor check for both).  Same shapes and results. */
+int hkv_decode_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
+                    const float *q_prerope, const float *k_prerope, const float *v, float *out,
+                    hkv_stream stream);
+
+/* Logical view of one slot/layer: rows [pos0, pos0 + n) as
+ * [n][n_head_kv][head_dim] F16 bits, the layout of the reference's cache
+ * rows (:1137-1142).  Test hook replacing ggml_backend_tensor_get on the
+ * cache (:6980-6981).  k_out, v_out: device pointers. */
+int hkv_gather(hkv_engine *eng, int32_t slot, int32_t layer, int64_t pos0, int64_t n,
+               uint16_t *k_out, uint16_t *v_out, hkv_stream stream);
+
+/* Waits for the engine's stream work, then reports a device-side error
+ * (HKV_ERR_DEVICE / HKV_ERR_TIMEOUT) recorded by a kernel since the last
+ * call, and clears it. */
+int hkv_sync_check(hkv_engine *eng, hkv_stream stream);
+
+/* Host copies of the BF16 RoPE tables, [context_length][head_dim/2] each. */
+int hkv_rope_tables(const hkv_engine *eng, float *cos_out, float *sin_out);
+
+/* ---------------------------------------------------------- profiling -- */
+
+/* When on, every kernel launch is bracketed by CUDA events on its stream;
+ * hkv_profile_read synchronises and returns launches and total device ms
+ * for one kernel id since the last reset. */
+int hkv_profile_enable(hkv_engine *eng, int on);
+int hkv_profile_reset(hkv_engine *eng);
+int hkv_profile_read(hkv_engine *eng, int kernel_id, int64_t *launches, double *total_ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HKV_H */

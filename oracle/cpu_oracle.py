@@ -1,0 +1,183 @@
+"""ctypes view of the CPU oracle (oracle/hkv_oracle.c, oracle/hkv_oracle_graph.c).
+
+TEST AND MEASUREMENT INFRASTRUCTURE.  Imported only by tests/, by
+__graft_entry__.smoke() as the checker, and by bench.py's CPU-baseline leg and
+`--impl reference` arm.  The engine never imports it.
+
+Pinning (see the C file header): append and layout are pinned by the
+reference's known-answer self-checks; the RoPE table formula is compared with
+the reference's own table code compiled from its source (oracle/_ref, when the
+reference checkout is present); the attention numerics are parity-unpinned.
+"""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "liboracle.so"
+
+EXACT = 0
+GGML_F16 = 1
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compiles the oracle with the committed Makefile (gcc, OpenMP)."""
+    srcs = [HERE / "hkv_oracle.c", HERE / "hkv_oracle_graph.c", HERE / "Makefile"]
+    if force or not LIB_PATH.exists() or any(
+            s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in srcs):
+        subprocess.run(["make", "-s", "-C", str(HERE), "-B" if force else "all"], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        L = ctypes.CDLL(str(LIB_PATH))
+        P = ctypes.c_void_p
+        I64 = ctypes.c_int64
+        L.hkvo_bf16_round.argtypes = [ctypes.c_float]
+        L.hkvo_bf16_round.restype = ctypes.c_float
+        L.hkvo_rope_table.argtypes = [I64, I64, ctypes.c_float, P, P]
+        L.hkvo_f32_to_f16.argtypes = [ctypes.c_float]
+        L.hkvo_f32_to_f16.restype = ctypes.c_uint16
+        L.hkvo_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.hkvo_f16_to_f32.restype = ctypes.c_float
+        L.hkvo_f32_to_f16_array.argtypes = [P, P, I64]
+        L.hkvo_f16_to_f32_array.argtypes = [P, P, I64]
+        L.hkvo_rope_neox.argtypes = [P, I64, I64, P, P, P]
+        L.hkvo_append_rows.argtypes = [I64, I64, I64, P, P, P, P, P, ctypes.c_int, P, P]
+        L.hkvo_decode_attn.argtypes = [ctypes.c_int, I64, I64, I64, I64, P, P, P, P, P,
+                                       ctypes.c_float, P]
+        L.hkvo_graph_decode_layer.argtypes = [I64, I64, I64, I64, P, P, P, P, P, P, P, P, P,
+                                              ctypes.c_float, P, P]
+        L.hkvo_graph_work_floats.argtypes = [I64, I64, I64, I64]
+        L.hkvo_graph_work_floats.restype = I64
+        L.hkvo_max_threads.restype = ctypes.c_int
+        L.hkvo_set_threads.argtypes = [ctypes.c_int]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags.c_contiguous
+    return a.ctypes.data
+
+
+def scale(head_dim: int = 128) -> float:
+    """1/sqrt(head_dim) in F32, as the reference computes it (:5767)."""
+    return float(np.float32(1.0) / np.sqrt(np.float32(head_dim)))
+
+
+def rope_table(context_length: int = 32768, key_length: int = 128, base: float = 1e6):
+    half = key_length // 2
+    cos = np.empty((context_length, half), np.float32)
+    sin = np.empty_like(cos)
+    lib().hkvo_rope_table(context_length, key_length, base, _p(cos), _p(sin))
+    return cos, sin
+
+
+def bf16_round(x: float) -> float:
+    return lib().hkvo_bf16_round(x)
+
+
+def f32_to_f16(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, np.float32)
+    out = np.empty(a.shape, np.uint16)
+    lib().hkvo_f32_to_f16_array(_p(a), _p(out), a.size)
+    return out
+
+
+def f16_to_f32(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, np.uint16)
+    out = np.empty(a.shape, np.float32)
+    lib().hkvo_f16_to_f32_array(_p(a), _p(out), a.size)
+    return out
+
+
+def rope_neox(x: np.ndarray, cos_row: np.ndarray, sin_row: np.ndarray) -> np.ndarray:
+    """x: [n_head][head_dim] F32 at one position."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().hkvo_rope_neox(_p(x), x.shape[0], x.shape[1], _p(np.ascontiguousarray(cos_row)),
+                         _p(np.ascontiguousarray(sin_row)), _p(y))
+    return y
+
+
+def append_rows(k: np.ndarray, v: np.ndarray, pos: np.ndarray, cos: np.ndarray,
+                sin: np.ndarray, rope: bool = True):
+    """F16 bits the cache must hold after appending rows k (pre-RoPE), v.
+
+    k, v: [n][n_head_kv][head_dim] F32; pos: [n] positions."""
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    pos = np.ascontiguousarray(pos, np.int32)
+    ko = np.empty(k.shape, np.uint16)
+    vo = np.empty(v.shape, np.uint16)
+    lib().hkvo_append_rows(k.shape[0], k.shape[1], k.shape[2], _p(k), _p(v), _p(pos), _p(cos),
+                           _p(sin), 1 if rope else 0, _p(ko), _p(vo))
+    return ko, vo
+
+
+def decode_attn(q_roped: np.ndarray, k_caches, v_caches, mode: int = EXACT) -> np.ndarray:
+    """Attention of one token per slot over logical F16 caches.
+
+    q_roped: [n][n_head][head_dim] F32; k_caches/v_caches: list of
+    [L_e][n_head_kv][head_dim] uint16 arrays.  Returns [n][n_head*head_dim]."""
+    q = np.ascontiguousarray(q_roped, np.float32)
+    n, H, D = q.shape
+    G = k_caches[0].shape[1]
+    lens = np.array([c.shape[0] for c in k_caches], np.int32)
+    row_off = np.zeros(n, np.int64)
+    row_off[1:] = np.cumsum(lens[:-1])
+    k_all = np.ascontiguousarray(np.concatenate(k_caches, 0), np.uint16)
+    v_all = np.ascontiguousarray(np.concatenate(v_caches, 0), np.uint16)
+    out = np.empty((n, H * D), np.float32)
+    lib().hkvo_decode_attn(mode, n, H, G, D, _p(q), _p(k_all), _p(v_all), _p(row_off), _p(lens),
+                           scale(D), _p(out))
+    return out
+
+
+class GraphBaseline:
+    """The reference's F32 decode graph for one layer over contiguous per-slot
+    caches (hkv_oracle_graph.c): the timed CPU baseline."""
+
+    def __init__(self, n_slots: int, capacity: int, n_head: int = 32, n_head_kv: int = 8,
+                 head_dim: int = 128, cos=None, sin=None):
+        self.n, self.cap, self.H, self.G, self.D = n_slots, capacity, n_head, n_head_kv, head_dim
+        self.k_cache = np.zeros((n_slots * capacity, n_head_kv, head_dim), np.float32)
+        self.v_cache = np.zeros_like(self.k_cache)
+        self.row_off = (np.arange(n_slots, dtype=np.int64) * capacity)
+        work = lib().hkvo_graph_work_floats(capacity, n_head, n_head_kv, head_dim)
+        self.work = np.zeros(int(work), np.float32)
+        if cos is None:
+            cos, sin = rope_table(key_length=head_dim)
+        self.cos, self.sin = np.ascontiguousarray(cos), np.ascontiguousarray(sin)
+        self.out = np.zeros((n_slots, n_head * head_dim), np.float32)
+
+    def decode_layer(self, q_pre, k_pre, v_new, past) -> np.ndarray:
+        past = np.ascontiguousarray(past, np.int32)
+        assert past.max() < self.cap
+        q_pre = np.ascontiguousarray(q_pre, np.float32)
+        k_pre = np.ascontiguousarray(k_pre, np.float32)
+        v_new = np.ascontiguousarray(v_new, np.float32)
+        lib().hkvo_graph_decode_layer(self.n, self.H, self.G, self.D, _p(q_pre), _p(k_pre),
+                                      _p(v_new), _p(self.k_cache), _p(self.v_cache),
+                                      _p(self.row_off), _p(past), _p(self.cos), _p(self.sin),
+                                      scale(self.D), _p(self.work), _p(self.out))
+        return self.out
+
+
+def max_threads() -> int:
+    return lib().hkvo_max_threads()
+
+
+def set_threads(n: int) -> None:
+    lib().hkvo_set_threads(n)
