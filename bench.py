@@ -1,0 +1,463 @@
+"""Decode-attention + KV-append throughput of the paged KV engine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload scaleout|batched16]
+
+One process per GPU (torchrun for N > 1).  A step is one decode step of every
+slot on the rank: for each of the 36 layers, the fused RoPE + K/V append of
+one row per slot and the GQA decode attention over each slot's whole context
+(hkv_rope_append + hkv_decode_attn), then the length advance.
+
+Workloads (synthetic N(0,1) data, random physical page order):
+  scaleout   (default) the per-GPU share of the 8xB200 scale-out config:
+             32 slots per GPU, contexts uniform in [2048, 16384] (seeded per
+             rank), so N GPUs run 32N slots (weak scaling, no collective).
+  batched16  16 slots, contexts uniform in [256, 4096], one GPU.
+
+Reported: `value` = tokens/s over all ranks (slots advanced one position
+through all 36 layers per second), device-timed with CUDA events, max over
+ranks, inputs resident in HBM (the KV read per step, tens of GB, is far
+larger than the 126 MB L2, so no flush is needed); `e2e` = the same metric
+through the C ABI with q/k/v copied in from pinned host memory and the
+attention output copied back every layer; `roofline` of the attention kernel
+(live per-launch CUDA events); `cpu_baseline` = the reference's F32 GGML
+decode graph restated in C (oracle/hkv_oracle_graph.c) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "higgs-audio.cpp_b200"))
+
+H, G, D = 32, 8, 128
+N_LAYERS = 36  # --layers overrides it for small profiler captures (same per-launch sizes)
+METRIC = "decode-attn+KV-append tokens/s (all slots), % of HBM peak, at 1/2/4/8 B200"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+def workload(name: str, rank: int):
+    import synth
+    if name == "scaleout":
+        n = 32
+        lens = synth.uniform_int(1000 + rank, n, 2048, 16384)
+        desc = ("scale-out shard: 32 slots per GPU, contexts U[2048,16384], 36 layers, "
+                "F16 KV in 16-token pages (permuted), GQA 32/8, head_dim 128")
+    elif name == "batched16":
+        n = 16
+        lens = synth.uniform_int(2000 + rank, n, 256, 4096)
+        desc = ("batched paged decode: 16 slots, contexts U[256,4096], 36 layers, F16 KV in "
+                "16-token pages (permuted), GQA 32/8, head_dim 128")
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    return [int(x) for x in lens], desc
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------- CPU baseline
+def cpu_baseline(lens, budget_s: float = 12.0, max_sample_slots: int = 2):
+    """Times the reference's F32 decode graph (oracle restatement) on the host
+    cores for a bounded sample of the workload and scales it to the whole
+    workload's tokens/s (CPU cost is linear in the context length)."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import cpu_oracle
+    cpu_oracle.build()
+    cores = cpu_oracle.max_threads()
+    sample = sorted(range(len(lens)), key=lambda i: lens[i])[len(lens) // 2:][:max_sample_slots]
+    sl = [lens[i] for i in sample]
+    cap = max(sl) + 1
+    base = cpu_oracle.GraphBaseline(len(sl), cap)
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((len(sl), H, D), dtype=np.float32)
+    k = rng.standard_normal((len(sl), G, D), dtype=np.float32)
+    v = rng.standard_normal((len(sl), G, D), dtype=np.float32)
+    past = np.array(sl, np.int32)
+    base.decode_layer(q, k, v, past)  # warm-up (first touch of caches and scratch)
+    t0 = time.perf_counter()
+    calls = 0
+    while True:
+        base.decode_layer(q, k, v, past)
+        calls += 1
+        if time.perf_counter() - t0 >= budget_s or calls >= 200:
+            break
+    dt = time.perf_counter() - t0
+    per_token_row = dt / calls / sum(s + 1 for s in sl)  # seconds per attended row per layer
+    step_s = per_token_row * N_LAYERS * sum(L + 1 for L in lens)
+    return {
+        "value": len(lens) / step_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+        "sample": (f"{calls} single-layer decode graphs of {len(sl)} slots (contexts {sl}), "
+                   f"F32 cache, materialised GQA repeat, {dt:.1f} s; scaled by context "
+                   f"length to all {len(lens)} slots x {N_LAYERS} layers"),
+    }, step_s
+
+
+# ------------------------------------------------------------------ ours
+def prefill(eng, slots, lens, stream, gen, dev):
+    import torch
+    sh = stream.cuda_stream
+    chunk = 4096
+    with torch.cuda.stream(stream):
+        for s, L in zip(slots, lens):
+            done = 0
+            while done < L:
+                t = min(chunk, L - done)
+                for layer in range(N_LAYERS):
+                    k = torch.randn((t, G, D), generator=gen, device=dev)
+                    v = torch.randn((t, G, D), generator=gen, device=dev)
+                    eng.rope_append_range(layer, s, t, k, v, sh)
+                eng.advance([s], t)
+                done += t
+    eng.sync_check(sh)
+
+
+def bench_ours(args):
+    import torch
+    import hkv
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    lens, desc = workload(args.workload, rank)
+    n = len(lens)
+    total_steps = args.warmup + args.steps + args.e2e_steps + 2
+    n_pages = sum((L + total_steps + 15) // 16 + 1 for L in lens) + 16
+    dev = f"cuda:{local}"
+    eng = hkv.Engine(n_layers=N_LAYERS, n_pages=n_pages, max_slots=n, device=local,
+                     shuffle_seed=0x5EED + rank)
+    stream = torch.cuda.Stream(device=local)
+    sh = stream.cuda_stream
+    slots = [eng.acquire(L + total_steps) for L in lens]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    prefill(eng, slots, lens, stream, gen, dev)
+
+    # Step inputs, resident in HBM: q [36][n][32][128], k/v [36][n][8][128] F32.
+    q = torch.randn((N_LAYERS, n, H, D), generator=gen, device=dev)
+    k = torch.randn((N_LAYERS, n, G, D), generator=gen, device=dev)
+    v = torch.randn((N_LAYERS, n, G, D), generator=gen, device=dev)
+    out = torch.empty((N_LAYERS, n, H * D), device=dev)
+
+    def step():
+        for layer in range(N_LAYERS):
+            eng.rope_append(layer, slots, k[layer], v[layer], sh)
+            eng.decode_attn(layer, slots, q[layer], out[layer], sh)
+        eng.advance(slots, 1)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    eng.sync_check(sh)
+
+    # ---------------- device-timed region (inputs resident)
+    ctx_before = [eng.length(s) + 1 for s in slots]  # rows attended in the first timed step
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    eng.profile_reset()
+    eng.profile_enable(True)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            step()
+    ev1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    eng.profile_enable(False)
+    ms_local = ev0.elapsed_time(ev1)
+    attn_launches, attn_ms = eng.profile_read(hkv.KERNEL_ATTN)
+    app_launches, app_ms = eng.profile_read(hkv.KERNEL_APPEND)
+    comb_launches, comb_ms = eng.profile_read(hkv.KERNEL_COMBINE)
+    eng.sync_check(sh)
+    ms = max_over_ranks(ms_local)
+
+    # Algorithmic bytes: per (slot, layer, step) with L rows attended:
+    # 4096 L (K+V F16 read) + 4096 (append write) + 8192 (k,v in) + 16384 (q in)
+    # + 16384 (out); the attention kernel alone reads 4096 L + 16384 (q).
+    rows = sum(L + s for L in ctx_before for s in range(args.steps))
+    step_bytes_local = N_LAYERS * (4096 * rows + 45056 * n * args.steps) / args.steps
+    attn_bytes_launch = (4096 * rows + 16384 * n * args.steps) / args.steps
+    tokens_total = sum_over_ranks(n * args.steps)
+    step_bytes_all = sum_over_ranks(step_bytes_local)
+    value = tokens_total / (ms / 1e3)
+    peak, peak_kind = measured_peaks()
+    attn_avg_ms = attn_ms / max(attn_launches, 1)
+    attn_gbs = attn_bytes_launch / (attn_avg_ms / 1e3) / 1e9
+    step_gbs_per_gpu = step_bytes_all / world / (ms / args.steps / 1e3) / 1e9
+
+    # ---------------- end to end through the C ABI from pinned host buffers
+    e2e = None
+    if args.e2e_steps > 0:
+        hq = torch.randn((N_LAYERS, n, H, D)).pin_memory()
+        hk = torch.randn((N_LAYERS, n, G, D)).pin_memory()
+        hv = torch.randn((N_LAYERS, n, G, D)).pin_memory()
+        hout = torch.empty((N_LAYERS, n, H * D)).pin_memory()
+        h2d = torch.cuda.Stream(device=local)
+        d2h = torch.cuda.Stream(device=local)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        in_ev = [torch.cuda.Event() for _ in range(N_LAYERS)]
+        out_ev = [torch.cuda.Event() for _ in range(N_LAYERS)]
+
+        def e2e_step():
+            # Inputs of layer l+1 stream in while layer l computes; the output
+            # of layer l streams out while layer l+1 computes.
+            for layer in range(N_LAYERS):
+                with torch.cuda.stream(h2d):
+                    dq[layer].copy_(hq[layer], non_blocking=True)
+                    dk[layer].copy_(hk[layer], non_blocking=True)
+                    dv[layer].copy_(hv[layer], non_blocking=True)
+                    in_ev[layer].record(h2d)
+            for layer in range(N_LAYERS):
+                stream.wait_event(in_ev[layer])
+                eng.rope_append(layer, slots, dk[layer], dv[layer], sh)
+                eng.decode_attn(layer, slots, dq[layer], out[layer], sh)
+                out_ev[layer].record(stream)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(out_ev[layer])
+                    hout[layer].copy_(out[layer], non_blocking=True)
+            eng.advance(slots, 1)
+            stream.wait_stream(d2h)
+            h2d.wait_stream(stream)  # next step's inputs overwrite dq/dk/dv
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        h2d.wait_stream(stream)
+        e0.record(h2d)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+        e2e_tokens = sum_over_ranks(n * args.e2e_steps)
+        h2d_bytes = N_LAYERS * n * (H * D + 2 * G * D) * 4
+        d2h_bytes = N_LAYERS * n * H * D * 4
+        e2e = {"value": e2e_tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+               "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
+               "path": "pinned host q/k/v -> hkv_rope_append + hkv_decode_attn -> pinned host out"}
+    eng.sync_check(sh)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu, _ = cpu_baseline(lens)
+
+    if rank == 0:
+        traffic = None
+        tfile = REPO / "profiles" / "attention_traffic.json"
+        if tfile.exists():
+            t = json.loads(tfile.read_text())
+            if t.get("workload") == args.workload:
+                traffic = t.get("dram_bytes_per_launch")
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16 KV, f32 accumulate",
+            "data": "synthetic N(0,1) (torch generator on device), random physical page order",
+            "config": {
+                "workload": desc,
+                "slots_per_gpu": n,
+                "global_batch": int(tokens_total / args.steps),
+                "layers": N_LAYERS,
+                "mean_context": float(np.mean(lens)),
+                "seq_len": "per-slot contexts, see workload",
+                "parallelism": f"slot-sharded x{world} (no collective)",
+                "l2": "inputs larger than L2: %.1f GB of KV read per step per GPU" % (
+                    step_bytes_local / 1e9),
+            },
+            "hbm": {"step_gbs_per_gpu": step_gbs_per_gpu, "peak_gbs": peak,
+                    "frac": step_gbs_per_gpu / peak, "peak_kind": peak_kind},
+            "roofline": {
+                "kernel": "attention_kernel (split-K flash-decode)",
+                "bound": "hbm", "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
+                "frac": attn_gbs / peak, "traffic": traffic,
+                "algorithmic_bytes_per_launch": attn_bytes_launch,
+                "avg_launch_ms": attn_avg_ms, "peak_kind": peak_kind,
+            },
+            "kernels_ms_per_step": {
+                "attention": attn_ms / args.steps, "append": app_ms / args.steps,
+                "combine": comb_ms / args.steps},
+            "gpu_launches": int(attn_launches + app_launches + comb_launches),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def bench_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    lens = []
+    for r in range(world):
+        lens += workload(args.workload, r)[0]
+    _, desc = workload(args.workload, 0)
+    t0 = time.perf_counter()
+    cpu, step_s = cpu_baseline(lens, budget_s=max(3.0, 2.0 * (args.steps + args.warmup)))
+    wall = time.perf_counter() - t0
+    line = {
+        "metric": METRIC,
+        "value": cpu["value"],
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (the reference's F32 cache and graph)",
+        "data": "synthetic N(0,1)",
+        "impl": "reference",
+        "config": {"workload": desc, "global_batch": len(lens), "layers": N_LAYERS,
+                   "parallelism": "host cores (the reference has no multi-GPU path)"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": ("the reference's GGML CPU graph cannot be built here (ggml submodule "
+                 "absent); this times its restatement in oracle/hkv_oracle_graph.c on "
+                 f"{cpu['cores']} threads; wall {wall:.1f} s"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="scaleout")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=36,
+                    help="layers per step (36 for every reported number; fewer only for "
+                         "profiler captures of the same per-launch sizes)")
+    args = ap.parse_args()
+    global N_LAYERS
+    N_LAYERS = args.layers
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        bench_reference(args)
+    else:
+        bench_ours(args)
+
+
+if __name__ == "__main__":
+    main()

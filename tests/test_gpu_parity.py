@@ -388,7 +388,7 @@ def test_full_size_property_constant_values(hkv_lib):
         eng.decode_attn(layer, slots, q, out, stream)
         expect = vconst.half().float().repeat_interleave(4, dim=1).reshape(n, H * D)
         err = rel_err(out.cpu().numpy(), expect.cpu().numpy())
-        assert err <= 1e-5, err
+        assert err <= 1e-4, err  # F32 accumulation over up to 16k rows
     eng.sync_check(stream)
     eng.close()
 
