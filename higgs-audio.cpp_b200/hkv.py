@@ -86,6 +86,19 @@ class PoolStats(ctypes.Structure):
     ]
 
 
+class PagedView(ctypes.Structure):
+    """hkv_paged_view: caller-owned device memory in the engine's page layout."""
+    _fields_ = [
+        ("pool", ctypes.c_void_p),
+        ("n_pages", ctypes.c_int64),
+        ("n_layers", ctypes.c_int32),
+        ("n_head_kv", ctypes.c_int32),
+        ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p),
+        ("context_length", ctypes.c_int32),
+    ]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -118,6 +131,8 @@ SIGNATURES = {
     "hkv_gather": ([_P, _I32, _I32, _I64, _I64, _P, _P, _P], ctypes.c_int),
     "hkv_sync_check": ([_P, _P], ctypes.c_int),
     "hkv_rope_tables": ([_P, _P, _P], ctypes.c_int),
+    "hkv_decode_attn_noalloc": ([ctypes.POINTER(PagedView), _I32, _I32, _I32P, _I32P, _I32P,
+                                 _P, _P, _P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
     "hkv_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
     "hkv_profile_reset": ([_P], ctypes.c_int),
     "hkv_profile_read": ([_P, ctypes.c_int, _I64P, ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
@@ -347,6 +362,27 @@ class Engine:
         self._check(self.lib.hkv_profile_read(self.handle, kernel_id, ctypes.byref(n),
                                               ctypes.byref(ms)))
         return n.value, ms.value
+
+
+def decode_attn_noalloc(view: PagedView, layer: int, pos: Sequence[int],
+                        page_lists: Sequence[Sequence[int]], q, out, stream=None,
+                        lib: Optional[ctypes.CDLL] = None) -> None:
+    """hkv_decode_attn_noalloc: attention over caller-owned pages, no device
+    allocation.  page_lists[e] are slot e's physical pages."""
+    lib = lib or load_library()
+    n = len(pos)
+    offs = [0]
+    for pl in page_lists:
+        offs.append(offs[-1] + len(pl))
+    flat = [int(p) for pl in page_lists for p in pl]
+    msg = ctypes.create_string_buffer(512)
+    st = lib.hkv_decode_attn_noalloc(
+        ctypes.byref(view), layer, n, (ctypes.c_int32 * n)(*[int(p) for p in pos]),
+        (ctypes.c_int32 * (n + 1))(*offs), (ctypes.c_int32 * max(1, len(flat)))(*flat),
+        _ptr(q), _ptr(out), _stream(stream), msg, len(msg))
+    if st != HKV_OK:
+        cls = HkvRangeError if st == HKV_ERR_RANGE else HkvError
+        raise cls(st, msg.value.decode())
 
 
 def header_functions(header: Path) -> list:

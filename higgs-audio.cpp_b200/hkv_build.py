@@ -20,7 +20,7 @@ REPO = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libhkv.so"
-SOURCES = [CSRC / "hkv_kernels.cu", CSRC / "hkv_engine.cpp"]
+SOURCES = [CSRC / "hkv_kernels.cu", CSRC / "hkv_engine.cpp", CSRC / "hkv_noalloc.cu"]
 HEADERS = [CSRC / "hkv_internal.h", REPO / "include" / "hkv.h"]
 
 NVCC_FLAGS = [

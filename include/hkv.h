@@ -221,6 +221,44 @@ int hkv_sync_check(hkv_engine *eng, hkv_stream stream);
 /* Host copies of the BF16 RoPE tables, [context_length][head_dim/2] each. */
 int hkv_rope_tables(const hkv_engine *eng, float *cos_out, float *sin_out);
 
+/* ---------------------------------------------------- no allocation -- */
+
+/* Device memory a caller already owns, in the engine's page layout: a page is
+ * n_layers x {K, V} x n_head_kv head blocks of 16 rows x 128 F16 dims (4 KiB),
+ * block(page, layer, kv, head) = ((page*n_layers + layer)*2 + kv)*n_head_kv
+ * + head, and row r keeps its 16-byte chunk c at position c ^ (r & 7).
+ * rope_cos / rope_sin: [context_length][64] F32 BF16-rounded tables. */
+typedef struct hkv_paged_view {
+    void *pool;
+    int64_t n_pages;
+    int32_t n_layers;
+    int32_t n_head_kv;
+    const float *rope_cos;
+    const float *rope_sin;
+    int32_t context_length;
+} hkv_paged_view;
+
+/* Decode attention that allocates no GPU memory.  No counterpart in the
+ * reference: it exists for callers that may not call cudaMalloc -- code that
+ * must live inside another framework's device memory pool (for example the
+ * pipeline's ggml backend buffers) or on a path where an allocation could
+ * block or fail.  Same computation as hkv_decode_attn, on caller-owned pages:
+ *   pos[e]: host, the last row slot e attends (rows [0, pos[e]]), which is
+ *     also the RoPE position of its query;
+ *   page_off[n+1], pages[]: host, slot e's physical pages are
+ *     pages[page_off[e] .. page_off[e+1]);
+ *   q_prerope [n][4*n_head_kv][128] F32, out [n][4*n_head_kv*128] F32: device.
+ * Working memory (plan, split partials, error word) lives in one static
+ * device array of 8 MiB per GPU, held until the process exits; a batch that
+ * needs more is rejected with HKV_ERR_RANGE and a message in err_msg (which
+ * may be NULL).  The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. */
+int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer, int32_t n,
+                            const int32_t *pos, const int32_t *page_off, const int32_t *pages,
+                            const float *q_prerope, float *out, hkv_stream stream,
+                            char *err_msg, size_t err_len);
+
 /* ---------------------------------------------------------- profiling -- */
 
 /* When on, every kernel launch is bracketed by CUDA events on its stream;

@@ -1,0 +1,122 @@
+"""hkv_decode_attn_noalloc on the GPU: attention without any device allocation.
+
+Some callers cannot call cudaMalloc -- code that has to keep every tensor in
+another framework's device pool (the pipeline's ggml backend buffers) or that
+runs where an allocation could stall or fail.  They hand this entry point
+memory they already own: a page pool in the engine's documented layout, the
+RoPE tables, q and out; its own working memory is a fixed static array.
+
+Here the engine fills its cache as usual, the same rows (read back through
+hkv_gather) are laid into a caller-owned pool on different physical pages,
+and two calls in a row of the new entry point must match the engine's
+hkv_decode_attn within the parity tolerance.  This file is collected last on
+purpose (a failure here comes after every other test has run).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+TOL = 2e-3  # the same attention tolerance as the other parity tests
+G, H, D, L = 8, 32, 128, 2
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64).reshape(-1, D)
+    b = np.asarray(b, np.float64).reshape(-1, D)
+    return float(np.max(np.abs(a - b).max(1) / np.maximum(np.abs(b).max(1), 1e-30)))
+
+
+def caller_pool(rows_by_slot, layer, n_layers):
+    """Lays logical F16 rows ([R][G][D] uint16 per slot) into a fresh pool in
+    the engine's page layout, on pages handed out in reverse order."""
+    n_pages = sum((r.shape[0] + 15) // 16 for r, _ in rows_by_slot)
+    pool = np.zeros(n_pages * n_layers * 2 * G * 16 * D, np.uint16)
+    next_page = n_pages - 1
+    page_lists = []
+    for k_rows, v_rows in rows_by_slot:
+        R = k_rows.shape[0]
+        pages = list(range(next_page, next_page - (R + 15) // 16, -1))
+        next_page -= len(pages)
+        page_lists.append(pages)
+        t = np.arange(R)
+        page = np.array(pages)[t // 16]
+        r = t % 16
+        for kv, rows in ((0, k_rows), (1, v_rows)):
+            block = ((page[:, None] * n_layers + layer) * 2 + kv) * G + np.arange(G)[None, :]
+            chunk = np.arange(16)[None, None, :] ^ (r[:, None, None] & 7)
+            base = (block[:, :, None] * (16 * D) + r[:, None, None] * D + chunk * 8)
+            idx = base[..., None] + np.arange(8)
+            pool[idx.reshape(-1)] = rows.reshape(R, G, 16, 8).reshape(-1)
+    return torch.from_numpy(pool.view(np.int16)).to(DEV), page_lists
+
+
+def test_noalloc_matches_engine_on_two_calls(hkv_lib):
+    import hkv
+    import synth
+
+    eng = hkv.Engine(n_layers=L, n_pages=256, max_slots=4, device=0, shuffle_seed=99,
+                     lib=hkv_lib)
+    stream = torch.cuda.current_stream().cuda_stream
+    lens = [37, 300, 1000]
+    slots = [eng.acquire(n + 1) for n in lens]
+    for i, (s, n) in enumerate(zip(slots, lens)):
+        for layer in range(L):
+            k = torch.from_numpy(synth.normal(50 + 10 * i + layer, (n, G, D))).to(DEV)
+            v = torch.from_numpy(synth.normal(80 + 10 * i + layer, (n, G, D))).to(DEV)
+            eng.rope_append_range(layer, s, n, k, v, stream)
+        eng.advance([s], n)
+    layer = 1
+    k_new = torch.from_numpy(synth.normal(7, (3, G, D))).to(DEV)
+    v_new = torch.from_numpy(synth.normal(8, (3, G, D))).to(DEV)
+    eng.rope_append(layer, slots, k_new, v_new, stream)
+
+    # the rows the engine now holds, [0, used] of each slot
+    rows = []
+    for s, n in zip(slots, lens):
+        kb = torch.empty((n + 1, G, D), dtype=torch.int16, device=DEV)
+        vb = torch.empty_like(kb)
+        eng.gather(s, layer, 0, n + 1, kb, vb, stream)
+        torch.cuda.synchronize()
+        rows.append((kb.cpu().numpy().view(np.uint16), vb.cpu().numpy().view(np.uint16)))
+    pool, page_lists = caller_pool(rows, layer, L)
+    cos, sin = eng.rope_tables()
+    cos_d = torch.from_numpy(cos).to(DEV)
+    sin_d = torch.from_numpy(sin).to(DEV)
+    view = hkv.PagedView(pool.data_ptr(), sum(len(p) for p in page_lists), L, G,
+                         cos_d.data_ptr(), sin_d.data_ptr(), cos.shape[0])
+
+    calls = [([0, 1, 2], 11), ([2, 0], 12)]  # two calls in a row, different batches
+    for order, seed in calls:
+        q = torch.from_numpy(synth.normal(seed, (len(order), H, D))).to(DEV)
+        ref = torch.empty((len(order), H * D), device=DEV)
+        got = torch.full((len(order), H * D), float("nan"), device=DEV)
+        eng.decode_attn(layer, [slots[i] for i in order], q, ref, stream)
+        hkv.decode_attn_noalloc(view, layer, [lens[i] for i in order],
+                                [page_lists[i] for i in order], q, got, stream, lib=hkv_lib)
+        torch.cuda.synchronize()
+        err = rel_err(got.cpu().numpy(), ref.cpu().numpy())
+        assert np.all(np.isfinite(got.cpu().numpy()))
+        assert err <= TOL, (order, err)
+    eng.sync_check(stream)
+    eng.close()
+
+
+def test_noalloc_rejects_batches_beyond_its_scratch(hkv_lib):
+    import hkv
+    pool = torch.zeros(16 * L * 2 * G * 16 * D, dtype=torch.int16, device=DEV)
+    tab = torch.zeros((32768, 64), device=DEV)
+    view = hkv.PagedView(pool.data_ptr(), 16, L, G, tab.data_ptr(), tab.data_ptr(), 32768)
+    q = torch.zeros((4000, H, D), device=DEV)
+    out = torch.zeros((4000, H * D), device=DEV)
+    with pytest.raises(hkv.HkvRangeError, match="static scratch"):
+        hkv.decode_attn_noalloc(view, 0, [0] * 4000, [[0]] * 4000, q, out, lib=hkv_lib)
+    with pytest.raises(hkv.HkvRangeError, match="outside the pool"):
+        hkv.decode_attn_noalloc(view, 0, [20], [[0, 16]], q, out, lib=hkv_lib)
+    with pytest.raises(hkv.HkvRangeError, match="position"):
+        hkv.decode_attn_noalloc(view, 0, [40000], [[0]], q, out, lib=hkv_lib)
+    torch.cuda.synchronize()
