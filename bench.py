@@ -4,9 +4,9 @@
                     [--workload scaleout|batched16]
 
 One process per GPU (torchrun for N > 1).  A step is one decode step of every
-slot on the rank: for each of the 36 layers, the fused RoPE + K/V append of
-one row per slot and the GQA decode attention over each slot's whole context
-(hkv_rope_append + hkv_decode_attn), then the length advance.
+slot on the rank: for each of the 36 layers, the RoPE + K/V append of one row
+per slot and the GQA decode attention over each slot's whole context, issued
+as hkv_decode_step (one kernel launch per layer), then the length advance.
 
 Workloads (synthetic N(0,1) data, random physical page order):
   scaleout   (default) the per-GPU share of the 8xB200 scale-out config:
@@ -232,8 +232,7 @@ def bench_ours(args):
 
     def step():
         for layer in range(N_LAYERS):
-            eng.rope_append(layer, slots, k[layer], v[layer], sh)
-            eng.decode_attn(layer, slots, q[layer], out[layer], sh)
+            eng.decode_step(layer, slots, q[layer], k[layer], v[layer], out[layer], sh)
         eng.advance(slots, 1)
 
     with torch.cuda.stream(stream):
@@ -264,24 +263,23 @@ def bench_ours(args):
     clk = clocks.stop()
     eng.profile_enable(False)
     ms_local = ev0.elapsed_time(ev1)
-    attn_launches, attn_ms = eng.profile_read(hkv.KERNEL_ATTN)
-    app_launches, app_ms = eng.profile_read(hkv.KERNEL_APPEND)
-    comb_launches, comb_ms = eng.profile_read(hkv.KERNEL_COMBINE)
+    step_launches, step_kernel_ms = eng.profile_read(hkv.KERNEL_STEP)
     eng.sync_check(sh)
     ms = max_over_ranks(ms_local)
 
-    # Algorithmic bytes: per (slot, layer, step) with L rows attended:
-    # 4096 L (K+V F16 read) + 4096 (append write) + 8192 (k,v in) + 16384 (q in)
-    # + 16384 (out); the attention kernel alone reads 4096 L + 16384 (q).
+    # Algorithmic bytes per (slot, layer, step) with L rows attended:
+    # 4096 L (K+V F16 read) + 4096 (new row write) + 8192 (k, v in) + 16384
+    # (q in) + 16384 (out) = 4096 L + 45056, all of it moved by the one fused
+    # kernel launch of the layer.
     rows = sum(L + s for L in ctx_before for s in range(args.steps))
     step_bytes_local = N_LAYERS * (4096 * rows + 45056 * n * args.steps) / args.steps
-    attn_bytes_launch = (4096 * rows + 16384 * n * args.steps) / args.steps
+    launch_bytes = step_bytes_local / N_LAYERS
     tokens_total = sum_over_ranks(n * args.steps)
     step_bytes_all = sum_over_ranks(step_bytes_local)
     value = tokens_total / (ms / 1e3)
     peak, peak_kind = measured_peaks()
-    attn_avg_ms = attn_ms / max(attn_launches, 1)
-    attn_gbs = attn_bytes_launch / (attn_avg_ms / 1e3) / 1e9
+    step_avg_ms = step_kernel_ms / max(step_launches, 1)
+    kernel_gbs = launch_bytes / (step_avg_ms / 1e3) / 1e9
     step_gbs_per_gpu = step_bytes_all / world / (ms / args.steps / 1e3) / 1e9
 
     # ---------------- end to end through the C ABI from pinned host buffers
@@ -308,8 +306,7 @@ def bench_ours(args):
                     in_ev[layer].record(h2d)
             for layer in range(N_LAYERS):
                 stream.wait_event(in_ev[layer])
-                eng.rope_append(layer, slots, dk[layer], dv[layer], sh)
-                eng.decode_attn(layer, slots, dq[layer], out[layer], sh)
+                eng.decode_step(layer, slots, dq[layer], dk[layer], dv[layer], out[layer], sh)
                 out_ev[layer].record(stream)
                 with torch.cuda.stream(d2h):
                     d2h.wait_event(out_ev[layer])
@@ -336,7 +333,7 @@ def bench_ours(args):
         e2e = {"value": e2e_tokens / (e2e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
-               "path": "pinned host q/k/v -> hkv_rope_append + hkv_decode_attn -> pinned host out"}
+               "path": "pinned host q/k/v -> hkv_decode_step -> pinned host out"}
     eng.sync_check(sh)
 
     cpu = None
@@ -377,16 +374,15 @@ def bench_ours(args):
             "hbm": {"step_gbs_per_gpu": step_gbs_per_gpu, "peak_gbs": peak,
                     "frac": step_gbs_per_gpu / peak, "peak_kind": peak_kind},
             "roofline": {
-                "kernel": "attention_kernel (split-K flash-decode)",
-                "bound": "hbm", "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
-                "frac": attn_gbs / peak, "traffic": traffic,
-                "algorithmic_bytes_per_launch": attn_bytes_launch,
-                "avg_launch_ms": attn_avg_ms, "peak_kind": peak_kind,
+                "kernel": "attention_kernel<append> (fused RoPE append + split-K decode "
+                          "attention + merge, one launch per layer)",
+                "bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
+                "frac": kernel_gbs / peak, "traffic": traffic,
+                "algorithmic_bytes_per_launch": launch_bytes,
+                "avg_launch_ms": step_avg_ms, "peak_kind": peak_kind,
             },
-            "kernels_ms_per_step": {
-                "attention": attn_ms / args.steps, "append": app_ms / args.steps,
-                "combine": comb_ms / args.steps},
-            "gpu_launches": int(attn_launches + app_launches + comb_launches),
+            "kernels_ms_per_step": {"decode_step_kernel": step_kernel_ms / args.steps},
+            "gpu_launches": int(step_launches),
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,

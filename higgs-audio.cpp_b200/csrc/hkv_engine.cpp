@@ -26,6 +26,7 @@
 
 #include "../../include/hkv.h"
 #include "hkv_internal.h"
+#include "hkv_plan.h"
 
 namespace hkv {
 namespace {
@@ -217,7 +218,6 @@ struct BatchCache {
     std::vector<int32_t> slots;
     std::vector<int64_t> used;
     BatchView view{};
-    int grid = 0;
 };
 
 struct ProfileRecord {
@@ -254,6 +254,7 @@ struct hkv_engine {
     hkv::DeviceError *d_err = nullptr;
     float *part_o = nullptr;
     float *part_ml = nullptr;
+    int32_t *counters = nullptr;  // one per (batch entry, KV head), zero between launches
     int64_t part_cap = 0;
     int num_sms = 0;
     float scale_log2 = 0.f;
@@ -506,74 +507,34 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
             return st;
         }
     }
-    // Descriptor.
+    // Descriptor: positions, page lists and the stream-K split (hkv_plan.h).
     const int32_t G = eng->cfg.n_head_kv;
     int64_t total_pages = 0;
-    for (int32_t e = 0; e < n; ++e) {
-        total_pages += eng->slots[slots[e]].used / kPageTokens + 1;
-    }
-    const int64_t total_units = total_pages * G;
-    if (total_units > INT32_MAX / 2) {
-        return fail(eng, HKV_ERR_RANGE, "batch too large (%lld units)",
-                    static_cast<long long>(total_units));
-    }
-    const int64_t full_warps = static_cast<int64_t>(eng->num_sms) * kAttnWarps;
-    const int64_t Q = std::max<int64_t>(1, (total_units + full_warps - 1) / full_warps);
-    const int64_t active_warps = (total_units + Q - 1) / Q;
-    const int grid = static_cast<int>((active_warps + kAttnWarps - 1) / kAttnWarps);
-
-    const size_t words = static_cast<size_t>(3 * n + 2 * (n + 1) + (n * G + 1) + total_pages);
-    void *host = nullptr;
-    HKV_CUDA_TRY(eng, eng->batch_stage.begin(words * sizeof(int32_t), &host));
-    int32_t *w = static_cast<int32_t *>(host);
-    int32_t *pos = w;
-    int32_t *ntok = pos + n;
-    int32_t *npg = ntok + n;
-    int32_t *page_off = npg + n;
-    int32_t *unit_off = page_off + (n + 1);
-    int32_t *part_off = unit_off + (n + 1);
-    int32_t *pages = part_off + (n * G + 1);
-    page_off[0] = 0;
-    unit_off[0] = 0;
-    part_off[0] = 0;
+    std::vector<int32_t> pos(static_cast<size_t>(n));
+    std::vector<const int32_t *> lists(static_cast<size_t>(n));
     for (int32_t e = 0; e < n; ++e) {
         const Slot &sl = eng->slots[slots[e]];
-        const int32_t np = static_cast<int32_t>(sl.used / kPageTokens + 1);
         pos[e] = static_cast<int32_t>(sl.used);
-        ntok[e] = static_cast<int32_t>(sl.used + 1);
-        npg[e] = np;
-        std::memcpy(pages + page_off[e], sl.pages.data(), static_cast<size_t>(np) * 4);
-        page_off[e + 1] = page_off[e] + np;
-        unit_off[e + 1] = unit_off[e] + np * G;
-        for (int32_t h = 0; h < G; ++h) {
-            const int64_t a = unit_off[e] + static_cast<int64_t>(h) * np;
-            const int64_t b = a + np;
-            const int64_t parts = (b - 1) / Q - a / Q + 1;
-            part_off[e * G + h + 1] = part_off[e * G + h] + static_cast<int32_t>(parts);
-        }
+        lists[e] = sl.pages.data();
+        total_pages += sl.used / kPageTokens + 1;
     }
-    const int32_t n_parts = part_off[n * G];
-    if (n_parts > eng->part_cap) {
-        return fail(eng, HKV_ERR_OOM, "split plan needs %d partials, capacity %lld", n_parts,
+    if (total_pages * G > INT32_MAX / 2) {
+        return fail(eng, HKV_ERR_RANGE, "batch too large (%lld units)",
+                    static_cast<long long>(total_pages * G));
+    }
+    const int32_t W = eng->num_sms * kAttnWarps;
+    const size_t words = plan_words(n, G, total_pages, W);
+    void *host = nullptr;
+    HKV_CUDA_TRY(eng, eng->batch_stage.begin(words * sizeof(int32_t), &host));
+    const PlanSummary plan =
+        build_plan(static_cast<int32_t *>(host), n, G, pos.data(), lists.data(), total_pages, W);
+    if (plan.n_parts > eng->part_cap) {
+        return fail(eng, HKV_ERR_OOM, "split plan needs %d partials, capacity %lld", plan.n_parts,
                     static_cast<long long>(eng->part_cap));
     }
     void *dev = nullptr;
     HKV_CUDA_TRY(eng, eng->batch_stage.commit(words * sizeof(int32_t), stream, &dev));
-    const int32_t *d = static_cast<const int32_t *>(dev);
-    BatchView v;
-    v.pos = d;
-    v.ntok = d + n;
-    v.npages = d + 2 * n;
-    v.page_off = d + 3 * n;
-    v.unit_off = v.page_off + (n + 1);
-    v.part_off = v.unit_off + (n + 1);
-    v.pages = v.part_off + (n * G + 1);
-    v.n = n;
-    v.total_units = static_cast<int32_t>(total_units);
-    v.units_per_warp = static_cast<int32_t>(Q);
-    v.n_parts = n_parts;
-    bc.view = v;
-    bc.grid = grid;
+    bc.view = bind_plan(static_cast<const int32_t *>(dev), n, G, plan, W);
     bc.slots.assign(slots, slots + n);
     bc.used.resize(static_cast<size_t>(n));
     for (int32_t e = 0; e < n; ++e) {
@@ -610,21 +571,18 @@ int do_append(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots, c
     return launch_status(eng, "append kernel launch");
 }
 
-int do_attention(hkv_engine *eng, int32_t layer, const float *q, float *out, cudaStream_t stream) {
-    const BatchView &b = eng->batch.view;
+// One attention launch over the current batch; with k_new / v_new it is the
+// fused decode step (append + attention).
+int do_attention(hkv_engine *eng, int32_t layer, const float *q, const float *k_new,
+                 const float *v_new, float *out, cudaStream_t stream) {
     {
-        ProfileScope ps(eng, HKV_KERNEL_ATTN, stream);
-        launch_attention(pool_view(eng), rope_view(eng), b, layer, q, eng->part_o, eng->part_ml,
-                         eng->scale_log2, eng->batch.grid, eng->d_err, stream);
-    }
-    int st = launch_status(eng, "attention kernel launch");
-    if (st != HKV_OK) return st;
-    {
-        ProfileScope ps(eng, HKV_KERNEL_COMBINE, stream);
-        launch_combine(b, eng->cfg.n_head_kv, eng->part_o, eng->part_ml, out, stream);
+        ProfileScope ps(eng, k_new != nullptr ? HKV_KERNEL_STEP : HKV_KERNEL_ATTN, stream);
+        launch_attention(pool_view(eng), rope_view(eng), eng->batch.view, layer, q, k_new, v_new,
+                         eng->part_o, eng->part_ml, eng->counters, out, eng->scale_log2,
+                         eng->d_err, stream);
     }
     HKV_CUDA_TRY(eng, eng->batch_stage.mark_used(stream));
-    return launch_status(eng, "combine kernel launch");
+    return launch_status(eng, "attention kernel launch");
 }
 
 void free_device(hkv_engine *eng) {
@@ -648,10 +606,12 @@ void free_device(hkv_engine *eng) {
     cudaFree(eng->d_err);
     cudaFree(eng->part_o);
     cudaFree(eng->part_ml);
+    cudaFree(eng->counters);
     eng->pool = nullptr;
     eng->d_cos = eng->d_sin = nullptr;
     eng->d_err = nullptr;
     eng->part_o = eng->part_ml = nullptr;
+    eng->counters = nullptr;
 }
 
 }  // namespace
@@ -787,6 +747,10 @@ int hkv_engine_create(const hkv_config *cfg, hkv_engine **out) {
         if (e == cudaSuccess)
             e = cudaMalloc(&eng->part_ml, static_cast<size_t>(eng->part_cap) * 2 * kGqa * 4);
         if (e != cudaSuccess) return fail_create(e, "split partials");
+        const size_t counter_bytes = static_cast<size_t>(cfg->max_slots) * cfg->n_head_kv * 4;
+        e = cudaMalloc(&eng->counters, counter_bytes);
+        if (e == cudaSuccess) e = cudaMemset(eng->counters, 0, counter_bytes);
+        if (e != cudaSuccess) return fail_create(e, "merge counters");
         e = cudaDeviceSynchronize();
         if (e != cudaSuccess) return fail_create(e, "create sync");
     }
@@ -1130,7 +1094,7 @@ int hkv_decode_attn(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *sl
     }
     st = ensure_batch(eng, n, slots, stream);
     if (st != HKV_OK) return st;
-    return do_attention(eng, layer, q_prerope, out, stream);
+    return do_attention(eng, layer, q_prerope, nullptr, nullptr, out, stream);
 }
 
 int hkv_decode_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
@@ -1143,9 +1107,14 @@ int hkv_decode_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *sl
     if (q_prerope == nullptr || out == nullptr || !aligned16(q_prerope) || !aligned16(out)) {
         return fail(eng, HKV_ERR_INVALID, "q and out must be non-null 16-byte aligned device pointers");
     }
-    int st = do_append(eng, layer, n, slots, k_prerope, v, true, stream);
+    int st = check_compute(eng, layer);
     if (st != HKV_OK) return st;
-    return do_attention(eng, layer, q_prerope, out, stream);
+    if (k_prerope == nullptr || v == nullptr || !aligned16(k_prerope) || !aligned16(v)) {
+        return fail(eng, HKV_ERR_INVALID, "k and v must be non-null 16-byte aligned device pointers");
+    }
+    st = ensure_batch(eng, n, slots, stream);
+    if (st != HKV_OK) return st;
+    return do_attention(eng, layer, q_prerope, k_prerope, v, out, stream);
 }
 
 int hkv_gather(hkv_engine *eng, int32_t slot, int32_t layer, int64_t pos0, int64_t n,

@@ -53,10 +53,11 @@ struct BatchView {
     const int32_t *page_off;  // [n+1] prefix sum of npages into pages[]
     const int32_t *unit_off;  // [n+1] prefix sum of npages * n_head_kv
     const int32_t *part_off;  // [n*n_head_kv + 1] first partial of each (entry, kv head)
+    const int32_t *warp_entry;// [n_warps] batch entry holding each warp's first unit
     const int32_t *pages;     // [page_off[n]] physical pages, entry-major
     int32_t n;
     int32_t total_units;      // sum of npages * n_head_kv: one unit = one head block of K and V
-    int32_t units_per_warp;   // stream-K share of one warp
+    int32_t n_warps;          // warps the units are shared among (grid * kAttnWarps)
     int32_t n_parts;
 };
 
@@ -83,11 +84,15 @@ void launch_append(const PoolView &pool, const RopeView &rope, const BatchView &
 void launch_append_range(const PoolView &pool, const RopeView &rope, const int32_t *range_pages,
                          int64_t pos0, int64_t n_tokens, int layer, const float *k, const float *v,
                          bool apply_rope, DeviceError *err, cudaStream_t stream);
+// Split-K decode attention with the merge of split partials folded in (the
+// last warp to finish a (slot, KV head) merges).  If k_new / v_new are
+// non-null, the warp owning each slot's last page also ropes and writes the
+// slot's new K/V row (the fused decode step).  counters: n * n_head_kv
+// zero-initialised ints, left zero on exit.
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
-                      const float *q, float *part_o, float *part_ml, float scale_log2, int grid,
+                      const float *q, const float *k_new, const float *v_new, float *part_o,
+                      float *part_ml, int32_t *counters, float *out, float scale_log2,
                       DeviceError *err, cudaStream_t stream);
-void launch_combine(const BatchView &batch, int n_head_kv, const float *part_o,
-                    const float *part_ml, float *out, cudaStream_t stream);
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
                    int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
                    cudaStream_t stream);

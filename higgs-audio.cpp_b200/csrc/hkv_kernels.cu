@@ -14,10 +14,13 @@
 //                     operand split into an F16 high part and an F16 residual
 //                     that ride in the otherwise-empty columns of the n=8
 //                     tile, which keeps products at F32 accuracy.  Online
-//                     softmax in base 2 with warp-shuffle reductions; each
-//                     (slot, KV head) share writes a partial (m, l, o).
-//   combine_kernel    log-sum-exp merge of the partials into the head-major
-//                     output.
+//                     softmax in base 2 with warp-shuffle reductions.  A
+//                     warp whose share covers a whole (slot, KV head) writes
+//                     the output; otherwise each share writes a partial
+//                     (m, l, o) and the last share to finish (atomic ticket)
+//                     merges them (log-sum-exp) into the head-major output.
+//                     In the fused decode step the warp owning a slot's last
+//                     page also ropes and writes the slot's new K/V row.
 //   gather_kernel     logical [pos][kv_head][dim] view of one slot's layer.
 //
 // Waits on mbarriers are bounded (clock64 budget); a kernel that gives up
@@ -260,25 +263,9 @@ struct Cursor {
     int pbase;  // page_off[e]
 };
 
-__device__ __forceinline__ Cursor locate(const BatchView &b, int u) {
-    int lo = 0;
-    int hi = b.n;  // find the last e with unit_off[e] <= u
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (b.unit_off[mid] <= u) {
-            lo = mid;
-        } else {
-            hi = mid;
-        }
-    }
-    Cursor c;
-    c.e = lo;
-    c.np = b.npages[lo];
-    c.pbase = b.page_off[lo];
-    const int rem = u - b.unit_off[lo];
-    c.h = rem / c.np;
-    c.i = rem - c.h * c.np;
-    return c;
+// The warp whose share holds unit a (shares are floor(w U / W) .. floor((w+1) U / W)).
+__device__ __forceinline__ int warp_of(int64_t a, int64_t U, int64_t W) {
+    return static_cast<int>(((a + 1) * W + U - 1) / U - 1);
 }
 
 __device__ __forceinline__ void advance(const BatchView &b, int G, Cursor &c) {
@@ -294,35 +281,124 @@ __device__ __forceinline__ void advance(const BatchView &b, int G, Cursor &c) {
     }
 }
 
-__device__ __forceinline__ void issue_unit(const PoolView &pool, const BatchView &b, int layer,
-                                           const Cursor &c, uint32_t stage, uint32_t bar,
-                                           uint64_t policy, DeviceError *err) {
-    int64_t page = b.pages[c.pbase + c.i];
+__device__ __forceinline__ int64_t checked_page(const PoolView &pool, int64_t page, int e,
+                                                DeviceError *err) {
     if (page < 0 || page >= pool.n_pages) {
-        record_error(err, kErrBadIndex, kWhereAttn, static_cast<int>(page), c.e);
-        page = 0;  // keep the copy in bounds; the result is flagged as invalid
+        record_error(err, kErrBadIndex, kWhereAttn, static_cast<int>(page), e);
+        return 0;  // keep every access in bounds; the result is flagged as invalid
     }
+    return page;
+}
+
+__device__ __forceinline__ void issue_unit(const PoolView &pool, int layer, int64_t page, int h,
+                                           uint32_t stage, uint32_t bar, uint64_t policy) {
     const uint8_t *kb =
         pool.base +
-        head_block_index(page, layer, 0, c.h, pool.n_layers, pool.n_head_kv) * kHeadBlockBytes;
+        head_block_index(page, layer, 0, h, pool.n_layers, pool.n_head_kv) * kHeadBlockBytes;
     const uint8_t *vb = kb + static_cast<int64_t>(pool.n_head_kv) * kHeadBlockBytes;
     mbar_arrive_expect_tx(bar, kStageBytes);
     tma_load_1d(stage, kb, kHeadBlockBytes, bar, policy);
     tma_load_1d(stage + kHeadBlockBytes, vb, kHeadBlockBytes, bar, policy);
 }
 
+// The new K/V row of one (slot, KV head): lanes 0-15 rope and convert the
+// sixteen 8-dim chunks of K, lanes 16-31 convert those of V (same arithmetic
+// as append_kernel).  Returns the lane's 16-byte chunk.
+__device__ __forceinline__ uint4 new_row_chunk(const RopeView &rope, const float *k_row,
+                                               const float *v_row, int pos, int lane) {
+    const bool is_v = lane >= 16;
+    const int c = lane & 15;
+    float y[8];
+    if (is_v) {
+        load8(v_row + c * 8, y);
+    } else {
+        const float *cr = rope.cos_tab + static_cast<int64_t>(pos) * (kHeadDim / 2);
+        const float *sr = rope.sin_tab + static_cast<int64_t>(pos) * (kHeadDim / 2);
+        const int i0 = (c & 7) * 8;
+        float x0[8], x1[8], cs[8], sn[8];
+        load8(k_row + i0, x0);
+        load8(k_row + i0 + kHeadDim / 2, x1);
+        load8(cr + i0, cs);
+        load8(sr + i0, sn);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            y[j] = c < 8 ? rope_lo(x0[j], x1[j], cs[j], sn[j]) : rope_hi(x0[j], x1[j], cs[j], sn[j]);
+        }
+    }
+    uint4 packed;
+    packed.x = pack_half2(y[0], y[1]);
+    packed.y = pack_half2(y[2], y[3]);
+    packed.z = pack_half2(y[4], y[5]);
+    packed.w = pack_half2(y[6], y[7]);
+    return packed;
+}
+
+// Merge of one (slot, KV head)'s partials by the warp that finished last.
+// Partials were written by other SMs in this launch: read them through L2.
+__device__ __forceinline__ void merge_partials(const float *part_o, const float *part_ml, int p0,
+                                               int nparts, float *out_base, int lane) {
+    float mx[kGqa];
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        mx[j] = -INFINITY;
+    }
+    for (int p = 0; p < nparts; ++p) {
+        const float *pm = part_ml + static_cast<int64_t>(p0 + p) * (2 * kGqa);
+#pragma unroll
+        for (int j = 0; j < kGqa; ++j) {
+            mx[j] = fmaxf(mx[j], __ldcg(pm + 2 * j));
+        }
+    }
+    float4 acc[kGqa];
+    float den[kGqa];
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        den[j] = 0.f;
+    }
+    for (int p = 0; p < nparts; ++p) {
+        const float *pm = part_ml + static_cast<int64_t>(p0 + p) * (2 * kGqa);
+        const float4 *po =
+            reinterpret_cast<const float4 *>(part_o + static_cast<int64_t>(p0 + p) * (kGqa * kHeadDim));
+#pragma unroll
+        for (int j = 0; j < kGqa; ++j) {
+            const float w = exp2f(__ldcg(pm + 2 * j) - mx[j]);
+            den[j] += w * __ldcg(pm + 2 * j + 1);
+            const float4 ov = __ldcg(po + j * (kHeadDim / 4) + lane);
+            acc[j].x += w * ov.x;
+            acc[j].y += w * ov.y;
+            acc[j].z += w * ov.z;
+            acc[j].w += w * ov.w;
+        }
+    }
+    float4 *ob = reinterpret_cast<float4 *>(out_base);
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        const float inv = 1.f / den[j];
+        ob[j * (kHeadDim / 4) + lane] =
+            make_float4(acc[j].x * inv, acc[j].y * inv, acc[j].z * inv, acc[j].w * inv);
+    }
+}
+
+template <bool kAppend>
 __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     attention_kernel(PoolView pool, RopeView rope, BatchView batch, int layer,
-                     const float *__restrict__ q, float *__restrict__ part_o,
-                     float *__restrict__ part_ml, float scale_log2, DeviceError *err) {
+                     const float *__restrict__ q, const float *__restrict__ k_new,
+                     const float *__restrict__ v_new, float *__restrict__ part_o,
+                     float *__restrict__ part_ml, int32_t *__restrict__ counters,
+                     float *__restrict__ out, float scale_log2, DeviceError *err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int lane = threadIdx.x & 31;
     const int wid = threadIdx.x >> 5;
     const int gw = blockIdx.x * kAttnWarps + wid;
     const int G = pool.n_head_kv;
-    const int Q = batch.units_per_warp;
-    const int u_begin = gw * Q;
-    const int u_end = min(u_begin + Q, batch.total_units);
+    const int64_t U = batch.total_units;
+    const int64_t W = batch.n_warps;
+    if (gw >= W) {
+        return;
+    }
+    const int u_begin = static_cast<int>(gw * U / W);
+    const int u_end = static_cast<int>((gw + 1) * U / W);
     if (u_begin >= u_end) {
         return;
     }
@@ -341,16 +417,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     }
     __syncwarp();
 
-    Cursor cons = locate(batch, u_begin);
+    Cursor cons;
+    cons.e = batch.warp_entry[gw];
+    cons.np = batch.npages[cons.e];
+    cons.pbase = batch.page_off[cons.e];
+    {
+        const int rem = u_begin - batch.unit_off[cons.e];
+        cons.h = rem / cons.np;
+        cons.i = rem - cons.h * cons.np;
+    }
+    // Producer (lane 0): issue the first stages, then keep the page id of the
+    // next unit to issue already loaded, one iteration ahead of its use.
     Cursor prod = cons;
+    int64_t next_page = 0;
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < kAttnStages; ++s) {
             if (u_begin + s < u_end) {
-                issue_unit(pool, batch, layer, prod, stage0 + s * kStageBytes, bar0 + 8 * s,
-                           policy, err);
+                const int64_t page = checked_page(pool, batch.pages[prod.pbase + prod.i], prod.e, err);
+                issue_unit(pool, layer, page, prod.h, stage0 + s * kStageBytes, bar0 + 8 * s, policy);
                 advance(batch, G, prod);
             }
+        }
+        if (u_begin + kAttnStages < u_end) {
+            next_page = batch.pages[prod.pbase + prod.i];
         }
     }
 
@@ -367,8 +457,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     float o[8][4];
     uint32_t qb[8][2];
     float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
-    int part = 0;
-    int ntok = 0;
+    int seg_e = 0, seg_h = 0, seg_pos = 0, part = 0, nparts = 1, ntok = 0;
 
     auto flush = [&]() {
 #pragma unroll
@@ -384,10 +473,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         l_b += __shfl_xor_sync(0xffffffffu, l_b, 4);
         l_b += __shfl_xor_sync(0xffffffffu, l_b, 8);
         l_b += __shfl_xor_sync(0xffffffffu, l_b, 16);
+        const int ha = (lane & 1) * 2;
+        const int d0 = lane >> 2;
+        float *out_base = out + (static_cast<int64_t>(seg_e) * (kGqa * G) + kGqa * seg_h) * kHeadDim;
+        if (nparts == 1) {
+            // The whole (slot, KV head) was this warp's: write the output.
+            if (!lo_side) {
+                const float ia = 1.f / l_a;
+                const float ib = 1.f / l_b;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    out_base[ha * kHeadDim + 16 * mt + d0] = o[mt][0] * ia;
+                    out_base[(ha + 1) * kHeadDim + 16 * mt + d0] = o[mt][1] * ib;
+                    out_base[ha * kHeadDim + 16 * mt + d0 + 8] = o[mt][2] * ia;
+                    out_base[(ha + 1) * kHeadDim + 16 * mt + d0 + 8] = o[mt][3] * ib;
+                }
+            }
+            return;
+        }
         if (!lo_side) {
-            const int ha = (lane & 1) * 2;
             float *po = part_o + static_cast<int64_t>(part) * (kGqa * kHeadDim);
-            const int d0 = lane >> 2;
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) {
                 po[ha * kHeadDim + 16 * mt + d0] = o[mt][0];
@@ -403,6 +508,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 pm[ha * 2 + 3] = l_b;
             }
         }
+        // Publish the partial; the warp that brings the count to nparts merges.
+        __threadfence();
+        __syncwarp();
+        int ticket = 0;
+        const int eh = seg_e * G + seg_h;
+        if (lane == 0) {
+            ticket = atomicAdd(counters + eh, 1);
+        }
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        if (ticket == nparts - 1) {
+            __threadfence();
+            merge_partials(part_o, part_ml, batch.part_off[eh], nparts, out_base, lane);
+            if (lane == 0) {
+                counters[eh] = 0;  // ready for the next launch
+            }
+        }
     };
 
     for (int u = u_begin, k = 0; u < u_end; ++u, ++k) {
@@ -413,15 +534,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 flush();
             }
             // ---- new (entry, KV head) share: stage RoPE'd q as F16 hi/lo rows
-            const int e = cons.e;
-            const int h = cons.h;
-            const int pos = batch.pos[e];
-            ntok = batch.ntok[e];
-            const int first_warp = (batch.unit_off[e] + h * cons.np) / Q;
-            part = batch.part_off[e * G + h] + (gw - first_warp);
-            const float *cr = rope.cos_tab + static_cast<int64_t>(pos) * (kHeadDim / 2);
-            const float *sr = rope.sin_tab + static_cast<int64_t>(pos) * (kHeadDim / 2);
-            const float *qe = q + (static_cast<int64_t>(e) * (kGqa * G) + kGqa * h) * kHeadDim;
+            seg_e = cons.e;
+            seg_h = cons.h;
+            seg_pos = batch.pos[seg_e];
+            ntok = seg_pos + 1;
+            {
+                const int64_t a = batch.unit_off[seg_e] + static_cast<int64_t>(seg_h) * cons.np;
+                const int first = warp_of(a, U, W);
+                nparts = warp_of(a + cons.np - 1, U, W) - first + 1;
+                part = batch.part_off[seg_e * G + seg_h] + (gw - first);
+            }
+            const float *cr = rope.cos_tab + static_cast<int64_t>(seg_pos) * (kHeadDim / 2);
+            const float *sr = rope.sin_tab + static_cast<int64_t>(seg_pos) * (kHeadDim / 2);
+            const float *qe = q + (static_cast<int64_t>(seg_e) * (kGqa * G) + kGqa * seg_h) * kHeadDim;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 const int i = lane + 32 * half;
@@ -485,6 +610,28 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             for (int idx = lane; idx < (kPageTokens - valid) * 16; idx += 32) {
                 st_shared_zero16(vt + (valid + (idx >> 4)) * kRowBytes + (idx & 15) * 16);
             }
+        }
+        if (kAppend && cons.i == cons.np - 1) {
+            // Fused append: this warp owns the slot's last page for this KV
+            // head, so it writes the new row to HBM and into its copy of the
+            // page (the copy arrived without it).
+            const int r = seg_pos & 15;
+            const int c = lane & 15;
+            const bool is_v = lane >= 16;
+            const int64_t row_base = (static_cast<int64_t>(seg_e) * G + seg_h) * kHeadDim;
+            const uint4 chunk = new_row_chunk(rope, k_new + row_base, v_new + row_base, seg_pos, lane);
+            const int64_t page = checked_page(pool, batch.pages[cons.pbase + cons.i], seg_e, err);
+            uint8_t *dst = pool.base +
+                           head_block_index(page, layer, is_v ? 1 : 0, seg_h, pool.n_layers, G) *
+                               kHeadBlockBytes +
+                           r * kRowBytes + swizzled_chunk(r, c) * 16;
+            *reinterpret_cast<uint4 *>(dst) = chunk;
+            const uint32_t sdst = (is_v ? vt : kt) + r * kRowBytes + swizzled_chunk(r, c) * 16;
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sdst), "r"(chunk.x),
+                         "r"(chunk.y), "r"(chunk.z), "r"(chunk.w)
+                         : "memory");
+        }
+        if (valid < kPageTokens || (kAppend && cons.i == cons.np - 1)) {
             fence_proxy_async_smem();
             __syncwarp();
         }
@@ -556,40 +703,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         __syncwarp();
         if (lane == 0 && u + kAttnStages < u_end) {
             fence_proxy_async_smem();
-            issue_unit(pool, batch, layer, prod, kt, bar, policy, err);
+            issue_unit(pool, layer, checked_page(pool, next_page, prod.e, err), prod.h, kt, bar,
+                       policy);
             advance(batch, G, prod);
+            if (u + kAttnStages + 1 < u_end) {
+                next_page = batch.pages[prod.pbase + prod.i];
+            }
         }
         advance(batch, G, cons);
     }
     flush();
-}
-
-// ==================================================================== combine
-__global__ void __launch_bounds__(kHeadDim) combine_kernel(BatchView batch, int G,
-                                                           const float *__restrict__ part_o,
-                                                           const float *__restrict__ part_ml,
-                                                           float *__restrict__ out) {
-    const int eh = blockIdx.x;
-    const int e = eh / G;
-    const int h = eh - e * G;
-    const int t = threadIdx.x;
-    const int p0 = batch.part_off[eh];
-    const int p1 = batch.part_off[eh + 1];
-#pragma unroll
-    for (int j = 0; j < kGqa; ++j) {
-        float mx = -INFINITY;
-        for (int p = p0; p < p1; ++p) {
-            mx = fmaxf(mx, part_ml[p * 2 * kGqa + 2 * j]);
-        }
-        float num = 0.f;
-        float den = 0.f;
-        for (int p = p0; p < p1; ++p) {
-            const float w = exp2f(part_ml[p * 2 * kGqa + 2 * j] - mx);
-            den += w * part_ml[p * 2 * kGqa + 2 * j + 1];
-            num += w * part_o[static_cast<int64_t>(p) * (kGqa * kHeadDim) + j * kHeadDim + t];
-        }
-        out[(static_cast<int64_t>(e) * (kGqa * G) + kGqa * h + j) * kHeadDim + t] = num / den;
-    }
 }
 
 // ===================================================================== gather
@@ -657,28 +780,38 @@ void launch_append_range(const PoolView &pool, const RopeView &rope, const int32
     }
 }
 
-void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
-                      const float *q, float *part_o, float *part_ml, float scale_log2, int grid,
-                      DeviceError *err, cudaStream_t stream) {
-    // The dynamic shared-memory opt-in is per device.
+template <bool kAppend>
+void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchView &batch,
+                        int layer, const float *q, const float *k_new, const float *v_new,
+                        float *part_o, float *part_ml, int32_t *counters, float *out,
+                        float scale_log2, DeviceError *err, cudaStream_t stream) {
+    // The dynamic shared-memory opt-in is per device and per kernel.
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(attention_kernel<kAppend>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attention_smem_bytes()));
         if (dev >= 0 && dev < 64) {
             configured[dev] = true;
         }
     }
-    attention_kernel<<<grid, kAttnWarps * 32, attention_smem_bytes(), stream>>>(
-        pool, rope, batch, layer, q, part_o, part_ml, scale_log2, err);
+    const int grid = (batch.n_warps + kAttnWarps - 1) / kAttnWarps;
+    attention_kernel<kAppend><<<grid, kAttnWarps * 32, attention_smem_bytes(), stream>>>(
+        pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml, counters, out, scale_log2, err);
 }
 
-void launch_combine(const BatchView &batch, int n_head_kv, const float *part_o,
-                    const float *part_ml, float *out, cudaStream_t stream) {
-    const int blocks = batch.n * n_head_kv;
-    combine_kernel<<<blocks, kHeadDim, 0, stream>>>(batch, n_head_kv, part_o, part_ml, out);
+void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
+                      const float *q, const float *k_new, const float *v_new, float *part_o,
+                      float *part_ml, int32_t *counters, float *out, float scale_log2,
+                      DeviceError *err, cudaStream_t stream) {
+    if (k_new != nullptr && v_new != nullptr) {
+        launch_attention_t<true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                 counters, out, scale_log2, err, stream);
+    } else {
+        launch_attention_t<false>(pool, rope, batch, layer, q, nullptr, nullptr, part_o, part_ml,
+                                  counters, out, scale_log2, err, stream);
+    }
 }
 
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,

@@ -7,7 +7,7 @@
 // block or fail.  hkv_decode_attn_noalloc serves them: it takes device memory
 // the caller already owns (a page pool in the engine's layout, the RoPE
 // tables, q, out) and keeps its own working memory -- the batch descriptor,
-// the split-K partials and the device error word -- in one file-scope
+// the split-K partials, the merge counters and the device error word -- in one file-scope
 // __device__ array of fixed size, so no call allocates device memory.
 //
 // The array is kNoAllocScratchBytes (8 MiB) on every GPU that loads the
@@ -26,6 +26,7 @@
 
 #include "../../include/hkv.h"
 #include "hkv_internal.h"
+#include "hkv_plan.h"
 
 namespace hkv {
 namespace {
@@ -141,56 +142,38 @@ extern "C" int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer
         }
         total_pages += np;
     }
-    const int64_t total_units = total_pages * G;
-    const int64_t full_warps = static_cast<int64_t>(g_num_sms[dev]) * kAttnWarps;
-    const int64_t Q = std::max<int64_t>(1, (total_units + full_warps - 1) / full_warps);
-    const int64_t active_warps = (total_units + Q - 1) / Q;
-    const int grid = static_cast<int>((active_warps + kAttnWarps - 1) / kAttnWarps);
-
-    const size_t words = static_cast<size_t>(3 * n + 2 * (n + 1) + (n * G + 1) + total_pages);
+    const int32_t W = g_num_sms[dev] * kAttnWarps;
+    const size_t words = plan_words(n, G, total_pages, W);
     std::vector<int32_t> w(words);
-    int32_t *hpos = w.data();
-    int32_t *ntok = hpos + n;
-    int32_t *npg = ntok + n;
-    int32_t *hpoff = npg + n;
-    int32_t *unit_off = hpoff + (n + 1);
-    int32_t *part_off = unit_off + (n + 1);
-    int32_t *hpages = part_off + (n * G + 1);
-    hpoff[0] = unit_off[0] = part_off[0] = 0;
+    std::vector<const int32_t *> lists(static_cast<size_t>(n));
     for (int32_t e = 0; e < n; ++e) {
-        const int32_t np = pos[e] / kPageTokens + 1;
-        hpos[e] = pos[e];
-        ntok[e] = pos[e] + 1;
-        npg[e] = np;
-        std::memcpy(hpages + hpoff[e], pages + page_off[e], static_cast<size_t>(np) * 4);
-        hpoff[e + 1] = hpoff[e] + np;
-        unit_off[e + 1] = unit_off[e] + np * G;
-        for (int32_t h = 0; h < G; ++h) {
-            const int64_t a = unit_off[e] + static_cast<int64_t>(h) * np;
-            const int64_t b = a + np;
-            part_off[e * G + h + 1] = part_off[e * G + h] + static_cast<int32_t>((b - 1) / Q - a / Q + 1);
-        }
+        lists[e] = pages + page_off[e];
     }
-    const int32_t n_parts = part_off[n * G];
+    const PlanSummary plan = build_plan(w.data(), n, G, pos, lists.data(), total_pages, W);
 
-    // ---- carve the static scratch: [error word][descriptor][partials o][partials m,l]
-    const size_t err_off = 0;
-    const size_t desc_off = align256(sizeof(DeviceError));
+    // ---- carve the static scratch:
+    //      [error word][merge counters][descriptor][partials o][partials m, l]
+    const size_t cnt_off = align256(sizeof(DeviceError));
+    const size_t desc_off = align256(cnt_off + static_cast<size_t>(n) * G * sizeof(int32_t));
     const size_t po_off = align256(desc_off + words * sizeof(int32_t));
-    const size_t pml_off = align256(po_off + static_cast<size_t>(n_parts) * kGqa * kHeadDim * 4);
-    const size_t need = pml_off + static_cast<size_t>(n_parts) * 2 * kGqa * 4;
+    const size_t pml_off =
+        align256(po_off + static_cast<size_t>(plan.n_parts) * kGqa * kHeadDim * sizeof(float));
+    const size_t need = pml_off + static_cast<size_t>(plan.n_parts) * 2 * kGqa * sizeof(float);
     if (need > kNoAllocScratchBytes) {
         set_msg(err_msg, err_len,
                 "batch needs %zu bytes of scratch (%d partials, %zu descriptor words); the "
                 "static scratch holds %zu bytes: split the batch",
-                need, n_parts, words, kNoAllocScratchBytes);
+                need, plan.n_parts, words, kNoAllocScratchBytes);
         return HKV_ERR_RANGE;
     }
-    DeviceError *err = reinterpret_cast<DeviceError *>(scratch + err_off);
+    DeviceError *err = reinterpret_cast<DeviceError *>(scratch);
+    int32_t *counters = reinterpret_cast<int32_t *>(scratch + cnt_off);
     int32_t *d = reinterpret_cast<int32_t *>(scratch + desc_off);
     float *part_o = reinterpret_cast<float *>(scratch + po_off);
     float *part_ml = reinterpret_cast<float *>(scratch + pml_off);
-    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(DeviceError), stream);
+    // The error word and the merge counters must start at zero; the array
+    // keeps whatever the previous call left.
+    cudaError_t e = cudaMemsetAsync(scratch, 0, desc_off, stream);
     if (e == cudaSuccess) {
         e = cudaMemcpyAsync(d, w.data(), words * sizeof(int32_t), cudaMemcpyHostToDevice, stream);
     }
@@ -198,18 +181,7 @@ extern "C" int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer
         set_msg(err_msg, err_len, "descriptor upload: %s", cudaGetErrorString(e));
         return HKV_ERR_CUDA;
     }
-    BatchView b;
-    b.pos = d;
-    b.ntok = d + n;
-    b.npages = d + 2 * n;
-    b.page_off = d + 3 * n;
-    b.unit_off = b.page_off + (n + 1);
-    b.part_off = b.unit_off + (n + 1);
-    b.pages = b.part_off + (n * G + 1);
-    b.n = n;
-    b.total_units = static_cast<int32_t>(total_units);
-    b.units_per_warp = static_cast<int32_t>(Q);
-    b.n_parts = n_parts;
+    const BatchView b = bind_plan(d, n, G, plan, W);
     PoolView pv;
     pv.base = static_cast<uint8_t *>(view->pool);
     pv.n_pages = view->n_pages;
@@ -221,8 +193,8 @@ extern "C" int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer
     rv.context_length = view->context_length;
     const float scale_log2 =
         (1.0f / std::sqrt(static_cast<float>(kHeadDim))) * 1.4426950408889634f;
-    launch_attention(pv, rv, b, layer, q_prerope, part_o, part_ml, scale_log2, grid, err, stream);
-    launch_combine(b, G, part_o, part_ml, out, stream);
+    launch_attention(pv, rv, b, layer, q_prerope, nullptr, nullptr, part_o, part_ml, counters, out,
+                     scale_log2, err, stream);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_msg(err_msg, err_len, "kernel launch: %s", cudaGetErrorString(e));

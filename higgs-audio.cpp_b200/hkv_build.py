@@ -21,7 +21,7 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libhkv.so"
 SOURCES = [CSRC / "hkv_kernels.cu", CSRC / "hkv_engine.cpp", CSRC / "hkv_noalloc.cu"]
-HEADERS = [CSRC / "hkv_internal.h", REPO / "include" / "hkv.h"]
+HEADERS = [CSRC / "hkv_internal.h", CSRC / "hkv_plan.h", REPO / "include" / "hkv.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -103,11 +103,12 @@ typedef struct hkv_pool_stats {
 
 /* Kernel ids for the CUDA-event profiler. */
 typedef enum hkv_kernel_id {
-    HKV_KERNEL_APPEND = 0,
-    HKV_KERNEL_ATTN = 1,
-    HKV_KERNEL_COMBINE = 2,
-    HKV_KERNEL_GATHER = 3,
-    HKV_KERNEL_STEP = 4,
+    HKV_KERNEL_APPEND = 0,  /* hkv_append, hkv_rope_append, hkv_rope_append_range */
+    HKV_KERNEL_ATTN = 1,    /* hkv_decode_attn                                    */
+    HKV_KERNEL_COMBINE = 2, /* reserved: the split merge runs inside the attention
+                               kernels, so nothing is recorded under this id    */
+    HKV_KERNEL_GATHER = 3,  /* hkv_gather                                         */
+    HKV_KERNEL_STEP = 4,    /* hkv_decode_step (append + attention, one launch)   */
     HKV_KERNEL_COUNT = 5
 } hkv_kernel_id;
 
@@ -200,8 +201,10 @@ int hkv_rope_append_range(hkv_engine *eng, int32_t layer, int32_t slot, int64_t 
 int hkv_decode_attn(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
                     const float *q_prerope, float *out, hkv_stream stream);
 
-/* hkv_rope_append followed by hkv_decode_attn for one layer, in one call
- * (one descriptor check for both).  Same shapes and results. */
+/* hkv_rope_append followed by hkv_decode_attn for one layer, as ONE kernel
+ * launch: the warp that owns a slot's last page for a KV head ropes the new
+ * K row, writes K and V to the page and patches the copy it attends from.
+ * Same shapes and results (cache bits and outputs) as the two calls. */
 int hkv_decode_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
                     const float *q_prerope, const float *k_prerope, const float *v, float *out,
                     hkv_stream stream);
