@@ -1,7 +1,7 @@
 """Decode-attention + KV-append throughput of the paged KV engine.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload scaleout|batched16]
+                    [--workload scaleout|batched16|headsplit]
 
 One process per GPU (torchrun for N > 1).  A step is one decode step of every
 slot on the rank: for each of the 36 layers, the RoPE + K/V append of one row
@@ -13,6 +13,8 @@ Workloads (synthetic N(0,1) data, random physical page order):
              32 slots per GPU, contexts uniform in [2048, 16384] (seeded per
              rank), so N GPUs run 32N slots (weak scaling, no collective).
   batched16  16 slots, contexts uniform in [256, 4096], one GPU.
+  headsplit  one request near the 32768-position context, split by KV head
+             over the N GPUs with an NCCL all-gather per layer.
 
 Reported: `value` = tokens/s over all ranks (slots advanced one position
 through all 36 layers per second), device-timed with CUDA events, max over
@@ -60,6 +62,11 @@ def workload(name: str, rank: int):
         lens = synth.uniform_int(1000 + rank, n, 2048, 16384)
         desc = ("scale-out shard: 32 slots per GPU, contexts U[2048,16384], 36 layers, "
                 "F16 KV in 16-token pages (permuted), GQA 32/8, head_dim 128")
+    elif name == "headsplit":
+        n = 1
+        lens = [32768 - 16]
+        desc = ("one request near the 32768-position context, split by KV head, 36 layers, "
+                "F16 KV in 16-token pages")
     elif name == "batched16":
         n = 16
         lens = synth.uniform_int(2000 + rank, n, 256, 4096)
@@ -394,6 +401,113 @@ def bench_ours(args):
         dist.destroy_process_group()
 
 
+def bench_headsplit(args):
+    """One long request split by KV head across the ranks (HeadSplit): rank g
+    holds KV heads [8g/N, 8(g+1)/N) of every layer, attends its 32/N query
+    heads, and one NCCL all-gather per layer assembles the head-major output."""
+    import datetime
+
+    import torch
+    import hkv
+    from hkv_dist import HeadSplit
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+    split = HeadSplit(world=world, rank=rank)
+    Gl, Hl = split.local_kv_heads, split.local_q_heads
+    total_steps = args.warmup + args.steps + 2
+    L0 = 32768 - total_steps - 1  # the last step's new row sits at position 32766
+    dev = f"cuda:{local}"
+    eng = hkv.Engine(n_layers=N_LAYERS, n_pages=(L0 + total_steps) // 16 + 2, max_slots=1,
+                     device=local, shuffle_seed=0xBEEF + rank, **split.engine_shape())
+    stream = torch.cuda.Stream(device=local)
+    sh = stream.cuda_stream
+    slot = eng.acquire(L0 + total_steps)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77 + rank)
+    with torch.cuda.stream(stream):
+        done = 0
+        while done < L0:
+            t = min(4096, L0 - done)
+            for layer in range(N_LAYERS):
+                k = torch.randn((t, Gl, D), generator=gen, device=dev)
+                v = torch.randn((t, Gl, D), generator=gen, device=dev)
+                eng.rope_append_range(layer, slot, t, k, v, sh)
+            eng.advance([slot], t)
+            done += t
+        q = torch.randn((N_LAYERS, 1, Hl, D), generator=gen, device=dev)
+        k = torch.randn((N_LAYERS, 1, Gl, D), generator=gen, device=dev)
+        v = torch.randn((N_LAYERS, 1, Gl, D), generator=gen, device=dev)
+        out_local = torch.empty((N_LAYERS, 1, Hl * D), device=dev)
+        out_full = torch.empty((N_LAYERS, world, Hl * D), device=dev)
+    eng.sync_check(sh)
+
+    def step():
+        for layer in range(N_LAYERS):
+            eng.decode_step(layer, [slot], q[layer], k[layer], v[layer], out_local[layer], sh)
+            if dist is not None:
+                dist.all_gather_into_tensor(out_full[layer], out_local[layer])
+        eng.advance([slot], 1)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ctx0 = eng.length(slot) + 1
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    eng.sync_check(sh)
+    # full-output check of the assembly on the last layer: rank order == head order
+    if dist is not None:
+        full = split.gather_output(out_local[N_LAYERS - 1])
+        assert torch.equal(full.view(world, Hl * D), out_full[N_LAYERS - 1])
+    rows = sum(ctx0 + s for s in range(args.steps))
+    bytes_per_rank = N_LAYERS * 512 * Gl * (rows + 11 * args.steps)
+    peak, peak_kind = measured_peaks()
+    gbs = bytes_per_rank / (ms / 1e3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": args.steps / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 KV, f32 accumulate",
+            "data": "synthetic N(0,1) (torch generator on device)",
+            "config": {"workload": (f"one {ctx0}-position request split by KV head over "
+                                    f"{world} GPU(s), {Gl} KV heads each, 36 layers, NCCL "
+                                    "all-gather of the per-head outputs every layer"),
+                       "global_batch": 1, "layers": N_LAYERS,
+                       "parallelism": f"KV-head split x{world}"},
+            "hbm": {"step_gbs_per_gpu": gbs, "peak_gbs": peak, "frac": gbs / peak,
+                    "peak_kind": peak_kind},
+            "gpu_launches": N_LAYERS * args.steps, "e2e": None,
+        }), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def bench_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -451,6 +565,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         bench_reference(args)
+    elif args.workload == "headsplit":
+        bench_headsplit(args)
     else:
         bench_ours(args)
 

@@ -522,7 +522,7 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
         return fail(eng, HKV_ERR_RANGE, "batch too large (%lld units)",
                     static_cast<long long>(total_pages * G));
     }
-    const int32_t W = eng->num_sms * kAttnWarps;
+    const int32_t W = plan_warps(total_pages * G, static_cast<int64_t>(eng->num_sms) * kAttnWarps);
     const size_t words = plan_words(n, G, total_pages, W);
     void *host = nullptr;
     HKV_CUDA_TRY(eng, eng->batch_stage.begin(words * sizeof(int32_t), &host));

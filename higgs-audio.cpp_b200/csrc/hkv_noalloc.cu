@@ -142,7 +142,7 @@ extern "C" int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer
         }
         total_pages += np;
     }
-    const int32_t W = g_num_sms[dev] * kAttnWarps;
+    const int32_t W = plan_warps(total_pages * G, static_cast<int64_t>(g_num_sms[dev]) * kAttnWarps);
     const size_t words = plan_words(n, G, total_pages, W);
     std::vector<int32_t> w(words);
     std::vector<const int32_t *> lists(static_cast<size_t>(n));

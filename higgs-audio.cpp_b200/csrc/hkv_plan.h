@@ -3,7 +3,8 @@
 // A batch of n slots attending pos[e] + 1 rows each is cut into units (one
 // unit = one 16-row page of one KV head, 8 KiB of K and V).  Units are
 // ordered (entry, KV head, page); the range [0, U) is split into W equal
-// shares, one per warp of the grid:
+// shares, one per warp, W = min(U, warps of a full grid) so that no share is
+// empty:
 //     share(w) = [floor(w U / W), floor((w + 1) U / W))
 // and the warp holding unit a is warp_of(a) = ceil((a + 1) W / U) - 1.
 // Each (entry, KV head) segment [a, a + np) is covered by warps
@@ -23,6 +24,13 @@
 namespace hkv {
 
 inline int64_t plan_warp_of(int64_t a, int64_t U, int64_t W) { return ((a + 1) * W + U - 1) / U - 1; }
+
+// Warps to share U units among: every share must hold at least one unit (a
+// segment's partial count is the number of warps its range touches, so an
+// empty share in the middle would be counted but never arrive).
+inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
+    return static_cast<int32_t>(total_units < max_warps ? total_units : max_warps);
+}
 
 inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
     return static_cast<size_t>(3 * n + 2 * (n + 1) + (n * G + 1) + W + total_pages);

@@ -1,0 +1,101 @@
+"""Invariants of the stream-K plan (higgs-audio.cpp_b200/csrc/hkv_plan.h), CPU.
+
+Restates the plan's formulas -- W = min(U, grid warps) equal shares
+floor(w U / W) .. floor((w + 1) U / W), warp_of(a) = ceil((a + 1) W / U) - 1,
+part_off from the warps a (slot, KV head) segment touches, warp_entry -- and
+walks every warp the way attention_kernel does, checking that each segment's
+partials are written exactly once and merged exactly once (or written
+directly when one warp holds the whole segment).  Empty shares would break
+this (a segment would count a partial that never arrives), which is why W is
+capped at U.
+"""
+from __future__ import annotations
+
+import random
+
+import pytest
+
+
+def plan(npages, G, w_full):
+    n = len(npages)
+    unit_off = [0]
+    for np_ in npages:
+        unit_off.append(unit_off[-1] + np_ * G)
+    U = unit_off[-1]
+    W = min(U, w_full)
+    warp_of = lambda a: ((a + 1) * W + U - 1) // U - 1  # noqa: E731
+    part_off = [0]
+    for e, np_ in enumerate(npages):
+        for h in range(G):
+            a = unit_off[e] + h * np_
+            part_off.append(part_off[-1] + warp_of(a + np_ - 1) - warp_of(a) + 1)
+    warp_entry, e = [], 0
+    for k in range(W):
+        ub = k * U // W
+        while e + 1 < n and unit_off[e + 1] <= ub:
+            e += 1
+        warp_entry.append(e)
+    return unit_off, part_off, warp_entry, U, W, warp_of
+
+
+def walk(npages, G=8, w_full=148 * 8):
+    unit_off, part_off, warp_entry, U, W, warp_of = plan(npages, G, w_full)
+    assert part_off[-1] <= W + len(npages) * G  # the engine's partial capacity
+    written, tickets, merges, direct = {}, {}, {}, {}
+    for gw in range(W):
+        ub, ue = gw * U // W, (gw + 1) * U // W
+        assert ub < ue, "empty share"
+        e = warp_entry[gw]
+        np_ = npages[e]
+        rem = ub - unit_off[e]
+        h, i = rem // np_, rem % np_
+        seg = None
+
+        def flush(seg):
+            e_, h_, part, nparts = seg
+            eh = e_ * G + h_
+            if nparts == 1:
+                direct[eh] = direct.get(eh, 0) + 1
+                return
+            assert part_off[eh] <= part < part_off[eh + 1]
+            written[part] = written.get(part, 0) + 1
+            t = tickets.get(eh, 0)
+            tickets[eh] = t + 1
+            if t == nparts - 1:
+                merges[eh] = merges.get(eh, 0) + 1
+
+        for u in range(ub, ue):
+            if u == ub or i == 0:
+                if u != ub:
+                    flush(seg)
+                a = unit_off[e] + h * np_
+                first = warp_of(a)
+                seg = (e, h, part_off[e * G + h] + (gw - first), warp_of(a + np_ - 1) - first + 1)
+            i += 1
+            if i == np_:
+                i, h = 0, h + 1
+                if h == G:
+                    h, e = 0, e + 1
+                    if e < len(npages):
+                        np_ = npages[e]
+        flush(seg)
+    for eh in range(len(npages) * G):
+        if part_off[eh + 1] - part_off[eh] == 1:
+            assert direct.get(eh) == 1
+        else:
+            assert merges.get(eh) == 1
+            for p in range(part_off[eh], part_off[eh + 1]):
+                assert written.get(p) == 1
+
+
+@pytest.mark.parametrize("npages", [[3, 1], [1] * 4, [1] * 300, [3, 19, 63], [2048],
+                                    [1, 1000, 1, 1000]])
+def test_plan_partitions_every_segment(npages):
+    walk(npages)
+
+
+def test_plan_random_batches():
+    rng = random.Random(0)
+    for _ in range(30):
+        walk([rng.randint(1, 1025) for _ in range(rng.randint(1, 64))],
+             G=rng.choice([1, 2, 4, 8]))
