@@ -332,8 +332,14 @@ int32_t take_page(hkv_engine *eng, Slot &slot) {
     return page;
 }
 
-uint8_t *page_ptr(const hkv_engine *eng, int32_t page) {
-    return eng->pool + static_cast<int64_t>(page) * eng->page_bytes;
+// Bytes of one page within one layer's slab (K and V of every KV head).
+int64_t layer_page_bytes(const hkv_engine *eng) {
+    return 2ll * eng->cfg.n_head_kv * kHeadBlockBytes;
+}
+
+uint8_t *page_ptr(const hkv_engine *eng, int32_t layer, int32_t page) {
+    return eng->pool +
+           (static_cast<int64_t>(layer) * eng->cfg.n_pages + page) * layer_page_bytes(eng);
 }
 
 // Pages `slot` must newly take to own every page touched by rows
@@ -377,9 +383,13 @@ int own_rows(hkv_engine *eng, Slot &s, int64_t begin, int64_t end, cudaStream_t 
             const int32_t old = s.pages[p];
             const int32_t fresh = take_page(eng, s);
             if (eng->device_mode) {
-                HKV_CUDA_TRY(eng, cudaMemcpyAsync(page_ptr(eng, fresh), page_ptr(eng, old),
-                                                  static_cast<size_t>(eng->page_bytes),
-                                                  cudaMemcpyDeviceToDevice, stream));
+                // The page lives in every layer's slab: one copy per layer.
+                for (int32_t layer = 0; layer < eng->cfg.n_layers; ++layer) {
+                    HKV_CUDA_TRY(eng, cudaMemcpyAsync(page_ptr(eng, layer, fresh),
+                                                      page_ptr(eng, layer, old),
+                                                      static_cast<size_t>(layer_page_bytes(eng)),
+                                                      cudaMemcpyDeviceToDevice, stream));
+                }
             }
             decref(eng, old);
             s.pages[p] = fresh;

@@ -16,9 +16,10 @@ constexpr int kPageTokens = 16;
 constexpr int kHeadBlockBytes = kPageTokens * kHeadDim * 2;
 constexpr int kRowBytes = kHeadDim * 2;  // 256 B, 16 chunks of 16 B
 
-// Page layout in HBM (page-major, so a copy-on-write duplicates one
-// contiguous range):
-//   block(page, layer, kv, head) = ((page * n_layers + layer) * 2 + kv) * n_head_kv + head
+// Page layout in HBM (layer-major: one decode launch reads one layer, and its
+// reads then stay inside that layer's contiguous slab of n_pages * 64 KiB,
+// which keeps the GPU's address translation working set small):
+//   block(page, layer, kv, head) = ((layer * n_pages + page) * 2 + kv) * n_head_kv + head
 //   byte(page, layer, kv, head, row, chunk) =
 //       block * 4096 + row * 256 + (chunk ^ (row & 7)) * 16
 // where kv = 0 for K and 1 for V, row = position % 16 and chunk = dim / 8.
@@ -27,8 +28,8 @@ constexpr int kRowBytes = kHeadDim * 2;  // 256 B, 16 chunks of 16 B
 // has been copied verbatim (TMA bulk copy) into shared memory, while a row
 // stays sixteen 16-byte pieces for the append's vector stores.
 __host__ __device__ inline int64_t head_block_index(int64_t page, int layer, int kv, int head,
-                                                   int n_layers, int n_head_kv) {
-    return ((page * n_layers + layer) * 2 + kv) * n_head_kv + head;
+                                                   int64_t n_pages, int n_head_kv) {
+    return ((static_cast<int64_t>(layer) * n_pages + page) * 2 + kv) * n_head_kv + head;
 }
 __host__ __device__ inline int swizzled_chunk(int row, int chunk) { return chunk ^ (row & 7); }
 
@@ -53,7 +54,8 @@ struct BatchView {
     const int32_t *page_off;  // [n+1] prefix sum of npages into pages[]
     const int32_t *unit_off;  // [n+1] prefix sum of npages * n_head_kv
     const int32_t *part_off;  // [n*n_head_kv + 1] first partial of each (entry, kv head)
-    const int32_t *warp_entry;// [n_warps] batch entry holding each warp's first unit
+    const int4 *warp_start;   // [n_warps][2] per warp: {entry, kv head, page index, pages of
+                              // the entry}, {page_off[entry], first three physical pages}
     const int32_t *pages;     // [page_off[n]] physical pages, entry-major
     int32_t n;
     int32_t total_units;      // sum of npages * n_head_kv: one unit = one head block of K and V

@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(128) append_kernel(PoolView pool, RopeView rop
     packed.z = pack_half2(y[4], y[5]);
     packed.w = pack_half2(y[6], y[7]);
     uint8_t *dst = pool.base +
-                   head_block_index(page, layer, is_v ? 1 : 0, head, pool.n_layers, G) *
+                   head_block_index(page, layer, is_v ? 1 : 0, head, pool.n_pages, G) *
                        kHeadBlockBytes +
                    r * kRowBytes + swizzled_chunk(r, c) * 16;
     *reinterpret_cast<uint4 *>(dst) = packed;
@@ -294,7 +294,7 @@ __device__ __forceinline__ void issue_unit(const PoolView &pool, int layer, int6
                                            uint32_t stage, uint32_t bar, uint64_t policy) {
     const uint8_t *kb =
         pool.base +
-        head_block_index(page, layer, 0, h, pool.n_layers, pool.n_head_kv) * kHeadBlockBytes;
+        head_block_index(page, layer, 0, h, pool.n_pages, pool.n_head_kv) * kHeadBlockBytes;
     const uint8_t *vb = kb + static_cast<int64_t>(pool.n_head_kv) * kHeadBlockBytes;
     mbar_arrive_expect_tx(bar, kStageBytes);
     tma_load_1d(stage, kb, kHeadBlockBytes, bar, policy);
@@ -335,6 +335,9 @@ __device__ __forceinline__ uint4 new_row_chunk(const RopeView &rope, const float
 
 // Merge of one (slot, KV head)'s partials by the warp that finished last.
 // Partials were written by other SMs in this launch: read them through L2.
+// Lane p holds the (m, l) of partial p (loaded in parallel, reduced by
+// shuffles); the partial outputs are then streamed with the weights
+// broadcast from their owner lane, several partials in flight at a time.
 __device__ __forceinline__ void merge_partials(const float *part_o, const float *part_ml, int p0,
                                                int nparts, float *out_base, int lane) {
     float mx[kGqa];
@@ -342,11 +345,20 @@ __device__ __forceinline__ void merge_partials(const float *part_o, const float 
     for (int j = 0; j < kGqa; ++j) {
         mx[j] = -INFINITY;
     }
-    for (int p = 0; p < nparts; ++p) {
-        const float *pm = part_ml + static_cast<int64_t>(p0 + p) * (2 * kGqa);
+    for (int p = lane; p < nparts; p += 32) {
+        const float4 *pm = reinterpret_cast<const float4 *>(part_ml + static_cast<int64_t>(p0 + p) * (2 * kGqa));
+        const float4 a = __ldcg(pm);
+        const float4 b = __ldcg(pm + 1);
+        mx[0] = fmaxf(mx[0], a.x);
+        mx[1] = fmaxf(mx[1], a.z);
+        mx[2] = fmaxf(mx[2], b.x);
+        mx[3] = fmaxf(mx[3], b.z);
+    }
 #pragma unroll
-        for (int j = 0; j < kGqa; ++j) {
-            mx[j] = fmaxf(mx[j], __ldcg(pm + 2 * j));
+    for (int j = 0; j < kGqa; ++j) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], off));
         }
     }
     float4 acc[kGqa];
@@ -356,19 +368,44 @@ __device__ __forceinline__ void merge_partials(const float *part_o, const float 
         acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
         den[j] = 0.f;
     }
-    for (int p = 0; p < nparts; ++p) {
-        const float *pm = part_ml + static_cast<int64_t>(p0 + p) * (2 * kGqa);
-        const float4 *po =
-            reinterpret_cast<const float4 *>(part_o + static_cast<int64_t>(p0 + p) * (kGqa * kHeadDim));
+    for (int base = 0; base < nparts; base += 32) {
+        // weights of the partials base .. base+31, one per lane
+        float w[kGqa] = {0.f, 0.f, 0.f, 0.f};
+        if (base + lane < nparts) {
+            const float4 *pm = reinterpret_cast<const float4 *>(
+                part_ml + static_cast<int64_t>(p0 + base + lane) * (2 * kGqa));
+            const float4 a = __ldcg(pm);
+            const float4 b = __ldcg(pm + 1);
+            w[0] = exp2f(a.x - mx[0]);
+            w[1] = exp2f(a.z - mx[1]);
+            w[2] = exp2f(b.x - mx[2]);
+            w[3] = exp2f(b.z - mx[3]);
+            den[0] += w[0] * a.y;
+            den[1] += w[1] * a.w;
+            den[2] += w[2] * b.y;
+            den[3] += w[3] * b.w;
+        }
+        const int cnt = min(32, nparts - base);
+#pragma unroll 4
+        for (int t = 0; t < cnt; ++t) {
+            const float4 *po = reinterpret_cast<const float4 *>(
+                part_o + static_cast<int64_t>(p0 + base + t) * (kGqa * kHeadDim));
 #pragma unroll
-        for (int j = 0; j < kGqa; ++j) {
-            const float w = exp2f(__ldcg(pm + 2 * j) - mx[j]);
-            den[j] += w * __ldcg(pm + 2 * j + 1);
-            const float4 ov = __ldcg(po + j * (kHeadDim / 4) + lane);
-            acc[j].x += w * ov.x;
-            acc[j].y += w * ov.y;
-            acc[j].z += w * ov.z;
-            acc[j].w += w * ov.w;
+            for (int j = 0; j < kGqa; ++j) {
+                const float wt = __shfl_sync(0xffffffffu, w[j], t);
+                const float4 ov = __ldcg(po + j * (kHeadDim / 4) + lane);
+                acc[j].x += wt * ov.x;
+                acc[j].y += wt * ov.y;
+                acc[j].z += wt * ov.z;
+                acc[j].w += wt * ov.w;
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            den[j] += __shfl_xor_sync(0xffffffffu, den[j], off);
         }
     }
     float4 *ob = reinterpret_cast<float4 *>(out_base);
@@ -417,24 +454,27 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     }
     __syncwarp();
 
+    // The plan hands each warp its starting cursor and the physical pages of
+    // its first units in two 16-byte records, so the first copies go out
+    // without a chain of dependent loads.
+    const int4 ws0 = batch.warp_start[2 * gw];
+    const int4 ws1 = batch.warp_start[2 * gw + 1];
     Cursor cons;
-    cons.e = batch.warp_entry[gw];
-    cons.np = batch.npages[cons.e];
-    cons.pbase = batch.page_off[cons.e];
-    {
-        const int rem = u_begin - batch.unit_off[cons.e];
-        cons.h = rem / cons.np;
-        cons.i = rem - cons.h * cons.np;
-    }
+    cons.e = ws0.x;
+    cons.h = ws0.y;
+    cons.i = ws0.z;
+    cons.np = ws0.w;
+    cons.pbase = ws1.x;
     // Producer (lane 0): issue the first stages, then keep the page id of the
     // next unit to issue already loaded, one iteration ahead of its use.
     Cursor prod = cons;
     int64_t next_page = 0;
     if (lane == 0) {
+        const int first_pages[kAttnStages] = {ws1.y, ws1.z, ws1.w};
 #pragma unroll
         for (int s = 0; s < kAttnStages; ++s) {
             if (u_begin + s < u_end) {
-                const int64_t page = checked_page(pool, batch.pages[prod.pbase + prod.i], prod.e, err);
+                const int64_t page = checked_page(pool, first_pages[s], prod.e, err);
                 issue_unit(pool, layer, page, prod.h, stage0 + s * kStageBytes, bar0 + 8 * s, policy);
                 advance(batch, G, prod);
             }
@@ -622,7 +662,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             const uint4 chunk = new_row_chunk(rope, k_new + row_base, v_new + row_base, seg_pos, lane);
             const int64_t page = checked_page(pool, batch.pages[cons.pbase + cons.i], seg_e, err);
             uint8_t *dst = pool.base +
-                           head_block_index(page, layer, is_v ? 1 : 0, seg_h, pool.n_layers, G) *
+                           head_block_index(page, layer, is_v ? 1 : 0, seg_h, pool.n_pages, G) *
                                kHeadBlockBytes +
                            r * kRowBytes + swizzled_chunk(r, c) * 16;
             *reinterpret_cast<uint4 *>(dst) = chunk;
@@ -739,9 +779,9 @@ __global__ void gather_kernel(PoolView pool, const int32_t *__restrict__ slot_pa
     const int r = static_cast<int>(pos & 15);
     const int64_t within = r * kRowBytes + swizzled_chunk(r, c) * 16;
     const uint8_t *kb =
-        pool.base + head_block_index(page, layer, 0, h, pool.n_layers, G) * kHeadBlockBytes;
+        pool.base + head_block_index(page, layer, 0, h, pool.n_pages, G) * kHeadBlockBytes;
     const uint8_t *vb =
-        pool.base + head_block_index(page, layer, 1, h, pool.n_layers, G) * kHeadBlockBytes;
+        pool.base + head_block_index(page, layer, 1, h, pool.n_pages, G) * kHeadBlockBytes;
     const int64_t o = (t * G + h) * kHeadDim + c * 8;
     *reinterpret_cast<uint4 *>(k_out + o) = *reinterpret_cast<const uint4 *>(kb + within);
     *reinterpret_cast<uint4 *>(v_out + o) = *reinterpret_cast<const uint4 *>(vb + within);

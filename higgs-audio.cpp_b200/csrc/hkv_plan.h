@@ -11,8 +11,11 @@
 // warp_of(a) .. warp_of(a + np - 1), one partial result each.
 //
 // Device descriptor (int32 words, uploaded in one copy):
+//   warp_start[W][8]  per warp {entry, kv head, page index, pages of the entry}
+//                     {page_off[entry], physical pages of its first 3 units}
+//                     (first, so each record is 16-byte aligned)
 //   pos[n] ntok[n] npages[n] page_off[n+1] unit_off[n+1] part_off[n*G+1]
-//   warp_entry[W] pages[total_pages]
+//   pages[total_pages]
 #pragma once
 
 #include <stdint.h>
@@ -32,8 +35,11 @@ inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
     return static_cast<int32_t>(total_units < max_warps ? total_units : max_warps);
 }
 
+constexpr int kWarpStartWords = 8;
+
 inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
-    return static_cast<size_t>(3 * n + 2 * (n + 1) + (n * G + 1) + W + total_pages);
+    return static_cast<size_t>(kWarpStartWords * W + 3 * n + 2 * (n + 1) + (n * G + 1) +
+                               total_pages);
 }
 
 struct PlanSummary {
@@ -42,22 +48,22 @@ struct PlanSummary {
     int32_t n_parts = 0;
 };
 
-// Fills `w` (plan_words(...) words).  page_lists[e] points at slot e's page
-// ids, at least pos[e] / 16 + 1 of them.
+// Fills `w` (plan_words(...) words, 16-byte aligned).  page_lists[e] points
+// at slot e's page ids, at least pos[e] / 16 + 1 of them.
 inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *pos_in,
                               const int32_t *const *page_lists, int64_t total_pages, int32_t W) {
     PlanSummary s;
     s.total_pages = total_pages;
     s.total_units = total_pages * G;
     const int64_t U = s.total_units;
-    int32_t *pos = w;
+    int32_t *warp_start = w;
+    int32_t *pos = warp_start + kWarpStartWords * W;
     int32_t *ntok = pos + n;
     int32_t *npg = ntok + n;
     int32_t *page_off = npg + n;
     int32_t *unit_off = page_off + (n + 1);
     int32_t *part_off = unit_off + (n + 1);
-    int32_t *warp_entry = part_off + (n * G + 1);
-    int32_t *pages = warp_entry + W;
+    int32_t *pages = part_off + (n * G + 1);
     page_off[0] = unit_off[0] = part_off[0] = 0;
     for (int32_t e = 0; e < n; ++e) {
         const int32_t np = pos_in[e] / kPageTokens + 1;
@@ -74,12 +80,37 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         }
     }
     int32_t e = 0;
+    static_assert(kAttnStages == 3, "warp_start carries the first three page ids");
     for (int32_t k = 0; k < W; ++k) {
         const int64_t ub = static_cast<int64_t>(k) * U / W;
+        const int64_t ue = static_cast<int64_t>(k + 1) * U / W;
         while (e + 1 < n && unit_off[e + 1] <= ub) {
             ++e;
         }
-        warp_entry[k] = e;
+        int32_t *ws = warp_start + kWarpStartWords * k;
+        const int32_t np = npg[e];
+        const int32_t rem = static_cast<int32_t>(ub - unit_off[e]);
+        ws[0] = e;
+        ws[1] = rem / np;
+        ws[2] = rem % np;
+        ws[3] = np;
+        ws[4] = page_off[e];
+        // physical pages of the share's first three units
+        int32_t ce = e, ch = ws[1], ci = ws[2];
+        for (int j = 0; j < 3; ++j) {
+            if (ub + j < ue) {
+                ws[5 + j] = pages[page_off[ce] + ci];
+                if (++ci == npg[ce]) {
+                    ci = 0;
+                    if (++ch == G) {
+                        ch = 0;
+                        ++ce;
+                    }
+                }
+            } else {
+                ws[5 + j] = -1;
+            }
+        }
     }
     s.n_parts = part_off[n * G];
     return s;
@@ -89,14 +120,14 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
 inline BatchView bind_plan(const int32_t *d, int32_t n, int32_t G, const PlanSummary &s,
                            int32_t W) {
     BatchView b;
-    b.pos = d;
-    b.ntok = d + n;
-    b.npages = d + 2 * n;
-    b.page_off = d + 3 * n;
+    b.warp_start = reinterpret_cast<const int4 *>(d);
+    b.pos = d + kWarpStartWords * W;
+    b.ntok = b.pos + n;
+    b.npages = b.ntok + n;
+    b.page_off = b.npages + n;
     b.unit_off = b.page_off + (n + 1);
     b.part_off = b.unit_off + (n + 1);
-    b.warp_entry = b.part_off + (n * G + 1);
-    b.pages = b.warp_entry + W;
+    b.pages = b.part_off + (n * G + 1);
     b.n = n;
     b.total_units = static_cast<int32_t>(s.total_units);
     b.n_warps = W;

@@ -8,8 +8,8 @@
  * the BF16 table (:471-506) and the GQA decode attention chain (:5750-5786).
  *
  * Storage model: one page pool per engine (per GPU).  A page holds 16
- * consecutive token positions of one slot for ALL layers, K and V, all KV
- * heads, in F16.  Each live slot owns a page list; pages are reference
+ * consecutive token positions of one slot for ALL layers (one block in each
+ * layer's slab), K and V, all KV heads, in F16.  Each live slot owns a page list; pages are reference
  * counted so slots can share a prefix (fork / published prefixes) and are
  * copied on the first write into a shared page (copy-on-write).
  *
@@ -226,10 +226,11 @@ int hkv_rope_tables(const hkv_engine *eng, float *cos_out, float *sin_out);
 
 /* ---------------------------------------------------- no allocation -- */
 
-/* Device memory a caller already owns, in the engine's page layout: a page is
- * n_layers x {K, V} x n_head_kv head blocks of 16 rows x 128 F16 dims (4 KiB),
- * block(page, layer, kv, head) = ((page*n_layers + layer)*2 + kv)*n_head_kv
- * + head, and row r keeps its 16-byte chunk c at position c ^ (r & 7).
+/* Device memory a caller already owns, in the engine's page layout: one slab
+ * per layer, each page of a slab {K, V} x n_head_kv head blocks of 16 rows x
+ * 128 F16 dims (4 KiB), block(page, layer, kv, head) =
+ * ((layer*n_pages + page)*2 + kv)*n_head_kv + head, and row r keeps its
+ * 16-byte chunk c at position c ^ (r & 7).
  * rope_cos / rope_sin: [context_length][64] F32 BF16-rounded tables. */
 typedef struct hkv_paged_view {
     void *pool;

@@ -47,7 +47,7 @@ def caller_pool(rows_by_slot, layer, n_layers):
         page = np.array(pages)[t // 16]
         r = t % 16
         for kv, rows in ((0, k_rows), (1, v_rows)):
-            block = ((page[:, None] * n_layers + layer) * 2 + kv) * G + np.arange(G)[None, :]
+            block = ((layer * n_pages + page[:, None]) * 2 + kv) * G + np.arange(G)[None, :]
             chunk = np.arange(16)[None, None, :] ^ (r[:, None, None] & 7)
             base = (block[:, :, None] * (16 * D) + r[:, None, None] * D + chunk * 8)
             idx = base[..., None] + np.arange(8)
