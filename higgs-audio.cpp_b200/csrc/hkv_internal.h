@@ -76,9 +76,16 @@ struct RopeView {
     int32_t context_length;
 };
 
-// Attention launch geometry (fixed per build).
-constexpr int kAttnWarps = 8;     // consumer warps per CTA, one CTA per SM
-constexpr int kAttnStages = 3;    // TMA ring depth per warp (K+V head block per stage)
+// Attention launch geometry (fixed per build; the -D overrides exist for
+// tuning sweeps).  Default: 8 warps per CTA, one CTA per SM, 3 stages each.
+#ifndef HKV_ATTN_WARPS
+#define HKV_ATTN_WARPS 8
+#endif
+#ifndef HKV_ATTN_STAGES
+#define HKV_ATTN_STAGES 3
+#endif
+constexpr int kAttnWarps = HKV_ATTN_WARPS;    // consumer warps per CTA, one CTA per SM
+constexpr int kAttnStages = HKV_ATTN_STAGES;  // TMA ring depth per warp (K+V block per stage)
 
 void launch_append(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
                    const float *k, const float *v, bool apply_rope, DeviceError *err,

@@ -39,13 +39,15 @@ constexpr int kStageBytes = 2 * kHeadBlockBytes;  // K block + V block
 constexpr int kQcStride = 136;                     // halves per staged-query row (272 B)
 constexpr int kQcBytes = 8 * kQcStride * 2;        // 8 rows: 4 heads x {hi, lo}
 constexpr int kPBufBytes = 16 * 16;                // 16 tokens x 8 halves
-constexpr int kWarpSmem = kAttnStages * kStageBytes + kQcBytes + kPBufBytes + 32;
+constexpr int kBarBytes = (kAttnStages * 8 + 15) / 16 * 16;  // one 8-byte mbarrier per stage
+constexpr int kWarpSmem = kAttnStages * kStageBytes + kQcBytes + kPBufBytes + kBarBytes;
 constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int kWhereAppend = 0;
 constexpr int kWhereAttn = 1;
 constexpr int kWhereGather = 3;
 
 static_assert(kWarpSmem % 16 == 0, "per-warp shared region must keep 16-byte alignment");
+static_assert(kBarBytes >= 8 * kAttnStages, "every stage needs its mbarrier inside the warp's region");
 static_assert(kAttnWarps * kWarpSmem <= 227 * 1024, "attention CTA exceeds shared memory");
 
 __device__ __forceinline__ void record_error(DeviceError *err, int code, int where, int a, int b) {
@@ -470,11 +472,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     Cursor prod = cons;
     int64_t next_page = 0;
     if (lane == 0) {
-        const int first_pages[kAttnStages] = {ws1.y, ws1.z, ws1.w};
+        const int first_pages[3] = {ws1.y, ws1.z, ws1.w};
 #pragma unroll
         for (int s = 0; s < kAttnStages; ++s) {
             if (u_begin + s < u_end) {
-                const int64_t page = checked_page(pool, first_pages[s], prod.e, err);
+                const int64_t page = checked_page(
+                    pool, s < 3 ? first_pages[s] : batch.pages[prod.pbase + prod.i], prod.e, err);
                 issue_unit(pool, layer, page, prod.h, stage0 + s * kStageBytes, bar0 + 8 * s, policy);
                 advance(batch, G, prod);
             }
@@ -677,16 +680,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
 
         // ---- S^T[token][col] = K[token][:] . Qc[col][:]   (col 0-3 hi, 4-7 lo)
+        // Two accumulators (even / odd k-steps) halve the dependent mma chain.
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        float sd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-            uint32_t a0, a1, a2, a3;
-            const int chunk = 2 * ks + k_chunk_hi;
-            ldsm_x4(kt + k_row_off + ((chunk ^ r7) << 4), a0, a1, a2, a3);
+        for (int ks = 0; ks < 8; ks += 2) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            ldsm_x4(kt + k_row_off + (((2 * ks + k_chunk_hi) ^ r7) << 4), a0, a1, a2, a3);
+            ldsm_x4(kt + k_row_off + (((2 * ks + 2 + k_chunk_hi) ^ r7) << 4), b0, b1, b2, b3);
             mma_16816(sc, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+            mma_16816(sd, b0, b1, b2, b3, qb[ks + 1][0], qb[ks + 1][1]);
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
+            sc[j] += sd[j];
             sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], 2);
         }
         const int tok = row0 + (lane >> 2);

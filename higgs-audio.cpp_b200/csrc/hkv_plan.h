@@ -80,7 +80,6 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         }
     }
     int32_t e = 0;
-    static_assert(kAttnStages == 3, "warp_start carries the first three page ids");
     for (int32_t k = 0; k < W; ++k) {
         const int64_t ub = static_cast<int64_t>(k) * U / W;
         const int64_t ue = static_cast<int64_t>(k + 1) * U / W;
