@@ -218,6 +218,11 @@ struct BatchCache {
     std::vector<int32_t> slots;
     std::vector<int64_t> used;
     BatchView view{};
+    // Kernels read the descriptor until the batch changes; its staging buffer
+    // is marked used (event on the consumers' stream) only then, so no event
+    // sits between the consecutive launches of a step.
+    bool consumed = false;
+    cudaStream_t consumer_stream = nullptr;
 };
 
 struct ProfileRecord {
@@ -260,6 +265,15 @@ struct hkv_engine {
     float scale_log2 = 0.f;
     hkv::Staging batch_stage, range_stage, gather_stage;
     hkv::BatchCache batch;
+
+    // Launch overlap bookkeeping: a decode launch may start while the previous
+    // kernel in the stream finishes (programmatic dependent launch) only if
+    // that kernel was this engine's decode launch of another layer on the same
+    // stream with nothing else enqueued by the engine in between.
+    uint64_t enqueue_seq = 0;       // bumped by every non-decode enqueue
+    uint64_t last_decode_seq = ~0ull;
+    int32_t last_decode_layer = -1;
+    cudaStream_t last_decode_stream = nullptr;
 
     // profiling
     bool profiling = false;
@@ -383,6 +397,7 @@ int own_rows(hkv_engine *eng, Slot &s, int64_t begin, int64_t end, cudaStream_t 
             const int32_t old = s.pages[p];
             const int32_t fresh = take_page(eng, s);
             if (eng->device_mode) {
+                ++eng->enqueue_seq;
                 // The page lives in every layer's slab: one copy per layer.
                 for (int32_t layer = 0; layer < eng->cfg.n_layers; ++layer) {
                     HKV_CUDA_TRY(eng, cudaMemcpyAsync(page_ptr(eng, layer, fresh),
@@ -534,6 +549,10 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
     }
     const int32_t W = plan_warps(total_pages * G, static_cast<int64_t>(eng->num_sms) * kAttnWarps);
     const size_t words = plan_words(n, G, total_pages, W);
+    if (bc.consumed) {
+        HKV_CUDA_TRY(eng, eng->batch_stage.mark_used(bc.consumer_stream));
+        bc.consumed = false;
+    }
     void *host = nullptr;
     HKV_CUDA_TRY(eng, eng->batch_stage.begin(words * sizeof(int32_t), &host));
     const PlanSummary plan =
@@ -543,6 +562,7 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
                     static_cast<long long>(eng->part_cap));
     }
     void *dev = nullptr;
+    ++eng->enqueue_seq;
     HKV_CUDA_TRY(eng, eng->batch_stage.commit(words * sizeof(int32_t), stream, &dev));
     bc.view = bind_plan(static_cast<const int32_t *>(dev), n, G, plan, W);
     bc.slots.assign(slots, slots + n);
@@ -572,12 +592,14 @@ int do_append(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots, c
     }
     st = ensure_batch(eng, n, slots, stream);
     if (st != HKV_OK) return st;
+    ++eng->enqueue_seq;
     {
         ProfileScope ps(eng, HKV_KERNEL_APPEND, stream);
         launch_append(pool_view(eng), rope_view(eng), eng->batch.view, layer, k, v, rope,
                       eng->d_err, stream);
     }
-    HKV_CUDA_TRY(eng, eng->batch_stage.mark_used(stream));
+    eng->batch.consumed = true;
+    eng->batch.consumer_stream = stream;
     return launch_status(eng, "append kernel launch");
 }
 
@@ -585,13 +607,21 @@ int do_append(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots, c
 // fused decode step (append + attention).
 int do_attention(hkv_engine *eng, int32_t layer, const float *q, const float *k_new,
                  const float *v_new, float *out, cudaStream_t stream) {
+    // Profiling brackets each launch with events, which would sit between the
+    // kernels, so overlap is only used when profiling is off.
+    const bool overlap = !eng->profiling && eng->last_decode_seq == eng->enqueue_seq &&
+                         eng->last_decode_stream == stream && eng->last_decode_layer != layer;
     {
         ProfileScope ps(eng, k_new != nullptr ? HKV_KERNEL_STEP : HKV_KERNEL_ATTN, stream);
         launch_attention(pool_view(eng), rope_view(eng), eng->batch.view, layer, q, k_new, v_new,
                          eng->part_o, eng->part_ml, eng->counters, out, eng->scale_log2,
-                         eng->d_err, stream);
+                         eng->d_err, overlap, stream);
     }
-    HKV_CUDA_TRY(eng, eng->batch_stage.mark_used(stream));
+    eng->last_decode_seq = eng->enqueue_seq;
+    eng->last_decode_layer = layer;
+    eng->last_decode_stream = stream;
+    eng->batch.consumed = true;
+    eng->batch.consumer_stream = stream;
     return launch_status(eng, "attention kernel launch");
 }
 
@@ -1081,6 +1111,7 @@ int hkv_rope_append_range(hkv_engine *eng, int32_t layer, int32_t slot, int64_t 
     HKV_CUDA_TRY(eng, eng->range_stage.begin(bytes, &host));
     std::memcpy(host, s.pages.data() + p0, bytes);
     void *dev = nullptr;
+    ++eng->enqueue_seq;
     HKV_CUDA_TRY(eng, eng->range_stage.commit(bytes, stream, &dev));
     {
         ProfileScope ps(eng, HKV_KERNEL_APPEND, stream);
@@ -1153,6 +1184,7 @@ int hkv_gather(hkv_engine *eng, int32_t slot, int32_t layer, int64_t pos0, int64
     HKV_CUDA_TRY(eng, eng->gather_stage.begin(bytes, &host));
     std::memcpy(host, s.pages.data(), bytes);
     void *dev = nullptr;
+    ++eng->enqueue_seq;
     HKV_CUDA_TRY(eng, eng->gather_stage.commit(bytes, stream, &dev));
     {
         ProfileScope ps(eng, HKV_KERNEL_GATHER, stream);

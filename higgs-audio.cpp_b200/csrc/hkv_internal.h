@@ -77,12 +77,14 @@ struct RopeView {
 };
 
 // Attention launch geometry (fixed per build; the -D overrides exist for
-// tuning sweeps).  Default: 8 warps per CTA, one CTA per SM, 3 stages each.
+// tuning sweeps).  Default: 6 warps per CTA, one CTA per SM, 2 stages each
+// (113 KB of shared memory): the best of the measured 4-12 warp x 1-6 stage
+// grid on both the 32-slot and the 16-slot decode workloads.
 #ifndef HKV_ATTN_WARPS
-#define HKV_ATTN_WARPS 8
+#define HKV_ATTN_WARPS 6
 #endif
 #ifndef HKV_ATTN_STAGES
-#define HKV_ATTN_STAGES 3
+#define HKV_ATTN_STAGES 2
 #endif
 constexpr int kAttnWarps = HKV_ATTN_WARPS;    // consumer warps per CTA, one CTA per SM
 constexpr int kAttnStages = HKV_ATTN_STAGES;  // TMA ring depth per warp (K+V block per stage)
@@ -97,11 +99,15 @@ void launch_append_range(const PoolView &pool, const RopeView &rope, const int32
 // last warp to finish a (slot, KV head) merges).  If k_new / v_new are
 // non-null, the warp owning each slot's last page also ropes and writes the
 // slot's new K/V row (the fused decode step).  counters: n * n_head_kv
-// zero-initialised ints, left zero on exit.
+// zero-initialised ints, left zero on exit.  overlap_previous launches with
+// programmatic stream serialization: the kernel's prologue (its plan and the
+// first copies of this layer's pages) may run before the previous kernel in
+// the stream has finished, so the caller may set it only when that kernel
+// cannot have written this layer's pages.
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
                       const float *q, const float *k_new, const float *v_new, float *part_o,
                       float *part_ml, int32_t *counters, float *out, float scale_log2,
-                      DeviceError *err, cudaStream_t stream);
+                      DeviceError *err, bool overlap_previous, cudaStream_t stream);
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
                    int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
                    cudaStream_t stream);

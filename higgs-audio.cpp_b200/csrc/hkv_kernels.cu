@@ -487,6 +487,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
     }
 
+    // Programmatic dependent launch: everything above only reads this launch's
+    // plan and this layer's pages; q / k / v may come from the kernel before,
+    // and the partials, counters and outputs may still be in use by it, so
+    // wait for it here (a no-op when launched without the attribute).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
     const int r7 = lane & 7;
     const int mi = lane >> 3;
     // Per-lane byte offsets inside a head block for the ldmatrix row addresses.
@@ -759,6 +765,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
         advance(batch, G, cons);
     }
+    // Let the next launch in the stream start its prologue while this CTA
+    // finishes its tail.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     flush();
 }
 
@@ -831,7 +840,8 @@ template <bool kAppend>
 void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchView &batch,
                         int layer, const float *q, const float *k_new, const float *v_new,
                         float *part_o, float *part_ml, int32_t *counters, float *out,
-                        float scale_log2, DeviceError *err, cudaStream_t stream) {
+                        float scale_log2, DeviceError *err, bool overlap_previous,
+                        cudaStream_t stream) {
     // The dynamic shared-memory opt-in is per device and per kernel.
     static bool configured[64] = {};
     int dev = 0;
@@ -844,20 +854,30 @@ void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchV
         }
     }
     const int grid = (batch.n_warps + kAttnWarps - 1) / kAttnWarps;
-    attention_kernel<kAppend><<<grid, kAttnWarps * 32, attention_smem_bytes(), stream>>>(
-        pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml, counters, out, scale_log2, err);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kAttnWarps * 32);
+    cfg.dynamicSmemBytes = attention_smem_bytes();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = overlap_previous ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, attention_kernel<kAppend>, pool, rope, batch, layer, q, k_new, v_new,
+                       part_o, part_ml, counters, out, scale_log2, err);
 }
 
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
                       const float *q, const float *k_new, const float *v_new, float *part_o,
                       float *part_ml, int32_t *counters, float *out, float scale_log2,
-                      DeviceError *err, cudaStream_t stream) {
+                      DeviceError *err, bool overlap_previous, cudaStream_t stream) {
     if (k_new != nullptr && v_new != nullptr) {
         launch_attention_t<true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
-                                 counters, out, scale_log2, err, stream);
+                                 counters, out, scale_log2, err, overlap_previous, stream);
     } else {
         launch_attention_t<false>(pool, rope, batch, layer, q, nullptr, nullptr, part_o, part_ml,
-                                  counters, out, scale_log2, err, stream);
+                                  counters, out, scale_log2, err, overlap_previous, stream);
     }
 }
 
