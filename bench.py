@@ -417,8 +417,11 @@ def bench_ours(args):
 
 def bench_headsplit(args):
     """One long request split by KV head across the ranks (HeadSplit): rank g
-    holds KV heads [8g/N, 8(g+1)/N) of every layer, attends its 32/N query
-    heads, and one NCCL all-gather per layer assembles the head-major output."""
+    holds KV heads [8g/N, 8(g+1)/N) of every layer and attends its 32/N query
+    heads.  The head-major output of each layer is assembled on every rank
+    either inside the decode kernel (--xchg p2p: peer stores over NVLink +
+    a bounded arrival wait, hkv_split_step / hkv_split_wait) or by an NCCL
+    all-gather after it (--xchg nccl)."""
     import datetime
 
     import torch
@@ -464,11 +467,22 @@ def bench_headsplit(args):
         out_full = torch.empty((N_LAYERS, world, Hl * D), device=dev)
     eng.sync_check(sh)
 
+    p2p = dist is not None and args.xchg == "p2p"
+    if p2p:
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.split_export(world, rank))
+        eng.split_connect(handles)
+        dist.barrier()
+
     def step():
         for layer in range(N_LAYERS):
-            eng.decode_step(layer, [slot], q[layer], k[layer], v[layer], out_local[layer], sh)
-            if dist is not None:
-                dist.all_gather_into_tensor(out_full[layer], out_local[layer])
+            if p2p:
+                eng.split_step(layer, [slot], q[layer], k[layer], v[layer], sh)
+                eng.split_wait(layer, sh)
+            else:
+                eng.decode_step(layer, [slot], q[layer], k[layer], v[layer], out_local[layer], sh)
+                if dist is not None:
+                    dist.all_gather_into_tensor(out_full[layer], out_local[layer])
         eng.advance([slot], 1)
 
     with torch.cuda.stream(stream):
@@ -493,7 +507,7 @@ def bench_headsplit(args):
         ms = float(t.item())
     eng.sync_check(sh)
     # full-output check of the assembly on the last layer: rank order == head order
-    if dist is not None:
+    if dist is not None and not p2p:
         full = split.gather_output(out_local[N_LAYERS - 1])
         assert torch.equal(full.view(world, Hl * D), out_full[N_LAYERS - 1])
     rows = sum(ctx0 + s for s in range(args.steps))
@@ -508,14 +522,21 @@ def bench_headsplit(args):
             "vs_baseline": None, "dtype": "f16 KV, f32 accumulate",
             "data": "synthetic N(0,1) (torch generator on device)",
             "config": {"workload": (f"one {ctx0}-position request split by KV head over "
-                                    f"{world} GPU(s), {Gl} KV heads each, 36 layers, NCCL "
-                                    "all-gather of the per-head outputs every layer"),
+                                    f"{world} GPU(s), {Gl} KV heads each, 36 layers; per-head "
+                                    "outputs assembled every layer by "
+                                    + ("in-kernel peer stores (NVLink)" if p2p else
+                                       ("NCCL all-gather" if dist is not None else "-"))),
                        "global_batch": 1, "layers": N_LAYERS,
                        "parallelism": f"KV-head split x{world}"},
             "hbm": {"step_gbs_per_gpu": gbs, "peak_gbs": peak, "frac": gbs / peak,
                     "peak_kind": peak_kind},
             "gpu_launches": N_LAYERS * args.steps, "e2e": None,
         }), flush=True)
+    if p2p:
+        dist.barrier()
+        eng.split_disconnect()
+    if dist is not None:
+        dist.barrier()
     eng.close()
     if dist is not None:
         dist.barrier()
@@ -569,6 +590,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="scaleout")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
+                    help="headsplit: how the per-head outputs reach every rank")
     ap.add_argument("--layers", type=int, default=36,
                     help="layers per step (36 for every reported number; fewer only for "
                          "profiler captures of the same per-launch sizes)")

@@ -275,6 +275,19 @@ struct hkv_engine {
     int32_t last_decode_layer = -1;
     cudaStream_t last_decode_stream = nullptr;
 
+    // KV-head split exchange (hkv_split_*): this rank's region holds the
+    // per-layer arrival counters, then the head-major output rows of all ranks.
+    int32_t split_world = 0;
+    int32_t split_rank = -1;
+    uint8_t *xchg = nullptr;
+    size_t xchg_flags_bytes = 0;
+    int32_t xchg_row_floats = 0;
+    std::vector<void *> peer_bases;          // opened IPC mappings (nullptr for self)
+    float **d_outs = nullptr;                // [world] device array
+    uint32_t **d_flags = nullptr;            // [world] device array
+    std::vector<uint32_t> split_target;      // expected arrivals per layer
+    bool split_connected = false;
+
     // profiling
     bool profiling = false;
     std::vector<hkv::ProfileRecord> prof[HKV_KERNEL_COUNT];
@@ -606,7 +619,8 @@ int do_append(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots, c
 // One attention launch over the current batch; with k_new / v_new it is the
 // fused decode step (append + attention).
 int do_attention(hkv_engine *eng, int32_t layer, const float *q, const float *k_new,
-                 const float *v_new, float *out, cudaStream_t stream) {
+                 const float *v_new, float *out, cudaStream_t stream,
+                 const Exchange &xchg = Exchange{nullptr, nullptr, 0, 0, 0, 0}) {
     // Profiling brackets each launch with events, which would sit between the
     // kernels, so overlap is only used when profiling is off.
     const bool overlap = !eng->profiling && eng->last_decode_seq == eng->enqueue_seq &&
@@ -614,8 +628,8 @@ int do_attention(hkv_engine *eng, int32_t layer, const float *q, const float *k_
     {
         ProfileScope ps(eng, k_new != nullptr ? HKV_KERNEL_STEP : HKV_KERNEL_ATTN, stream);
         launch_attention(pool_view(eng), rope_view(eng), eng->batch.view, layer, q, k_new, v_new,
-                         eng->part_o, eng->part_ml, eng->counters, out, eng->scale_log2,
-                         eng->d_err, overlap, stream);
+                         eng->part_o, eng->part_ml, eng->counters, out, xchg,
+                         eng->scale_log2, eng->d_err, overlap, stream);
     }
     eng->last_decode_seq = eng->enqueue_seq;
     eng->last_decode_layer = layer;
@@ -625,7 +639,26 @@ int do_attention(hkv_engine *eng, int32_t layer, const float *q, const float *k_
     return launch_status(eng, "attention kernel launch");
 }
 
+void free_split(hkv_engine *eng) {
+    for (void *p : eng->peer_bases) {
+        if (p != nullptr) {
+            cudaIpcCloseMemHandle(p);
+        }
+    }
+    eng->peer_bases.clear();
+    cudaFree(eng->d_outs);
+    cudaFree(eng->d_flags);
+    cudaFree(eng->xchg);
+    eng->d_outs = nullptr;
+    eng->d_flags = nullptr;
+    eng->xchg = nullptr;
+    eng->split_world = 0;
+    eng->split_rank = -1;
+    eng->split_connected = false;
+}
+
 void free_device(hkv_engine *eng) {
+    free_split(eng);
     eng->batch_stage.release();
     eng->range_stage.release();
     eng->gather_stage.release();
@@ -1224,6 +1257,151 @@ int hkv_rope_tables(const hkv_engine *eng, float *cos_out, float *sin_out) {
     std::lock_guard<std::mutex> lock(eng->mu);
     std::memcpy(cos_out, eng->rope_cos.data(), eng->rope_cos.size() * sizeof(float));
     std::memcpy(sin_out, eng->rope_sin.data(), eng->rope_sin.size() * sizeof(float));
+    return HKV_OK;
+}
+
+// ---------------------------------------------------------- KV-head split
+
+int hkv_split_export(hkv_engine *eng, int32_t world, int32_t rank, void *handle_out) {
+    if (eng == nullptr || handle_out == nullptr) return HKV_ERR_INVALID;
+    std::lock_guard<std::mutex> lock(eng->mu);
+    if (!eng->device_mode) {
+        return fail(eng, HKV_ERR_NO_DEVICE, "engine was created without a device");
+    }
+    if (world < 1 || rank < 0 || rank >= world) {
+        return fail(eng, HKV_ERR_INVALID, "rank %d outside a world of %d", rank, world);
+    }
+    DeviceGuard guard(eng->cfg.device);
+    free_split(eng);
+    eng->xchg_flags_bytes = (static_cast<size_t>(eng->cfg.n_layers) * sizeof(uint32_t) + 255) & ~size_t(255);
+    eng->xchg_row_floats = world * kGqa * eng->cfg.n_head_kv * kHeadDim;
+    const size_t bytes = eng->xchg_flags_bytes + static_cast<size_t>(eng->cfg.n_layers) *
+                                                     eng->cfg.max_slots * eng->xchg_row_floats *
+                                                     sizeof(float);
+    HKV_CUDA_TRY(eng, cudaMalloc(&eng->xchg, bytes));
+    HKV_CUDA_TRY(eng, cudaMemset(eng->xchg, 0, bytes));
+    cudaIpcMemHandle_t h;
+    HKV_CUDA_TRY(eng, cudaIpcGetMemHandle(&h, eng->xchg));
+    std::memcpy(handle_out, &h, sizeof(h));
+    eng->split_world = world;
+    eng->split_rank = rank;
+    eng->split_target.assign(static_cast<size_t>(eng->cfg.n_layers), 0u);
+    HKV_CUDA_TRY(eng, cudaDeviceSynchronize());
+    return HKV_OK;
+}
+
+int hkv_split_connect(hkv_engine *eng, const void *handles) {
+    if (eng == nullptr) return HKV_ERR_INVALID;
+    std::lock_guard<std::mutex> lock(eng->mu);
+    if (eng->xchg == nullptr) {
+        return fail(eng, HKV_ERR_INVALID, "hkv_split_export first");
+    }
+    DeviceGuard guard(eng->cfg.device);
+    if (handles == nullptr) {
+        // Disconnect: close the peers' mappings, keep this rank's region.
+        HKV_CUDA_TRY(eng, cudaDeviceSynchronize());
+        for (void *p : eng->peer_bases) {
+            if (p != nullptr) {
+                HKV_CUDA_TRY(eng, cudaIpcCloseMemHandle(p));
+            }
+        }
+        eng->peer_bases.clear();
+        cudaFree(eng->d_outs);
+        cudaFree(eng->d_flags);
+        eng->d_outs = nullptr;
+        eng->d_flags = nullptr;
+        eng->split_connected = false;
+        return HKV_OK;
+    }
+    const int32_t world = eng->split_world;
+    eng->peer_bases.assign(static_cast<size_t>(world), nullptr);
+    std::vector<float *> outs(static_cast<size_t>(world));
+    std::vector<uint32_t *> flags(static_cast<size_t>(world));
+    for (int32_t r = 0; r < world; ++r) {
+        uint8_t *base = eng->xchg;
+        if (r != eng->split_rank) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const uint8_t *>(handles) + r * sizeof(h), sizeof(h));
+            void *p = nullptr;
+            const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                return cuda_fail(eng, e, "cudaIpcOpenMemHandle of a peer's exchange region");
+            }
+            eng->peer_bases[r] = p;
+            base = static_cast<uint8_t *>(p);
+        }
+        flags[r] = reinterpret_cast<uint32_t *>(base);
+        outs[r] = reinterpret_cast<float *>(base + eng->xchg_flags_bytes);  // layer 0 block
+    }
+    HKV_CUDA_TRY(eng, cudaMalloc(&eng->d_outs, world * sizeof(float *)));
+    HKV_CUDA_TRY(eng, cudaMalloc(&eng->d_flags, world * sizeof(uint32_t *)));
+    HKV_CUDA_TRY(eng, cudaMemcpy(eng->d_outs, outs.data(), world * sizeof(float *),
+                                 cudaMemcpyHostToDevice));
+    HKV_CUDA_TRY(eng, cudaMemcpy(eng->d_flags, flags.data(), world * sizeof(uint32_t *),
+                                 cudaMemcpyHostToDevice));
+    eng->split_connected = true;
+    return HKV_OK;
+}
+
+int hkv_split_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
+                   const float *q_prerope, const float *k_prerope, const float *v,
+                   hkv_stream stream_h) {
+    if (eng == nullptr) return HKV_ERR_INVALID;
+    std::lock_guard<std::mutex> lock(eng->mu);
+    DeviceGuard guard(eng->cfg.device);
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_h);
+    int st = check_compute(eng, layer);
+    if (st != HKV_OK) return st;
+    if (!eng->split_connected) {
+        return fail(eng, HKV_ERR_INVALID, "hkv_split_connect first");
+    }
+    if (q_prerope == nullptr || k_prerope == nullptr || v == nullptr || !aligned16(q_prerope) ||
+        !aligned16(k_prerope) || !aligned16(v)) {
+        return fail(eng, HKV_ERR_INVALID, "q, k and v must be non-null 16-byte aligned device pointers");
+    }
+    st = ensure_batch(eng, n, slots, stream);
+    if (st != HKV_OK) return st;
+    Exchange x;
+    x.outs = eng->d_outs;
+    x.flags = eng->d_flags;
+    x.n_ranks = eng->split_world;
+    x.row_floats = eng->xchg_row_floats;
+    x.col_off = eng->split_rank * kGqa * eng->cfg.n_head_kv * kHeadDim;
+    x.layer_floats = static_cast<int64_t>(eng->cfg.max_slots) * eng->xchg_row_floats;
+    st = do_attention(eng, layer, q_prerope, k_prerope, v, nullptr, stream, x);
+    if (st != HKV_OK) return st;
+    // every rank's kernel signals once per (entry, KV head)
+    eng->split_target[layer] += static_cast<uint32_t>(n) * eng->cfg.n_head_kv * eng->split_world;
+    return HKV_OK;
+}
+
+int hkv_split_wait(hkv_engine *eng, int32_t layer, hkv_stream stream_h) {
+    if (eng == nullptr) return HKV_ERR_INVALID;
+    std::lock_guard<std::mutex> lock(eng->mu);
+    DeviceGuard guard(eng->cfg.device);
+    int st = check_compute(eng, layer);
+    if (st != HKV_OK) return st;
+    if (!eng->split_connected) {
+        return fail(eng, HKV_ERR_INVALID, "hkv_split_connect first");
+    }
+    ++eng->enqueue_seq;
+    launch_split_wait(reinterpret_cast<const uint32_t *>(eng->xchg) + layer,
+                      eng->split_target[layer], eng->d_err, static_cast<cudaStream_t>(stream_h));
+    return launch_status(eng, "split wait launch");
+}
+
+int hkv_split_output(const hkv_engine *eng, int32_t layer, float **out_dev, int64_t *row_floats) {
+    if (eng == nullptr || out_dev == nullptr || row_floats == nullptr) return HKV_ERR_INVALID;
+    std::lock_guard<std::mutex> lock(eng->mu);
+    if (eng->xchg == nullptr) {
+        return fail(eng, HKV_ERR_INVALID, "hkv_split_export first");
+    }
+    if (layer < 0 || layer >= eng->cfg.n_layers) {
+        return fail(eng, HKV_ERR_RANGE, "layer %d outside [0, %d)", layer, eng->cfg.n_layers);
+    }
+    *out_dev = reinterpret_cast<float *>(eng->xchg + eng->xchg_flags_bytes) +
+               static_cast<int64_t>(layer) * eng->cfg.max_slots * eng->xchg_row_floats;
+    *row_floats = eng->xchg_row_floats;
     return HKV_OK;
 }
 

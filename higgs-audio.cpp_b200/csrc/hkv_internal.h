@@ -70,6 +70,22 @@ struct PoolView {
     int32_t n_head_kv;
 };
 
+// Where finished outputs go.  n_ranks == 0: the caller's `out` only.
+// Otherwise (KV-head split of one batch across ranks) every finished
+// (entry, KV head) slice is stored into each rank's exchange region --
+// outs[r] + layer * layer_floats + entry * row_floats + col_off + head
+// slice, over NVLink for the peers -- and each rank's arrival counter for the
+// layer is bumped once.  One output block per layer, so a rank that runs
+// ahead never overwrites a layer its peers have not consumed yet.
+struct Exchange {
+    float *const *outs;       // [n_ranks] output regions (device-visible pointers)
+    uint32_t *const *flags;   // [n_ranks] per-layer arrival counters
+    int32_t n_ranks;
+    int32_t row_floats;       // floats per entry row: 4 * n_head_kv(total) * 128
+    int32_t col_off;          // this rank's first column
+    int64_t layer_floats;     // floats per layer block (max entries * row_floats)
+};
+
 struct RopeView {
     const float *cos_tab;  // [context][64]
     const float *sin_tab;
@@ -106,8 +122,13 @@ void launch_append_range(const PoolView &pool, const RopeView &rope, const int32
 // cannot have written this layer's pages.
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
                       const float *q, const float *k_new, const float *v_new, float *part_o,
-                      float *part_ml, int32_t *counters, float *out, float scale_log2,
-                      DeviceError *err, bool overlap_previous, cudaStream_t stream);
+                      float *part_ml, int32_t *counters, float *out, const Exchange &xchg,
+                      float scale_log2, DeviceError *err, bool overlap_previous,
+                      cudaStream_t stream);
+// Bounded wait (one thread) until *flag has reached `target` arrivals
+// (wrap-around safe); records kErrTimeout and returns if it never does.
+void launch_split_wait(const uint32_t *flag, uint32_t target, DeviceError *err,
+                       cudaStream_t stream);
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
                    int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
                    cudaStream_t stream);

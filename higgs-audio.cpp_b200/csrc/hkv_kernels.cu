@@ -45,6 +45,7 @@ constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int kWhereAppend = 0;
 constexpr int kWhereAttn = 1;
 constexpr int kWhereGather = 3;
+constexpr int kWhereSplitWait = 5;
 
 static_assert(kWarpSmem % 16 == 0, "per-warp shared region must keep 16-byte alignment");
 static_assert(kBarBytes >= 8 * kAttnStages, "every stage needs its mbarrier inside the warp's region");
@@ -341,7 +342,7 @@ __device__ __forceinline__ uint4 new_row_chunk(const RopeView &rope, const float
 // shuffles); the partial outputs are then streamed with the weights
 // broadcast from their owner lane, several partials in flight at a time.
 __device__ __forceinline__ void merge_partials(const float *part_o, const float *part_ml, int p0,
-                                               int nparts, float *out_base, int lane) {
+                                               int nparts, int lane, float4 (&res)[kGqa]) {
     float mx[kGqa];
 #pragma unroll
     for (int j = 0; j < kGqa; ++j) {
@@ -410,12 +411,35 @@ __device__ __forceinline__ void merge_partials(const float *part_o, const float 
             den[j] += __shfl_xor_sync(0xffffffffu, den[j], off);
         }
     }
-    float4 *ob = reinterpret_cast<float4 *>(out_base);
 #pragma unroll
     for (int j = 0; j < kGqa; ++j) {
         const float inv = 1.f / den[j];
-        ob[j * (kHeadDim / 4) + lane] =
-            make_float4(acc[j].x * inv, acc[j].y * inv, acc[j].z * inv, acc[j].w * inv);
+        res[j] = make_float4(acc[j].x * inv, acc[j].y * inv, acc[j].z * inv, acc[j].w * inv);
+    }
+}
+
+// Destination of the 4 x 128 output floats of (entry e, KV head h).
+__device__ __forceinline__ float *out_slice(float *out, const Exchange &x, int r, int layer, int e,
+                                            int h, int G) {
+    if (x.n_ranks == 0) {
+        return out + (static_cast<int64_t>(e) * (kGqa * G) + kGqa * h) * kHeadDim;
+    }
+    return x.outs[r] + layer * x.layer_floats + static_cast<int64_t>(e) * x.row_floats + x.col_off +
+           kGqa * h * kHeadDim;
+}
+
+// After a warp has stored a finished slice everywhere: make the stores
+// visible system-wide, then count one arrival at every rank for this layer.
+__device__ __forceinline__ void signal_arrival(const Exchange &x, int layer, int lane) {
+    if (x.n_ranks == 0) {
+        return;
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+        for (int r = 0; r < x.n_ranks; ++r) {
+            atomicAdd_system(x.flags[r] + layer, 1u);
+        }
     }
 }
 
@@ -425,7 +449,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                      const float *__restrict__ q, const float *__restrict__ k_new,
                      const float *__restrict__ v_new, float *__restrict__ part_o,
                      float *__restrict__ part_ml, int32_t *__restrict__ counters,
-                     float *__restrict__ out, float scale_log2, DeviceError *err) {
+                     float *__restrict__ out, Exchange xchg, float scale_log2, DeviceError *err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int lane = threadIdx.x & 31;
     const int wid = threadIdx.x >> 5;
@@ -524,20 +548,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         l_b += __shfl_xor_sync(0xffffffffu, l_b, 16);
         const int ha = (lane & 1) * 2;
         const int d0 = lane >> 2;
-        float *out_base = out + (static_cast<int64_t>(seg_e) * (kGqa * G) + kGqa * seg_h) * kHeadDim;
+        const int n_dst = xchg.n_ranks == 0 ? 1 : xchg.n_ranks;
         if (nparts == 1) {
             // The whole (slot, KV head) was this warp's: write the output.
             if (!lo_side) {
                 const float ia = 1.f / l_a;
                 const float ib = 1.f / l_b;
+                for (int r = 0; r < n_dst; ++r) {
+                    float *ob = out_slice(out, xchg, r, layer, seg_e, seg_h, G);
 #pragma unroll
-                for (int mt = 0; mt < 8; ++mt) {
-                    out_base[ha * kHeadDim + 16 * mt + d0] = o[mt][0] * ia;
-                    out_base[(ha + 1) * kHeadDim + 16 * mt + d0] = o[mt][1] * ib;
-                    out_base[ha * kHeadDim + 16 * mt + d0 + 8] = o[mt][2] * ia;
-                    out_base[(ha + 1) * kHeadDim + 16 * mt + d0 + 8] = o[mt][3] * ib;
+                    for (int mt = 0; mt < 8; ++mt) {
+                        ob[ha * kHeadDim + 16 * mt + d0] = o[mt][0] * ia;
+                        ob[(ha + 1) * kHeadDim + 16 * mt + d0] = o[mt][1] * ib;
+                        ob[ha * kHeadDim + 16 * mt + d0 + 8] = o[mt][2] * ia;
+                        ob[(ha + 1) * kHeadDim + 16 * mt + d0 + 8] = o[mt][3] * ib;
+                    }
                 }
             }
+            signal_arrival(xchg, layer, lane);
             return;
         }
         if (!lo_side) {
@@ -568,10 +596,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         ticket = __shfl_sync(0xffffffffu, ticket, 0);
         if (ticket == nparts - 1) {
             __threadfence();
-            merge_partials(part_o, part_ml, batch.part_off[eh], nparts, out_base, lane);
+            float4 res[kGqa];
+            merge_partials(part_o, part_ml, batch.part_off[eh], nparts, lane, res);
+            for (int r = 0; r < n_dst; ++r) {
+                float4 *ob = reinterpret_cast<float4 *>(out_slice(out, xchg, r, layer, seg_e, seg_h, G));
+#pragma unroll
+                for (int j = 0; j < kGqa; ++j) {
+                    ob[j * (kHeadDim / 4) + lane] = res[j];
+                }
+            }
             if (lane == 0) {
                 counters[eh] = 0;  // ready for the next launch
             }
+            signal_arrival(xchg, layer, lane);
         }
     };
 
@@ -840,8 +877,8 @@ template <bool kAppend>
 void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchView &batch,
                         int layer, const float *q, const float *k_new, const float *v_new,
                         float *part_o, float *part_ml, int32_t *counters, float *out,
-                        float scale_log2, DeviceError *err, bool overlap_previous,
-                        cudaStream_t stream) {
+                        const Exchange &xchg, float scale_log2, DeviceError *err,
+                        bool overlap_previous, cudaStream_t stream) {
     // The dynamic shared-memory opt-in is per device and per kernel.
     static bool configured[64] = {};
     int dev = 0;
@@ -865,20 +902,41 @@ void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchV
     cfg.attrs = attr;
     cfg.numAttrs = overlap_previous ? 1 : 0;
     cudaLaunchKernelEx(&cfg, attention_kernel<kAppend>, pool, rope, batch, layer, q, k_new, v_new,
-                       part_o, part_ml, counters, out, scale_log2, err);
+                       part_o, part_ml, counters, out, xchg, scale_log2, err);
 }
 
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
                       const float *q, const float *k_new, const float *v_new, float *part_o,
-                      float *part_ml, int32_t *counters, float *out, float scale_log2,
-                      DeviceError *err, bool overlap_previous, cudaStream_t stream) {
+                      float *part_ml, int32_t *counters, float *out, const Exchange &xchg,
+                      float scale_log2, DeviceError *err, bool overlap_previous,
+                      cudaStream_t stream) {
     if (k_new != nullptr && v_new != nullptr) {
         launch_attention_t<true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
-                                 counters, out, scale_log2, err, overlap_previous, stream);
+                                 counters, out, xchg, scale_log2, err, overlap_previous, stream);
     } else {
         launch_attention_t<false>(pool, rope, batch, layer, q, nullptr, nullptr, part_o, part_ml,
-                                  counters, out, scale_log2, err, overlap_previous, stream);
+                                  counters, out, xchg, scale_log2, err, overlap_previous, stream);
     }
+}
+
+// =================================================================== split wait
+__global__ void split_wait_kernel(const uint32_t *flag, uint32_t target, DeviceError *err) {
+    const long long t0 = clock64();
+    const volatile uint32_t *f = flag;
+    while (static_cast<int32_t>(*f - target) < 0) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            record_error(err, kErrTimeout, kWhereSplitWait, static_cast<int>(*f),
+                         static_cast<int>(target));
+            return;
+        }
+        __nanosleep(200);
+    }
+    __threadfence_system();
+}
+
+void launch_split_wait(const uint32_t *flag, uint32_t target, DeviceError *err,
+                       cudaStream_t stream) {
+    split_wait_kernel<<<1, 1, 0, stream>>>(flag, target, err);
 }
 
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,

@@ -193,8 +193,9 @@ extern "C" int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer
     rv.context_length = view->context_length;
     const float scale_log2 =
         (1.0f / std::sqrt(static_cast<float>(kHeadDim))) * 1.4426950408889634f;
+    const Exchange no_exchange{nullptr, nullptr, 0, 0, 0, 0};
     launch_attention(pv, rv, b, layer, q_prerope, nullptr, nullptr, part_o, part_ml, counters, out,
-                     scale_log2, err, /*overlap_previous=*/false, stream);
+                     no_exchange, scale_log2, err, /*overlap_previous=*/false, stream);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_msg(err_msg, err_len, "kernel launch: %s", cudaGetErrorString(e));

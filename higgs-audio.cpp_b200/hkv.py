@@ -133,6 +133,11 @@ SIGNATURES = {
     "hkv_rope_tables": ([_P, _P, _P], ctypes.c_int),
     "hkv_decode_attn_noalloc": ([ctypes.POINTER(PagedView), _I32, _I32, _I32P, _I32P, _I32P,
                                  _P, _P, _P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
+    "hkv_split_export": ([_P, _I32, _I32, _P], ctypes.c_int),
+    "hkv_split_connect": ([_P, _P], ctypes.c_int),
+    "hkv_split_step": ([_P, _I32, _I32, _I32P, _P, _P, _P, _P], ctypes.c_int),
+    "hkv_split_wait": ([_P, _I32, _P], ctypes.c_int),
+    "hkv_split_output": ([_P, _I32, ctypes.POINTER(_P), _I64P], ctypes.c_int),
     "hkv_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
     "hkv_profile_reset": ([_P], ctypes.c_int),
     "hkv_profile_read": ([_P, ctypes.c_int, _I64P, ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
@@ -348,6 +353,35 @@ class Engine:
         sin = np.empty_like(cos)
         self._check(self.lib.hkv_rope_tables(self.handle, cos.ctypes.data, sin.ctypes.data))
         return cos, sin
+
+    # ------------------------------------------------------- KV-head split
+    def split_export(self, world: int, rank: int) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        self._check(self.lib.hkv_split_export(self.handle, world, rank, buf))
+        return buf.raw
+
+    def split_connect(self, handles: Sequence[bytes]) -> None:
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        self._check(self.lib.hkv_split_connect(self.handle, buf))
+
+    def split_disconnect(self) -> None:
+        self._check(self.lib.hkv_split_connect(self.handle, None))
+
+    def split_step(self, layer: int, slots: Sequence[int], q, k, v, stream=None) -> None:
+        n, arr = _slots_arg(slots)
+        self._check(self.lib.hkv_split_step(self.handle, layer, n, arr, _ptr(q), _ptr(k), _ptr(v),
+                                            _stream(stream)))
+
+    def split_wait(self, layer: int, stream=None) -> None:
+        self._check(self.lib.hkv_split_wait(self.handle, layer, _stream(stream)))
+
+    def split_output(self, layer: int):
+        """(device pointer, floats per row) of this rank's full output of one layer."""
+        p = ctypes.c_void_p()
+        w = ctypes.c_int64()
+        self._check(self.lib.hkv_split_output(self.handle, layer, ctypes.byref(p), ctypes.byref(w)))
+        return p.value, w.value
 
     # ----------------------------------------------------------- profiling
     def profile_enable(self, on: bool = True) -> None:

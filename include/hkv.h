@@ -224,6 +224,44 @@ int hkv_sync_check(hkv_engine *eng, hkv_stream stream);
 /* Host copies of the BF16 RoPE tables, [context_length][head_dim/2] each. */
 int hkv_rope_tables(const hkv_engine *eng, float *cos_out, float *sin_out);
 
+/* ------------------------------------------------------ KV-head split -- */
+
+/* One long request split by KV head across `world` GPUs, one process and one
+ * engine per GPU, each engine holding n_head_kv = (total KV heads) / world of
+ * every layer.  The reference has no multi-GPU path (it runs on CUDA device 0,
+ * src/higgs_pipeline.cpp:126); this replaces an all-gather of the per-head
+ * attention outputs before o_proj with peer stores from inside the decode
+ * kernel: every finished head slice is written into every rank's exchange
+ * region over NVLink and each rank's per-layer arrival counter is bumped.
+ *
+ *   hkv_split_export   allocate this rank's exchange region (zeroed) and
+ *                      export its CUDA IPC handle (64 bytes) to handle_out
+ *   hkv_split_connect  map every peer's region from the world's handles
+ *                      (world x 64 bytes, rank order); all ranks must have
+ *                      exported before any rank runs hkv_split_step.  With
+ *                      handles == NULL it closes the peer mappings: every
+ *                      rank must do so (then meet at a barrier) before any
+ *                      rank destroys its engine, which frees its region
+ *   hkv_split_step     hkv_decode_step over this rank's KV heads (q, k, v hold
+ *                      this rank's heads), the outputs going to all ranks
+ *   hkv_split_wait     enqueue a bounded wait until every rank's slices of
+ *                      this layer's latest step have arrived here; after it,
+ *                      work on `stream` may read the output (a peer that
+ *                      never delivers ends the wait with HKV_ERR_TIMEOUT at
+ *                      the next hkv_sync_check)
+ *   hkv_split_output   this rank's full output of one layer, rows of
+ *                      row_floats F32 (one row per batch entry, heads in
+ *                      global order); each layer has its own block, so a rank
+ *                      running ahead never overwrites what a peer still reads
+ * Every rank must pass its entries in the same request order. */
+int hkv_split_export(hkv_engine *eng, int32_t world, int32_t rank, void *handle_out);
+int hkv_split_connect(hkv_engine *eng, const void *handles);
+int hkv_split_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
+                   const float *q_prerope, const float *k_prerope, const float *v,
+                   hkv_stream stream);
+int hkv_split_wait(hkv_engine *eng, int32_t layer, hkv_stream stream);
+int hkv_split_output(const hkv_engine *eng, int32_t layer, float **out_dev, int64_t *row_floats);
+
 /* ---------------------------------------------------- no allocation -- */
 
 /* Device memory a caller already owns, in the engine's page layout: one slab
