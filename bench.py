@@ -30,9 +30,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -79,52 +77,75 @@ def workload(name: str, rank: int):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed
+    region: NVML read-only queries from a thread every ~5 ms (the timed region
+    can be well under a second).  Nothing here changes a GPU setting."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": "HwSlowdown", "hw_thermal_slowdown": "HwThermalSlowdown",
+               "sw_thermal_slowdown": "SwThermalSlowdown", "sw_power_cap": "SwPowerCap"}
 
     def __init__(self, device: int):
         self.device = device
-        self.proc = None
-        self.file = None
+        self.samples = []
+        self.thread = None
+        self.stop_flag = False
+        self.handle = None
+        self.max_mhz = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+        for cand in (uuid, "GPU-" + uuid):
+            try:
+                return pynvml.nvmlDeviceGetHandleByUUID(cand)
+            except Exception:
+                pass
+        return pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def start(self):
+        import threading
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.file, stderr=subprocess.DEVNULL)
+            import pynvml
+            self.handle = self._nvml_handle()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
+            self.handle = None
+            return
+        masks = {}
+        for key, name in self.REASONS.items():
+            masks[key] = getattr(pynvml, "nvmlClocksEventReason" + name,
+                                 getattr(pynvml, "nvmlClocksThrottleReason" + name, 0))
+
+        def loop():
+            import time as _t
+            while not self.stop_flag:
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+                    try:
+                        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                    except Exception:
+                        bits = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                    self.samples.append((mhz, [k for k, m in masks.items() if bits & m]))
+                except Exception:
+                    break
+                _t.sleep(0.005)
+
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.file.flush()
-        rows = []
-        with open(self.file.name) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        os.unlink(self.file.name)
-        if not rows:
+        self.stop_flag = True
+        self.thread.join(timeout=5)
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        mhz = [m for m, _ in self.samples]
+        reasons = sorted({r for _, rs in self.samples for r in rs})
+        return {"sm_mhz": float(np.median(mhz)), "sm_max_mhz": float(self.max_mhz),
+                "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
 
 
 # ----------------------------------------------------------- CPU baseline
