@@ -570,9 +570,9 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
     HKV_CUDA_TRY(eng, eng->batch_stage.begin(words * sizeof(int32_t), &host));
     const PlanSummary plan =
         build_plan(static_cast<int32_t *>(host), n, G, pos.data(), lists.data(), total_pages, W);
-    if (plan.n_parts > eng->part_cap) {
-        return fail(eng, HKV_ERR_OOM, "split plan needs %d partials, capacity %lld", plan.n_parts,
-                    static_cast<long long>(eng->part_cap));
+    if (static_cast<int64_t>(plan.n_parts) + plan.n_groups > eng->part_cap) {
+        return fail(eng, HKV_ERR_OOM, "split plan needs %d partials, capacity %lld",
+                    plan.n_parts + plan.n_groups, static_cast<long long>(eng->part_cap));
     }
     void *dev = nullptr;
     ++eng->enqueue_seq;
@@ -813,14 +813,18 @@ int hkv_engine_create(const hkv_config *cfg, hkv_engine **out) {
         if (e == cudaSuccess) e = cudaMemset(eng->d_err, 0, sizeof(DeviceError));
         if (e != cudaSuccess) return fail_create(e, "error word");
         // Worst case partial count: one per active warp plus one extra per
-        // (entry, KV head) share boundary.
-        eng->part_cap = static_cast<int64_t>(eng->num_sms) * kAttnWarps +
-                        static_cast<int64_t>(cfg->max_slots) * cfg->n_head_kv;
+        // (entry, KV head) share boundary, then the group partials of the
+        // two-level merge (at most one per kMergeGroup partials, rounded up).
+        const int64_t segs = static_cast<int64_t>(cfg->max_slots) * cfg->n_head_kv;
+        const int64_t level1 = static_cast<int64_t>(eng->num_sms) * kAttnWarps + segs;
+        const int64_t groups = level1 / kMergeGroup + segs;
+        eng->part_cap = level1 + groups;
         e = cudaMalloc(&eng->part_o, static_cast<size_t>(eng->part_cap) * kGqa * kHeadDim * 4);
         if (e == cudaSuccess)
             e = cudaMalloc(&eng->part_ml, static_cast<size_t>(eng->part_cap) * 2 * kGqa * 4);
         if (e != cudaSuccess) return fail_create(e, "split partials");
-        const size_t counter_bytes = static_cast<size_t>(cfg->max_slots) * cfg->n_head_kv * 4;
+        // segment counters, then group counters
+        const size_t counter_bytes = static_cast<size_t>(segs + groups) * 4;
         e = cudaMalloc(&eng->counters, counter_bytes);
         if (e == cudaSuccess) e = cudaMemset(eng->counters, 0, counter_bytes);
         if (e != cudaSuccess) return fail_create(e, "merge counters");

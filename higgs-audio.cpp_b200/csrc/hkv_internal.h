@@ -54,6 +54,7 @@ struct BatchView {
     const int32_t *page_off;  // [n+1] prefix sum of npages into pages[]
     const int32_t *unit_off;  // [n+1] prefix sum of npages * n_head_kv
     const int32_t *part_off;  // [n*n_head_kv + 1] first partial of each (entry, kv head)
+    const int32_t *part2_off; // [n*n_head_kv + 1] first group partial / group counter of each
     const int4 *warp_start;   // [n_warps][2] per warp: {entry, kv head, page index, pages of
                               // the entry}, {page_off[entry], first three physical pages}
     const int32_t *pages;     // [page_off[n]] physical pages, entry-major
@@ -62,6 +63,10 @@ struct BatchView {
     int32_t n_warps;          // warps the units are shared among (grid * kAttnWarps)
     int32_t n_parts;
 };
+
+// Partials of one (entry, KV head) are merged in groups of this many (two
+// levels when a segment has more), so no single warp merges a long list.
+constexpr int kMergeGroup = 8;
 
 struct PoolView {
     uint8_t *base;

@@ -341,8 +341,17 @@ __device__ __forceinline__ uint4 new_row_chunk(const RopeView &rope, const float
 // Lane p holds the (m, l) of partial p (loaded in parallel, reduced by
 // shuffles); the partial outputs are then streamed with the weights
 // broadcast from their owner lane, several partials in flight at a time.
+// Result of a merge before normalisation: o = sum_p w_p o_p, l = sum_p w_p l_p
+// with w_p = 2^(m_p - m); the final output is o / l, a group partial keeps
+// (o, m, l) as is.
+struct Merged {
+    float4 o[kGqa];  // this lane's 4 dims of each head
+    float m[kGqa];
+    float l[kGqa];
+};
+
 __device__ __forceinline__ void merge_partials(const float *part_o, const float *part_ml, int p0,
-                                               int nparts, int lane, float4 (&res)[kGqa]) {
+                                               int nparts, int lane, Merged &res) {
     float mx[kGqa];
 #pragma unroll
     for (int j = 0; j < kGqa; ++j) {
@@ -413,9 +422,15 @@ __device__ __forceinline__ void merge_partials(const float *part_o, const float 
     }
 #pragma unroll
     for (int j = 0; j < kGqa; ++j) {
-        const float inv = 1.f / den[j];
-        res[j] = make_float4(acc[j].x * inv, acc[j].y * inv, acc[j].z * inv, acc[j].w * inv);
+        res.o[j] = acc[j];
+        res.m[j] = mx[j];
+        res.l[j] = den[j];
     }
+}
+
+__device__ __forceinline__ float4 normalised(const Merged &r, int j) {
+    const float inv = 1.f / r.l[j];
+    return make_float4(r.o[j].x * inv, r.o[j].y * inv, r.o[j].z * inv, r.o[j].w * inv);
 }
 
 // Destination of the 4 x 128 output floats of (entry e, KV head h).
@@ -585,30 +600,86 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 pm[ha * 2 + 3] = l_b;
             }
         }
-        // Publish the partial; the warp that brings the count to nparts merges.
+        // Publish the partial; the last of a group of kMergeGroup partials
+        // merges the group, and the last group (or the only one) produces
+        // the output.
         __threadfence();
         __syncwarp();
-        int ticket = 0;
         const int eh = seg_e * G + seg_h;
-        if (lane == 0) {
-            ticket = atomicAdd(counters + eh, 1);
-        }
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket == nparts - 1) {
-            __threadfence();
-            float4 res[kGqa];
-            merge_partials(part_o, part_ml, batch.part_off[eh], nparts, lane, res);
+        const int p_first = batch.part_off[eh];
+        const int j_part = part - p_first;
+        const int n_groups = nparts > kMergeGroup ? (nparts + kMergeGroup - 1) / kMergeGroup : 0;
+        const int n_seg = batch.n * G;  // segment counters come first, then group counters
+        auto finish = [&](const Merged &res) {
             for (int r = 0; r < n_dst; ++r) {
                 float4 *ob = reinterpret_cast<float4 *>(out_slice(out, xchg, r, layer, seg_e, seg_h, G));
 #pragma unroll
                 for (int j = 0; j < kGqa; ++j) {
-                    ob[j * (kHeadDim / 4) + lane] = res[j];
+                    ob[j * (kHeadDim / 4) + lane] = normalised(res, j);
                 }
             }
             if (lane == 0) {
                 counters[eh] = 0;  // ready for the next launch
             }
             signal_arrival(xchg, layer, lane);
+        };
+        if (n_groups == 0) {
+            int ticket = 0;
+            if (lane == 0) {
+                ticket = atomicAdd(counters + eh, 1);
+            }
+            ticket = __shfl_sync(0xffffffffu, ticket, 0);
+            if (ticket == nparts - 1) {
+                __threadfence();
+                Merged res;
+                merge_partials(part_o, part_ml, p_first, nparts, lane, res);
+                finish(res);
+            }
+            return;
+        }
+        const int g = j_part / kMergeGroup;
+        const int g_size = min(kMergeGroup, nparts - g * kMergeGroup);
+        const int g_index = batch.part2_off[eh] + g;
+        int ticket = 0;
+        if (lane == 0) {
+            ticket = atomicAdd(counters + n_seg + g_index, 1);
+        }
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        if (ticket != g_size - 1) {
+            return;
+        }
+        __threadfence();
+        Merged grp;
+        merge_partials(part_o, part_ml, p_first + g * kMergeGroup, g_size, lane, grp);
+        {
+            // the group partial, stored after the level-1 partials
+            const int gp = batch.n_parts + g_index;
+            float4 *po = reinterpret_cast<float4 *>(part_o + static_cast<int64_t>(gp) * (kGqa * kHeadDim));
+#pragma unroll
+            for (int j = 0; j < kGqa; ++j) {
+                po[j * (kHeadDim / 4) + lane] = grp.o[j];
+            }
+            if (lane == 0) {
+                float *pm = part_ml + static_cast<int64_t>(gp) * (2 * kGqa);
+#pragma unroll
+                for (int j = 0; j < kGqa; ++j) {
+                    pm[2 * j] = grp.m[j];
+                    pm[2 * j + 1] = grp.l[j];
+                }
+                counters[n_seg + g_index] = 0;
+            }
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) {
+            ticket = atomicAdd(counters + eh, 1);
+        }
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        if (ticket == n_groups - 1) {
+            __threadfence();
+            Merged res;
+            merge_partials(part_o, part_ml, batch.n_parts + batch.part2_off[eh], n_groups, lane, res);
+            finish(res);
         }
     };
 

@@ -153,17 +153,19 @@ extern "C" int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer
 
     // ---- carve the static scratch:
     //      [error word][merge counters][descriptor][partials o][partials m, l]
+    // segment counters then group counters; level-1 then group partials
+    const size_t n_counters = static_cast<size_t>(n) * G + plan.n_groups;
+    const size_t n_partials = static_cast<size_t>(plan.n_parts) + plan.n_groups;
     const size_t cnt_off = align256(sizeof(DeviceError));
-    const size_t desc_off = align256(cnt_off + static_cast<size_t>(n) * G * sizeof(int32_t));
+    const size_t desc_off = align256(cnt_off + n_counters * sizeof(int32_t));
     const size_t po_off = align256(desc_off + words * sizeof(int32_t));
-    const size_t pml_off =
-        align256(po_off + static_cast<size_t>(plan.n_parts) * kGqa * kHeadDim * sizeof(float));
-    const size_t need = pml_off + static_cast<size_t>(plan.n_parts) * 2 * kGqa * sizeof(float);
+    const size_t pml_off = align256(po_off + n_partials * kGqa * kHeadDim * sizeof(float));
+    const size_t need = pml_off + n_partials * 2 * kGqa * sizeof(float);
     if (need > kNoAllocScratchBytes) {
         set_msg(err_msg, err_len,
-                "batch needs %zu bytes of scratch (%d partials, %zu descriptor words); the "
+                "batch needs %zu bytes of scratch (%zu partials, %zu descriptor words); the "
                 "static scratch holds %zu bytes: split the batch",
-                need, plan.n_parts, words, kNoAllocScratchBytes);
+                need, n_partials, words, kNoAllocScratchBytes);
         return HKV_ERR_RANGE;
     }
     DeviceError *err = reinterpret_cast<DeviceError *>(scratch);

@@ -10,12 +10,19 @@
 // Each (entry, KV head) segment [a, a + np) is covered by warps
 // warp_of(a) .. warp_of(a + np - 1), one partial result each.
 //
+// A segment with more than kMergeGroup partials is merged in two levels:
+// groups of kMergeGroup partials are merged by the last warp of each group
+// into one "group partial", and the last group merges the group partials.
+// part2_off gives each such segment's first group partial (stored after the
+// n_parts partials) and its first group counter (after the n*G segment
+// counters).
+//
 // Device descriptor (int32 words, uploaded in one copy):
 //   warp_start[W][8]  per warp {entry, kv head, page index, pages of the entry}
 //                     {page_off[entry], physical pages of its first 3 units}
 //                     (first, so each record is 16-byte aligned)
 //   pos[n] ntok[n] npages[n] page_off[n+1] unit_off[n+1] part_off[n*G+1]
-//   pages[total_pages]
+//   part2_off[n*G+1] pages[total_pages]
 #pragma once
 
 #include <stdint.h>
@@ -37,15 +44,20 @@ inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
 
 constexpr int kWarpStartWords = 8;
 
+inline int32_t plan_groups(int32_t nparts) {
+    return nparts > kMergeGroup ? (nparts + kMergeGroup - 1) / kMergeGroup : 0;
+}
+
 inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
-    return static_cast<size_t>(kWarpStartWords * W + 3 * n + 2 * (n + 1) + (n * G + 1) +
+    return static_cast<size_t>(kWarpStartWords * W + 3 * n + 2 * (n + 1) + 2 * (n * G + 1) +
                                total_pages);
 }
 
 struct PlanSummary {
     int64_t total_pages = 0;
     int64_t total_units = 0;
-    int32_t n_parts = 0;
+    int32_t n_parts = 0;   // level-1 partials
+    int32_t n_groups = 0;  // group partials (and group counters)
 };
 
 // Fills `w` (plan_words(...) words, 16-byte aligned).  page_lists[e] points
@@ -63,8 +75,9 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
     int32_t *page_off = npg + n;
     int32_t *unit_off = page_off + (n + 1);
     int32_t *part_off = unit_off + (n + 1);
-    int32_t *pages = part_off + (n * G + 1);
-    page_off[0] = unit_off[0] = part_off[0] = 0;
+    int32_t *part2_off = part_off + (n * G + 1);
+    int32_t *pages = part2_off + (n * G + 1);
+    page_off[0] = unit_off[0] = part_off[0] = part2_off[0] = 0;
     for (int32_t e = 0; e < n; ++e) {
         const int32_t np = pos_in[e] / kPageTokens + 1;
         pos[e] = pos_in[e];
@@ -77,6 +90,8 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
             const int64_t a = unit_off[e] + static_cast<int64_t>(h) * np;
             const int64_t parts = plan_warp_of(a + np - 1, U, W) - plan_warp_of(a, U, W) + 1;
             part_off[e * G + h + 1] = part_off[e * G + h] + static_cast<int32_t>(parts);
+            part2_off[e * G + h + 1] =
+                part2_off[e * G + h] + plan_groups(static_cast<int32_t>(parts));
         }
     }
     int32_t e = 0;
@@ -112,6 +127,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         }
     }
     s.n_parts = part_off[n * G];
+    s.n_groups = part2_off[n * G];
     return s;
 }
 
@@ -126,7 +142,8 @@ inline BatchView bind_plan(const int32_t *d, int32_t n, int32_t G, const PlanSum
     b.page_off = b.npages + n;
     b.unit_off = b.page_off + (n + 1);
     b.part_off = b.unit_off + (n + 1);
-    b.pages = b.part_off + (n * G + 1);
+    b.part2_off = b.part_off + (n * G + 1);
+    b.pages = b.part2_off + (n * G + 1);
     b.n = n;
     b.total_units = static_cast<int32_t>(s.total_units);
     b.n_warps = W;

@@ -1,5 +1,9 @@
 """Invariants of the stream-K plan (higgs-audio.cpp_b200/csrc/hkv_plan.h), CPU.
 
+Also walks the two-level merge: a segment with more than 8 partials is
+merged in groups of 8 by the last warp of each group, and the last group
+merges the group partials; every segment must finish exactly once.
+
 Restates the plan's formulas -- W = min(U, grid warps) equal shares
 floor(w U / W) .. floor((w + 1) U / W), warp_of(a) = ceil((a + 1) W / U) - 1,
 part_off from the warps a (slot, KV head) segment touches, warp_entry -- and
@@ -38,10 +42,17 @@ def plan(npages, G, w_full):
     return unit_off, part_off, warp_entry, U, W, warp_of
 
 
-def walk(npages, G=8, w_full=148 * 8):
+GROUP = 8
+
+
+def walk(npages, G=8, w_full=148 * 6):
     unit_off, part_off, warp_entry, U, W, warp_of = plan(npages, G, w_full)
     assert part_off[-1] <= W + len(npages) * G  # the engine's partial capacity
+    n_groups = [(part_off[i + 1] - part_off[i] + GROUP - 1) // GROUP
+                if part_off[i + 1] - part_off[i] > GROUP else 0 for i in range(len(npages) * G)]
+    assert sum(n_groups) <= (W + len(npages) * G) // GROUP + len(npages) * G
     written, tickets, merges, direct = {}, {}, {}, {}
+    group_tickets, group_merges = {}, {}
     for gw in range(W):
         ub, ue = gw * U // W, (gw + 1) * U // W
         assert ub < ue, "empty share"
@@ -59,9 +70,22 @@ def walk(npages, G=8, w_full=148 * 8):
                 return
             assert part_off[eh] <= part < part_off[eh + 1]
             written[part] = written.get(part, 0) + 1
+            if nparts <= GROUP:
+                t = tickets.get(eh, 0)
+                tickets[eh] = t + 1
+                if t == nparts - 1:
+                    merges[eh] = merges.get(eh, 0) + 1
+                return
+            g = (part - part_off[eh]) // GROUP
+            g_size = min(GROUP, nparts - g * GROUP)
+            t = group_tickets.get((eh, g), 0)
+            group_tickets[(eh, g)] = t + 1
+            if t != g_size - 1:
+                return
+            group_merges[(eh, g)] = group_merges.get((eh, g), 0) + 1
             t = tickets.get(eh, 0)
             tickets[eh] = t + 1
-            if t == nparts - 1:
+            if t == (nparts + GROUP - 1) // GROUP - 1:
                 merges[eh] = merges.get(eh, 0) + 1
 
         for u in range(ub, ue):
@@ -86,10 +110,12 @@ def walk(npages, G=8, w_full=148 * 8):
             assert merges.get(eh) == 1
             for p in range(part_off[eh], part_off[eh + 1]):
                 assert written.get(p) == 1
+            for g in range(n_groups[eh]):
+                assert group_merges.get((eh, g)) == 1
 
 
 @pytest.mark.parametrize("npages", [[3, 1], [1] * 4, [1] * 300, [3, 19, 63], [2048],
-                                    [1, 1000, 1, 1000]])
+                                    [1, 1000, 1, 1000], [40], [33, 2048]])
 def test_plan_partitions_every_segment(npages):
     walk(npages)
 
