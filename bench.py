@@ -1,7 +1,7 @@
 """Decode-attention + KV-append throughput of the paged KV engine.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload scaleout|batched16|headsplit]
+                    [--workload scaleout|batched16|churn|headsplit]
 
 One process per GPU (torchrun for N > 1).  A step is one decode step of every
 slot on the rank: for each of the 36 layers, the RoPE + K/V append of one row
@@ -13,6 +13,8 @@ Workloads (synthetic N(0,1) data, random physical page order):
              32 slots per GPU, contexts uniform in [2048, 16384] (seeded per
              rank), so N GPUs run 32N slots (weak scaling, no collective).
   batched16  16 slots, contexts uniform in [256, 4096], one GPU.
+  churn      64 slots in 8 groups sharing a 768-token prefix (copy-on-write);
+             slots finish with p=0.01 per step and are replaced at once.
   headsplit  one request near the 32768-position context, split by KV head
              over the N GPUs with an NCCL all-gather per layer.
 
@@ -65,6 +67,11 @@ def workload(name: str, rank: int):
         lens = [32768 - 16]
         desc = ("one request near the 32768-position context, split by KV head, 36 layers, "
                 "F16 KV in 16-token pages")
+    elif name == "churn":
+        n = 64
+        lens = synth.uniform_int(3000 + rank, n, 769, 8192)
+        desc = ("slot churn with prefix sharing: 64 slots in 8 groups sharing a 768-token "
+                "prefix, contexts U[769, 8192], 36 layers")
     elif name == "batched16":
         n = 16
         lens = synth.uniform_int(2000 + rank, n, 256, 4096)
@@ -238,19 +245,58 @@ def bench_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
-    lens, desc = workload(args.workload, rank)
-    n = len(lens)
-    total_steps = args.warmup + args.steps + args.e2e_steps + 2
-    n_pages = sum((L + total_steps + 15) // 16 + 1 for L in lens) + 16
+    total_steps = args.warmup + args.steps + args.e2e_steps + 4
     dev = f"cuda:{local}"
-    eng = hkv.Engine(n_layers=N_LAYERS, n_pages=n_pages, max_slots=n, device=local,
-                     shuffle_seed=0x5EED + rank)
     stream = torch.cuda.Stream(device=local)
     sh = stream.cuda_stream
-    slots = [eng.acquire(L + total_steps) for L in lens]
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
-    prefill(eng, slots, lens, stream, gen, dev)
+    churn = None
+    if args.workload == "churn":
+        # 64 slots in 8 groups; each group shares a published reference-prompt
+        # prefix (copy-on-write pages); slots finish with probability 0.01 per
+        # step and are replaced by fresh prefix-only slots of the same group.
+        import synth
+        n, group, prefix = 64, 8, args.prefix
+        lens = [int(x) for x in synth.uniform_int(3000 + rank, n, prefix + 1, 8192)]
+        desc = (f"slot churn with prefix sharing: 64 slots in 8 groups sharing a {prefix}-token "
+                "prefix (copy-on-write pages), contexts U[prefix+1, 8192], each slot finishes "
+                "with p=0.01 per step and is replaced at once, 36 layers, F16 KV")
+        prefix_pages = (prefix + 15) // 16
+        n_pages = (sum((L - prefix + total_steps + 15) // 16 + 2 for L in lens)
+                   + (n // group) * prefix_pages + n * ((total_steps + 15) // 16 + 2) + 64)
+        eng = hkv.Engine(n_layers=N_LAYERS, n_pages=n_pages, max_slots=n + 1, device=local,
+                         shuffle_seed=0x5EED + rank)
+        for g in range(n // group):
+            owner = eng.acquire(prefix)
+            prefill(eng, [owner], [prefix], stream, gen, dev)
+            eng.publish(g + 1, prefix, owner)
+            eng.release(owner)  # the published prefix keeps its pages
+        slots = []
+        for i, L in enumerate(lens):
+            s_ = eng.acquire(L + total_steps, share=(i // group + 1, prefix))
+            prefill(eng, [s_], [L - prefix], stream, gen, dev)
+            slots.append(s_)
+        cur_len = list(lens)
+        rng = np.random.default_rng(4242 + rank)
+        churn_stats = {"replaced": 0}
+
+        def churn():
+            for i in range(n):
+                if rng.random() < 0.01:
+                    eng.release(slots[i])
+                    slots[i] = eng.acquire(prefix + total_steps, share=(i // group + 1, prefix))
+                    cur_len[i] = prefix
+                    churn_stats["replaced"] += 1
+    else:
+        lens, desc = workload(args.workload, rank)
+        n = len(lens)
+        n_pages = sum((L + total_steps + 15) // 16 + 1 for L in lens) + 16
+        eng = hkv.Engine(n_layers=N_LAYERS, n_pages=n_pages, max_slots=n, device=local,
+                         shuffle_seed=0x5EED + rank)
+        slots = [eng.acquire(L + total_steps) for L in lens]
+        prefill(eng, slots, lens, stream, gen, dev)
+        cur_len = list(lens)
 
     # Step inputs, resident in HBM: q [36][n][32][128], k/v [36][n][8][128] F32.
     q = torch.randn((N_LAYERS, n, H, D), generator=gen, device=dev)
@@ -258,10 +304,17 @@ def bench_ours(args):
     v = torch.randn((N_LAYERS, n, G, D), generator=gen, device=dev)
     out = torch.empty((N_LAYERS, n, H * D), device=dev)
 
+    rows_seen = [0]  # rows attended, summed over decode steps (algorithmic bytes)
+
     def step():
+        rows_seen[0] += sum(L + 1 for L in cur_len)
         for layer in range(N_LAYERS):
             eng.decode_step(layer, slots, q[layer], k[layer], v[layer], out[layer], sh)
         eng.advance(slots, 1)
+        for i in range(n):
+            cur_len[i] += 1
+        if churn is not None:
+            churn()
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -270,7 +323,8 @@ def bench_ours(args):
     eng.sync_check(sh)
 
     # ---------------- device-timed region (inputs resident)
-    ctx_before = [eng.length(s) + 1 for s in slots]  # rows attended in the first timed step
+    stats_before = eng.stats()
+    rows_seen[0] = 0
     clocks = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()
@@ -291,6 +345,8 @@ def bench_ours(args):
     barrier()
     clk = clocks.stop()
     ms_local = ev0.elapsed_time(ev1)
+    rows = rows_seen[0]
+    stats_after = eng.stats()
     eng.sync_check(sh)
     # Kernel-only time from the engine's event profiler on two extra steps.
     eng.profile_reset()
@@ -308,7 +364,6 @@ def bench_ours(args):
     # 4096 L (K+V F16 read) + 4096 (new row write) + 8192 (k, v in) + 16384
     # (q in) + 16384 (out) = 4096 L + 45056, all of it moved by the one fused
     # kernel launch of the layer.
-    rows = sum(L + s for L in ctx_before for s in range(args.steps))
     step_bytes_local = N_LAYERS * (4096 * rows + 45056 * n * args.steps) / args.steps
     launch_bytes = step_bytes_local / N_LAYERS
     tokens_total = sum_over_ranks(n * args.steps)
@@ -353,6 +408,10 @@ def bench_ours(args):
                     d2h.wait_event(out_ev[layer])
                     hout[layer].copy_(out[layer], non_blocking=True)
             eng.advance(slots, 1)
+            for i in range(n):
+                cur_len[i] += 1
+            if churn is not None:
+                churn()
             stream.wait_stream(d2h)
             h2d.wait_stream(stream)  # next step's inputs overwrite dq/dk/dv
 
@@ -425,6 +484,9 @@ def bench_ours(args):
                 "kernel_only_ms_profiled": kernel_only_ms,
             },
             "gpu_launches": N_LAYERS * args.steps,
+            "pool": {"cow_copies_timed": stats_after["cow_copies"] - stats_before["cow_copies"],
+                     "shared_pages": stats_after["shared_pages"],
+                     "replaced_slots": (churn_stats["replaced"] if churn is not None else 0)},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,
@@ -551,7 +613,10 @@ def bench_headsplit(args):
                        "parallelism": f"KV-head split x{world}"},
             "hbm": {"step_gbs_per_gpu": gbs, "peak_gbs": peak, "frac": gbs / peak,
                     "peak_kind": peak_kind},
-            "gpu_launches": N_LAYERS * args.steps, "e2e": None,
+            "gpu_launches": N_LAYERS * args.steps,
+            "pool": {"cow_copies_timed": stats_after["cow_copies"] - stats_before["cow_copies"],
+                     "shared_pages": stats_after["shared_pages"],
+                     "replaced_slots": (churn_stats["replaced"] if churn is not None else 0)}, "e2e": None,
         }), flush=True)
     if p2p:
         dist.barrier()
@@ -611,6 +676,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="scaleout")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefix", type=int, default=768,
+                    help="churn: shared prefix length (770 puts the first append of every "
+                         "replacement slot into a shared partial page: copy-on-write)")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
                     help="headsplit: how the per-head outputs reach every rank")
     ap.add_argument("--layers", type=int, default=36,

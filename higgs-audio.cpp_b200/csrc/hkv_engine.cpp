@@ -814,10 +814,10 @@ int hkv_engine_create(const hkv_config *cfg, hkv_engine **out) {
         if (e != cudaSuccess) return fail_create(e, "error word");
         // Worst case partial count: one per active warp plus one extra per
         // (entry, KV head) share boundary, then the group partials of the
-        // two-level merge (at most one per kMergeGroup partials, rounded up).
+        // two-level merge (at most one per 8 partials, rounded up).
         const int64_t segs = static_cast<int64_t>(cfg->max_slots) * cfg->n_head_kv;
         const int64_t level1 = static_cast<int64_t>(eng->num_sms) * kAttnWarps + segs;
-        const int64_t groups = level1 / kMergeGroup + segs;
+        const int64_t groups = level1 / 8 + segs;
         eng->part_cap = level1 + groups;
         e = cudaMalloc(&eng->part_o, static_cast<size_t>(eng->part_cap) * kGqa * kHeadDim * 4);
         if (e == cudaSuccess)

@@ -64,9 +64,25 @@ struct BatchView {
     int32_t n_parts;
 };
 
-// Partials of one (entry, KV head) are merged in groups of this many (two
-// levels when a segment has more), so no single warp merges a long list.
-constexpr int kMergeGroup = 8;
+// Partials of one (entry, KV head) are merged by one warp when there are at
+// most kMergeSingleMax of them; beyond that in two levels: groups of
+// merge_group_size(n) partials, then the group results, so no single warp
+// merges a long list.  Host plan and kernel share this function.
+constexpr int kMergeSingleMax = 16;
+__host__ __device__ inline int merge_group_size(int nparts) {
+    int g = 8;
+    while (g * g < nparts) {
+        ++g;
+    }
+    return g;  // max(8, ceil(sqrt(nparts)))
+}
+__host__ __device__ inline int merge_groups(int nparts) {
+    if (nparts <= kMergeSingleMax) {
+        return 0;
+    }
+    const int g = merge_group_size(nparts);
+    return (nparts + g - 1) / g;
+}
 
 struct PoolView {
     uint8_t *base;

@@ -600,15 +600,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 pm[ha * 2 + 3] = l_b;
             }
         }
-        // Publish the partial; the last of a group of kMergeGroup partials
-        // merges the group, and the last group (or the only one) produces
-        // the output.
+        // Publish the partial; the last of a group of partials merges the
+        // group, and the last group (or the only one) produces the output.
         __threadfence();
         __syncwarp();
         const int eh = seg_e * G + seg_h;
         const int p_first = batch.part_off[eh];
         const int j_part = part - p_first;
-        const int n_groups = nparts > kMergeGroup ? (nparts + kMergeGroup - 1) / kMergeGroup : 0;
+        const int n_groups = merge_groups(nparts);
         const int n_seg = batch.n * G;  // segment counters come first, then group counters
         auto finish = [&](const Merged &res) {
             for (int r = 0; r < n_dst; ++r) {
@@ -637,8 +636,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             }
             return;
         }
-        const int g = j_part / kMergeGroup;
-        const int g_size = min(kMergeGroup, nparts - g * kMergeGroup);
+        const int gsz = merge_group_size(nparts);
+        const int g = j_part / gsz;
+        const int g_size = min(gsz, nparts - g * gsz);
         const int g_index = batch.part2_off[eh] + g;
         int ticket = 0;
         if (lane == 0) {
@@ -650,7 +650,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
         __threadfence();
         Merged grp;
-        merge_partials(part_o, part_ml, p_first + g * kMergeGroup, g_size, lane, grp);
+        merge_partials(part_o, part_ml, p_first + g * gsz, g_size, lane, grp);
         {
             // the group partial, stored after the level-1 partials
             const int gp = batch.n_parts + g_index;

@@ -10,9 +10,9 @@
 // Each (entry, KV head) segment [a, a + np) is covered by warps
 // warp_of(a) .. warp_of(a + np - 1), one partial result each.
 //
-// A segment with more than kMergeGroup partials is merged in two levels:
-// groups of kMergeGroup partials are merged by the last warp of each group
-// into one "group partial", and the last group merges the group partials.
+// A segment with more than kMergeSingleMax partials is merged in two levels:
+// groups of merge_group_size() partials are merged by the last warp of each
+// group into one "group partial", and the last group merges those.
 // part2_off gives each such segment's first group partial (stored after the
 // n_parts partials) and its first group counter (after the n*G segment
 // counters).
@@ -43,10 +43,6 @@ inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
 }
 
 constexpr int kWarpStartWords = 8;
-
-inline int32_t plan_groups(int32_t nparts) {
-    return nparts > kMergeGroup ? (nparts + kMergeGroup - 1) / kMergeGroup : 0;
-}
 
 inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
     return static_cast<size_t>(kWarpStartWords * W + 3 * n + 2 * (n + 1) + 2 * (n * G + 1) +
@@ -91,7 +87,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
             const int64_t parts = plan_warp_of(a + np - 1, U, W) - plan_warp_of(a, U, W) + 1;
             part_off[e * G + h + 1] = part_off[e * G + h] + static_cast<int32_t>(parts);
             part2_off[e * G + h + 1] =
-                part2_off[e * G + h] + plan_groups(static_cast<int32_t>(parts));
+                part2_off[e * G + h] + merge_groups(static_cast<int32_t>(parts));
         }
     }
     int32_t e = 0;

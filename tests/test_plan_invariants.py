@@ -1,8 +1,9 @@
 """Invariants of the stream-K plan (higgs-audio.cpp_b200/csrc/hkv_plan.h), CPU.
 
-Also walks the two-level merge: a segment with more than 8 partials is
-merged in groups of 8 by the last warp of each group, and the last group
-merges the group partials; every segment must finish exactly once.
+Also walks the two-level merge: a segment with more than 16 partials is
+merged in groups of max(8, ceil(sqrt(n))) by the last warp of each group,
+and the last group merges the group partials; every segment must finish
+exactly once.
 
 Restates the plan's formulas -- W = min(U, grid warps) equal shares
 floor(w U / W) .. floor((w + 1) U / W), warp_of(a) = ceil((a + 1) W / U) - 1,
@@ -42,15 +43,25 @@ def plan(npages, G, w_full):
     return unit_off, part_off, warp_entry, U, W, warp_of
 
 
-GROUP = 8
+SINGLE_MAX = 16
+
+
+def group_size(nparts):  # max(8, ceil(sqrt(nparts))), as merge_group_size
+    g = 8
+    while g * g < nparts:
+        g += 1
+    return g
+
+
+def n_groups_of(nparts):
+    return 0 if nparts <= SINGLE_MAX else -(-nparts // group_size(nparts))
 
 
 def walk(npages, G=8, w_full=148 * 6):
     unit_off, part_off, warp_entry, U, W, warp_of = plan(npages, G, w_full)
     assert part_off[-1] <= W + len(npages) * G  # the engine's partial capacity
-    n_groups = [(part_off[i + 1] - part_off[i] + GROUP - 1) // GROUP
-                if part_off[i + 1] - part_off[i] > GROUP else 0 for i in range(len(npages) * G)]
-    assert sum(n_groups) <= (W + len(npages) * G) // GROUP + len(npages) * G
+    n_groups = [n_groups_of(part_off[i + 1] - part_off[i]) for i in range(len(npages) * G)]
+    assert sum(n_groups) <= (W + len(npages) * G) // 8 + len(npages) * G
     written, tickets, merges, direct = {}, {}, {}, {}
     group_tickets, group_merges = {}, {}
     for gw in range(W):
@@ -70,14 +81,15 @@ def walk(npages, G=8, w_full=148 * 6):
                 return
             assert part_off[eh] <= part < part_off[eh + 1]
             written[part] = written.get(part, 0) + 1
-            if nparts <= GROUP:
+            if nparts <= SINGLE_MAX:
                 t = tickets.get(eh, 0)
                 tickets[eh] = t + 1
                 if t == nparts - 1:
                     merges[eh] = merges.get(eh, 0) + 1
                 return
-            g = (part - part_off[eh]) // GROUP
-            g_size = min(GROUP, nparts - g * GROUP)
+            gs = group_size(nparts)
+            g = (part - part_off[eh]) // gs
+            g_size = min(gs, nparts - g * gs)
             t = group_tickets.get((eh, g), 0)
             group_tickets[(eh, g)] = t + 1
             if t != g_size - 1:
@@ -85,7 +97,7 @@ def walk(npages, G=8, w_full=148 * 6):
             group_merges[(eh, g)] = group_merges.get((eh, g), 0) + 1
             t = tickets.get(eh, 0)
             tickets[eh] = t + 1
-            if t == (nparts + GROUP - 1) // GROUP - 1:
+            if t == n_groups_of(nparts) - 1:
                 merges[eh] = merges.get(eh, 0) + 1
 
         for u in range(ub, ue):
