@@ -613,10 +613,7 @@ def bench_headsplit(args):
                        "parallelism": f"KV-head split x{world}"},
             "hbm": {"step_gbs_per_gpu": gbs, "peak_gbs": peak, "frac": gbs / peak,
                     "peak_kind": peak_kind},
-            "gpu_launches": N_LAYERS * args.steps,
-            "pool": {"cow_copies_timed": stats_after["cow_copies"] - stats_before["cow_copies"],
-                     "shared_pages": stats_after["shared_pages"],
-                     "replaced_slots": (churn_stats["replaced"] if churn is not None else 0)}, "e2e": None,
+            "gpu_launches": N_LAYERS * args.steps, "e2e": None,
         }), flush=True)
     if p2p:
         dist.barrier()
