@@ -112,6 +112,38 @@ inline ScopedBackendKvCacheSlot acquire_backend_kv_cache_slot(PagedKvRuntime &rt
     return ScopedBackendKvCacheSlot(rt.engine(), slot);
 }
 
+// Positions of build_reference_prompt_ids (:2507-2524) that depend only on
+// the reference wav and its transcript, and so hold the same KV rows for
+// every request using that reference: <|tts|>, [<|ref_text|>, transcript
+// ids...], <|ref_audio|>, and one row per delayed reference-code frame.
+inline int64_t reference_prefix_tokens(size_t ref_text_ids, int64_t delayed_ref_rows) {
+    return 1 + (ref_text_ids > 0 ? 1 + static_cast<int64_t>(ref_text_ids) : 0) + 1 +
+           delayed_ref_rows;
+}
+
+// Key under which such a prefix is published: 64-bit FNV-1a over the
+// reference-code cache key (reference_code_cache_key, :1545-1551: model path,
+// wav path, size, mtime) and the transcript token ids, with the prefix length.
+inline hkv_prefix_key reference_prefix_key(const std::string &code_cache_key,
+                                           const std::vector<int32_t> &ref_text_ids,
+                                           int64_t delayed_ref_rows) {
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&h](const void *data, size_t n) {
+        const unsigned char *p = static_cast<const unsigned char *>(data);
+        for (size_t i = 0; i < n; ++i) {
+            h ^= p[i];
+            h *= 1099511628211ull;
+        }
+    };
+    mix(code_cache_key.data(), code_cache_key.size());
+    mix(ref_text_ids.data(), ref_text_ids.size() * sizeof(int32_t));
+    mix(&delayed_ref_rows, sizeof(delayed_ref_rows));
+    hkv_prefix_key key;
+    key.hash = h;
+    key.n_tokens = reference_prefix_tokens(ref_text_ids.size(), delayed_ref_rows);
+    return key;
+}
+
 // One decode layer for all live slots (the per-layer block :5748-5786).
 inline void decode_layer(PagedKvRuntime &rt, int layer, const std::vector<int32_t> &slots,
                          const float *q, const float *k, const float *v, float *out,

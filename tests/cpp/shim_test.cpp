@@ -58,6 +58,17 @@ int main() {
     }
     hkv_pool_stats_get(rt.engine(), &st);
     EXPECT(st.live_slots == 0 && st.reserved == 0 && st.free_pages == 8);
+
+    // prefix keys: same reference -> same key; another transcript -> another key
+    const std::vector<int32_t> text{11, 12, 13};
+    const hkv_prefix_key k1 = hkv_pipeline::reference_prefix_key("m\nref.wav\n100\n7", text, 40);
+    const hkv_prefix_key k2 = hkv_pipeline::reference_prefix_key("m\nref.wav\n100\n7", text, 40);
+    const hkv_prefix_key k3 = hkv_pipeline::reference_prefix_key("m\nref.wav\n100\n7", {11, 12}, 40);
+    const hkv_prefix_key k4 = hkv_pipeline::reference_prefix_key("m\nother.wav\n100\n7", text, 40);
+    EXPECT(k1.hash == k2.hash && k1.n_tokens == 1 + 1 + 3 + 1 + 40);
+    EXPECT(k3.hash != k1.hash && k3.n_tokens == k1.n_tokens - 1);
+    EXPECT(k4.hash != k1.hash);
+    EXPECT(hkv_pipeline::reference_prefix_tokens(0, 5) == 7);
     std::printf("shim ok\n");
     return 0;
 }

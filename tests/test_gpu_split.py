@@ -136,3 +136,59 @@ def test_split_exchange_two_gpus():
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     mp.start_processes(_worker, args=(2, _free_port()), nprocs=2, start_method="spawn", join=True)
+
+
+def _silent_peer_worker(rank, world, port):
+    """Rank 1 connects but never runs its step: rank 0's bounded arrival wait
+    must give up (HKV_ERR_TIMEOUT at hkv_sync_check) and leave the engine
+    usable.  Nobody dies or faults; rank 1 only stays away between steps."""
+    import datetime
+
+    import torch.distributed as dist
+    for p in (str(REPO / "higgs-audio.cpp_b200"), str(REPO / "oracle")):
+        sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    import hkv
+    from hkv_dist import HeadSplit
+
+    dev = f"cuda:{rank}"
+    split = HeadSplit(world=world, rank=rank)
+    eng = hkv.Engine(n_layers=1, n_pages=16, max_slots=2, device=rank, **split.engine_shape())
+    stream = torch.cuda.current_stream().cuda_stream
+    s = eng.acquire(40)
+    kv = torch.randn((20, split.local_kv_heads, D), device=dev)
+    eng.rope_append_range(0, s, 20, kv, kv, stream)
+    eng.advance([s], 20)
+    handles = [None] * world
+    dist.all_gather_object(handles, eng.split_export(world, rank))
+    eng.split_connect(handles)
+    dist.barrier()
+    if rank == 0:
+        q = torch.randn((1, split.local_q_heads, D), device=dev)
+        k = torch.randn((1, split.local_kv_heads, D), device=dev)
+        eng.split_step(0, [s], q, k, k, stream)
+        eng.split_wait(0, stream)  # rank 1 never sends its slices
+        with pytest.raises(hkv.HkvError) as ei:
+            eng.sync_check(stream)
+        assert ei.value.status == hkv.HKV_ERR_TIMEOUT, ei.value
+        # the context is still good: an ordinary call works and reports clean
+        out = torch.empty((1, split.local_q_heads * D), device=dev)
+        eng.decode_attn(0, [s], q, out, stream)
+        eng.sync_check(stream)
+        assert torch.isfinite(out).all()
+    dist.barrier()
+    eng.split_disconnect()
+    dist.barrier()
+    eng.close()
+    dist.destroy_process_group()
+
+
+def test_split_wait_times_out_without_peer():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    mp.start_processes(_silent_peer_worker, args=(2, _free_port()), nprocs=2,
+                       start_method="spawn", join=True)
