@@ -391,16 +391,22 @@ def bench_ours(args):
         in_ev = [torch.cuda.Event() for _ in range(N_LAYERS)]
         out_ev = [torch.cuda.Event() for _ in range(N_LAYERS)]
 
+        def upload(layer):
+            with torch.cuda.stream(h2d):
+                dq[layer].copy_(hq[layer], non_blocking=True)
+                dk[layer].copy_(hk[layer], non_blocking=True)
+                dv[layer].copy_(hv[layer], non_blocking=True)
+                in_ev[layer].record(h2d)
+
         def e2e_step():
             # Inputs of layer l+1 stream in while layer l computes; the output
-            # of layer l streams out while layer l+1 computes.
+            # of layer l streams out while layer l+1 computes.  Uploads are
+            # enqueued one layer ahead of the launches, so the first launch of
+            # a step does not wait behind the host enqueueing 36 uploads.
+            upload(0)
             for layer in range(N_LAYERS):
-                with torch.cuda.stream(h2d):
-                    dq[layer].copy_(hq[layer], non_blocking=True)
-                    dk[layer].copy_(hk[layer], non_blocking=True)
-                    dv[layer].copy_(hv[layer], non_blocking=True)
-                    in_ev[layer].record(h2d)
-            for layer in range(N_LAYERS):
+                if layer + 1 < N_LAYERS:
+                    upload(layer + 1)
                 stream.wait_event(in_ev[layer])
                 eng.decode_step(layer, slots, dq[layer], dk[layer], dv[layer], out[layer], sh)
                 out_ev[layer].record(stream)
@@ -669,7 +675,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="scaleout")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -69,6 +69,15 @@ int main() {
     EXPECT(k3.hash != k1.hash && k3.n_tokens == k1.n_tokens - 1);
     EXPECT(k4.hash != k1.hash);
     EXPECT(hkv_pipeline::reference_prefix_tokens(0, 5) == 7);
+
+    // before anything is published under a key, acquiring with it gives an
+    // empty slot (the caller then writes the prompt and publishes it)
+    {
+        auto first = hkv_pipeline::acquire_backend_kv_cache_slot(rt, k1.n_tokens + 8, &k1);
+        EXPECT(first.used() == 0);
+        hkv_pool_stats_get(rt.engine(), &st);
+        EXPECT(st.prefixes == 0 && st.shared_pages == 0);
+    }
     std::printf("shim ok\n");
     return 0;
 }
