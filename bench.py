@@ -23,8 +23,8 @@ through all 36 layers per second), device-timed with CUDA events, max over
 ranks, inputs resident in HBM (the KV read per step, tens of GB, is far
 larger than the 126 MB L2, so no flush is needed); `e2e` = the same metric
 through the C ABI with q/k/v copied in from pinned host memory and the
-attention output copied back every layer; `roofline` of the attention kernel
-(live per-launch CUDA events); `cpu_baseline` = the reference's F32 GGML
+attention outputs copied back (one copy each way per 9 layers) every step;
+`roofline` of the attention kernel (live per-launch CUDA events); `cpu_baseline` = the reference's F32 GGML
 decode graph restated in C (oracle/hkv_oracle_graph.c) on a bounded sample.
 """
 from __future__ import annotations
@@ -381,65 +381,89 @@ def bench_ours(args):
     # ---------------- end to end through the C ABI from pinned host buffers
     e2e = None
     if args.e2e_steps > 0:
-        hq = torch.randn((N_LAYERS, n, H, D)).pin_memory()
-        hk = torch.randn((N_LAYERS, n, G, D)).pin_memory()
-        hv = torch.randn((N_LAYERS, n, G, D)).pin_memory()
-        hout = torch.empty((N_LAYERS, n, H * D)).pin_memory()
+        # Host inputs q | k | v per layer in one pinned buffer; device inputs
+        # and outputs double-buffered by step parity.  The layers run in
+        # chunks of 9: the inputs of step s+1's chunk c stream in while step
+        # s computes, and the outputs of chunk c stream out while the next
+        # chunk computes, so the stream sees event waits only at chunk
+        # boundaries and the launches inside a chunk still overlap.
+        qkv_floats = n * (H + 2 * G) * D
+        chunk = 9
+        chunks = [(c, min(c + chunk, N_LAYERS)) for c in range(0, N_LAYERS, chunk)]
+        hin = torch.randn((N_LAYERS, qkv_floats)).pin_memory()
+        hout = torch.empty((2, N_LAYERS, n, H * D)).pin_memory()
+        din = torch.empty((2, N_LAYERS, qkv_floats), device=dev)
+        dout = torch.empty((2, N_LAYERS, n, H * D), device=dev)
         h2d = torch.cuda.Stream(device=local)
         d2h = torch.cuda.Stream(device=local)
-        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        in_ev = [torch.cuda.Event() for _ in range(N_LAYERS)]
-        out_ev = [torch.cuda.Event() for _ in range(N_LAYERS)]
+        ev_in = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
+        ev_done = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
+        ev_back = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
+        used = [[False] * len(chunks) for _ in range(2)]
+        host_s = [0.0]
 
-        def upload(layer):
+        def upload(p, c):
+            lo, hi = chunks[c]
             with torch.cuda.stream(h2d):
-                dq[layer].copy_(hq[layer], non_blocking=True)
-                dk[layer].copy_(hk[layer], non_blocking=True)
-                dv[layer].copy_(hv[layer], non_blocking=True)
-                in_ev[layer].record(h2d)
+                if used[p][c]:
+                    h2d.wait_event(ev_done[p][c])  # the step two back has read din[p]
+                din[p, lo:hi].copy_(hin[lo:hi], non_blocking=True)
+                ev_in[p][c].record(h2d)
 
-        def e2e_step():
-            # Inputs of layer l+1 stream in while layer l computes; the output
-            # of layer l streams out while layer l+1 computes.  Uploads are
-            # enqueued one layer ahead of the launches, so the first launch of
-            # a step does not wait behind the host enqueueing 36 uploads.
-            upload(0)
-            for layer in range(N_LAYERS):
-                if layer + 1 < N_LAYERS:
-                    upload(layer + 1)
-                stream.wait_event(in_ev[layer])
-                eng.decode_step(layer, slots, dq[layer], dk[layer], dv[layer], out[layer], sh)
-                out_ev[layer].record(stream)
+        def e2e_step(s, first, last):
+            t0 = time.perf_counter()
+            p = s % 2
+            if first:
+                for c in range(len(chunks)):
+                    upload(p, c)
+            for c, (lo, hi) in enumerate(chunks):
+                if not last:
+                    upload(1 - p, c)
+                stream.wait_event(ev_in[p][c])
+                if used[p][c]:
+                    stream.wait_event(ev_back[p][c])  # dout[p] chunk is on the host
+                for layer in range(lo, hi):
+                    x = din[p, layer]
+                    eng.decode_step(layer, slots, x[:n * H * D], x[n * H * D:n * (H + G) * D],
+                                    x[n * (H + G) * D:], dout[p, layer], sh)
+                ev_done[p][c].record(stream)
+                used[p][c] = True
                 with torch.cuda.stream(d2h):
-                    d2h.wait_event(out_ev[layer])
-                    hout[layer].copy_(out[layer], non_blocking=True)
+                    d2h.wait_event(ev_done[p][c])
+                    hout[p, lo:hi].copy_(dout[p, lo:hi], non_blocking=True)
+                    ev_back[p][c].record(d2h)
             eng.advance(slots, 1)
             for i in range(n):
                 cur_len[i] += 1
             if churn is not None:
                 churn()
-            stream.wait_stream(d2h)
-            h2d.wait_stream(stream)  # next step's inputs overwrite dq/dk/dv
+            host_s[0] += time.perf_counter() - t0
 
-        e2e_step()
+        e2e_step(0, True, True)
+        stream.wait_stream(d2h)
         torch.cuda.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
         h2d.wait_stream(stream)
-        e0.record(h2d)
-        for _ in range(args.e2e_steps):
-            e2e_step()
+        d2h.wait_stream(stream)
+        host_s[0] = 0.0
+        for i in range(args.e2e_steps):
+            e2e_step(i, i == 0, i == args.e2e_steps - 1)
+        stream.wait_stream(d2h)  # the last outputs are on the host
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
         e2e_tokens = sum_over_ranks(n * args.e2e_steps)
-        h2d_bytes = N_LAYERS * n * (H * D + 2 * G * D) * 4
+        h2d_bytes = N_LAYERS * qkv_floats * 4
         d2h_bytes = N_LAYERS * n * H * D * 4
         e2e = {"value": e2e_tokens / (e2e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
-               "path": "pinned host q/k/v -> hkv_decode_step -> pinned host out"}
+               "host_enqueue_ms_per_step": 1e3 * host_s[0] / args.e2e_steps,
+               "path": "pinned host q|k|v -> hkv_decode_step -> pinned host out "
+                       "(one copy each way per 9 layers)"}
     eng.sync_check(sh)
 
     cpu = None

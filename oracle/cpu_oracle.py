@@ -28,7 +28,8 @@ _lib = None
 
 def build(force: bool = False) -> Path:
     """Compiles the oracle with the committed Makefile (gcc, OpenMP)."""
-    srcs = [HERE / "hkv_oracle.c", HERE / "hkv_oracle_graph.c", HERE / "Makefile"]
+    srcs = [HERE / "hkv_oracle.c", HERE / "hkv_oracle_q4k.c", HERE / "hkv_oracle_graph.c",
+            HERE / "Makefile"]
     if force or not LIB_PATH.exists() or any(
             s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE), "-B" if force else "all"], check=True)
@@ -60,6 +61,13 @@ def lib() -> ctypes.CDLL:
                                               ctypes.c_float, P, P]
         L.hkvo_graph_work_floats.argtypes = [I64, I64, I64, I64]
         L.hkvo_graph_work_floats.restype = I64
+        L.hkvo_q4k_dequant.argtypes = [P, I64, P]
+        L.hkvo_q8k_quantize.argtypes = [P, I64, P]
+        L.hkvo_q4k_dot_q8k.argtypes = [P, P, I64]
+        L.hkvo_q4k_dot_q8k.restype = ctypes.c_float
+        L.hkvo_q4k_gemv.argtypes = [P, I64, I64, P, I64, P, P]
+        L.hkvo_rms_norm_mul.argtypes = [P, I64, I64, ctypes.c_float, P, P]
+        L.hkvo_silu_mul.argtypes = [P, P, I64, P]
         L.hkvo_max_threads.restype = ctypes.c_int
         L.hkvo_set_threads.argtypes = [ctypes.c_int]
         _lib = L
@@ -173,6 +181,71 @@ class GraphBaseline:
                                       _p(self.row_off), _p(past), _p(self.cos), _p(self.sin),
                                       scale(self.D), _p(self.work), _p(self.out))
         return self.out
+
+
+# ------------------------------------------------------------ Q4_K backbone
+Q4K_BYTES = 144  # bytes of one 256-weight Q4_K block
+Q8K_BYTES = 292  # bytes of one 256-activation Q8_K block
+
+
+def q4k_dequant(blocks: np.ndarray, cols: int) -> np.ndarray:
+    """Q4_K bytes [rows][cols/256*144] -> F32 [rows][cols]."""
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    n_blocks = blocks.size // Q4K_BYTES
+    out = np.empty(n_blocks * 256, np.float32)
+    lib().hkvo_q4k_dequant(_p(blocks), n_blocks, _p(out))
+    return out.reshape(-1, cols)
+
+
+def q8k_quantize(x: np.ndarray) -> np.ndarray:
+    """F32 [..., k] -> Q8_K bytes [..., k/256*292]."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(x.size // 256 * Q8K_BYTES, np.uint8)
+    lib().hkvo_q8k_quantize(_p(x), x.size, _p(out))
+    return out.reshape(x.shape[:-1] + (x.shape[-1] // 256 * Q8K_BYTES,))
+
+
+def q8k_dequant(blocks: np.ndarray) -> np.ndarray:
+    """Q8_K bytes -> F32 (d * q), for checks."""
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, Q8K_BYTES)
+    d = b[:, :4].copy().view(np.float32)
+    q = b[:, 4:260].view(np.int8).astype(np.float32)
+    return (q * d).reshape(-1)
+
+
+def q4k_dot_q8k(w_row: np.ndarray, a: np.ndarray) -> float:
+    w_row = np.ascontiguousarray(w_row, np.uint8)
+    a = np.ascontiguousarray(a, np.uint8)
+    return float(lib().hkvo_q4k_dot_q8k(_p(w_row), _p(a), w_row.size // Q4K_BYTES))
+
+
+def q4k_gemv(w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    """mul_mat_f32(W, x) with Q4_K W: x [n][cols] F32 -> [n][rows]."""
+    w = np.ascontiguousarray(w, np.uint8)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
+    n = x.shape[0]
+    y = np.empty((n, rows), np.float32)
+    scratch = np.empty(n * (cols // 256) * Q8K_BYTES, np.uint8)
+    lib().hkvo_q4k_gemv(_p(w), rows, cols, _p(x), n, _p(y), _p(scratch))
+    return y
+
+
+def rms_norm_mul(x: np.ndarray, eps: float, weight=None) -> np.ndarray:
+    """ggml_rms_norm over the last axis, then ggml_mul by `weight`."""
+    x = np.ascontiguousarray(x, np.float32)
+    n = x.shape[-1]
+    y = np.empty_like(x)
+    w = None if weight is None else np.ascontiguousarray(weight, np.float32)
+    lib().hkvo_rms_norm_mul(_p(x), x.size // n, n, eps, None if w is None else _p(w), _p(y))
+    return y
+
+
+def silu_mul(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    gate = np.ascontiguousarray(gate, np.float32)
+    up = np.ascontiguousarray(up, np.float32)
+    y = np.empty_like(gate)
+    lib().hkvo_silu_mul(_p(gate), _p(up), gate.size, _p(y))
+    return y
 
 
 def max_threads() -> int:
