@@ -1078,6 +1078,14 @@ int hkv_slot_pages(const hkv_engine *eng, int32_t slot, int32_t *pages_out, int6
     return HKV_OK;
 }
 
+int hkv_engine_config(const hkv_engine *eng, hkv_config *out) {
+    if (eng == nullptr || out == nullptr) {
+        return HKV_ERR_INVALID;
+    }
+    *out = eng->cfg;
+    return HKV_OK;
+}
+
 int hkv_pool_stats_get(const hkv_engine *eng, hkv_pool_stats *out) {
     if (eng == nullptr || out == nullptr) {
         return HKV_ERR_INVALID;

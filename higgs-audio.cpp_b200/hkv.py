@@ -99,6 +99,39 @@ class PagedView(ctypes.Structure):
     ]
 
 
+class Q4kGemvArgs(ctypes.Structure):
+    """hkv_q4k_gemv_args."""
+    _fields_ = [("w", ctypes.c_void_p), ("w_up", ctypes.c_void_p), ("rows", ctypes.c_int64),
+                ("cols", ctypes.c_int64), ("n", ctypes.c_int32), ("x", ctypes.c_void_p),
+                ("norm", ctypes.c_void_p), ("eps", ctypes.c_float), ("residual", ctypes.c_void_p),
+                ("y", ctypes.c_void_p)]
+
+
+class Q4kQkvArgs(ctypes.Structure):
+    """hkv_q4k_qkv_args."""
+    _fields_ = [("wq", ctypes.c_void_p), ("wk", ctypes.c_void_p), ("wv", ctypes.c_void_p),
+                ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32), ("cols", ctypes.c_int64),
+                ("n", ctypes.c_int32), ("x", ctypes.c_void_p), ("norm", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
+                ("q_out", ctypes.c_void_p), ("k_out", ctypes.c_void_p), ("v_out", ctypes.c_void_p)]
+
+
+class BackboneLayer(ctypes.Structure):
+    """hkv_backbone_layer: one layer's weight pointers."""
+    _fields_ = [(name, ctypes.c_void_p) for name in (
+        "attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down",
+        "attn_norm", "ffn_norm", "attn_q_norm", "attn_k_norm")]
+
+
+class BackboneWeights(ctypes.Structure):
+    """hkv_backbone_weights."""
+    _fields_ = [("hidden", ctypes.c_int32), ("ffn", ctypes.c_int32), ("text_vocab", ctypes.c_int64),
+                ("n_codebooks", ctypes.c_int32), ("codebook_size", ctypes.c_int32),
+                ("rms_eps", ctypes.c_float), ("layers", ctypes.POINTER(BackboneLayer)),
+                ("token_embd", ctypes.c_void_p), ("audio_embd", ctypes.c_void_p),
+                ("output_norm", ctypes.c_void_p), ("audio_output", ctypes.c_void_p)]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -138,6 +171,22 @@ SIGNATURES = {
     "hkv_split_step": ([_P, _I32, _I32, _I32P, _P, _P, _P, _P], ctypes.c_int),
     "hkv_split_wait": ([_P, _I32, _P], ctypes.c_int),
     "hkv_split_output": ([_P, _I32, ctypes.POINTER(_P), _I64P], ctypes.c_int),
+    "hkv_engine_config": ([_P, ctypes.POINTER(Config)], ctypes.c_int),
+    "hkv_q4k_quantize": ([_P, _I64, _I64, _P, _P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
+    "hkv_q4k_gemv": ([ctypes.POINTER(Q4kGemvArgs), _P, ctypes.c_char_p, ctypes.c_size_t],
+                     ctypes.c_int),
+    "hkv_q4k_qkv": ([ctypes.POINTER(Q4kQkvArgs), _P, ctypes.c_char_p, ctypes.c_size_t],
+                    ctypes.c_int),
+    "hkv_backbone_create": ([_P, ctypes.POINTER(BackboneWeights), _I32, ctypes.POINTER(_P)],
+                            ctypes.c_int),
+    "hkv_backbone_destroy": ([_P], None),
+    "hkv_backbone_last_error": ([_P], ctypes.c_char_p),
+    "hkv_backbone_embed_text": ([_P, _I32, _I32P, _P], ctypes.c_int),
+    "hkv_backbone_embed_codes": ([_P, _I32, _P, _P], ctypes.c_int),
+    "hkv_backbone_decode": ([_P, _I32, _I32P, _I32, _P], ctypes.c_int),
+    "hkv_backbone_buffers": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)],
+                             ctypes.c_int),
+    "hkv_backbone_sync_check": ([_P, _P], ctypes.c_int),
     "hkv_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
     "hkv_profile_reset": ([_P], ctypes.c_int),
     "hkv_profile_read": ([_P, ctypes.c_int, _I64P, ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
@@ -417,6 +466,114 @@ def decode_attn_noalloc(view: PagedView, layer: int, pos: Sequence[int],
     if st != HKV_OK:
         cls = HkvRangeError if st == HKV_ERR_RANGE else HkvError
         raise cls(st, msg.value.decode())
+
+
+class DeviceArray:
+    """A raw device pointer exposed through __cuda_array_interface__ (wrap it
+    with torch.as_tensor(..., device=...) to read an engine buffer)."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+# --------------------------------------------------------- Q4_K backbone
+def _raise_msg(st: int, msg) -> None:
+    if st != HKV_OK:
+        cls = HkvRangeError if st == HKV_ERR_RANGE else HkvError
+        raise cls(st, msg.value.decode())
+
+
+def q4k_quantize(w, rows: int, cols: int, blocks, stream=None, lib=None) -> None:
+    """hkv_q4k_quantize: F32 [rows][cols] device -> Q4_K blocks (rows*cols/256*144 bytes)."""
+    lib = lib or load_library()
+    msg = ctypes.create_string_buffer(512)
+    _raise_msg(lib.hkv_q4k_quantize(_ptr(w), rows, cols, _ptr(blocks), _stream(stream), msg,
+                                    len(msg)), msg)
+
+
+def q4k_gemv(w, rows: int, cols: int, x, y, n: int = 1, norm=None, eps: float = 1e-6,
+             residual=None, w_up=None, stream=None, lib=None) -> None:
+    """hkv_q4k_gemv: y = [residual +] W x' or silu(W x') * (W_up x')."""
+    lib = lib or load_library()
+    a = Q4kGemvArgs(_ptr(w), _ptr(w_up), rows, cols, n, _ptr(x), _ptr(norm), eps, _ptr(residual),
+                    _ptr(y))
+    msg = ctypes.create_string_buffer(512)
+    _raise_msg(lib.hkv_q4k_gemv(ctypes.byref(a), _stream(stream), msg, len(msg)), msg)
+
+
+def q4k_qkv(wq, wk, wv, cols: int, x, q_norm, k_norm, q_out, k_out, v_out, n: int = 1,
+            norm=None, eps: float = 1e-6, n_head: int = 32, n_head_kv: int = 8, stream=None,
+            lib=None) -> None:
+    """hkv_q4k_qkv: q/k/v projections with the per-head norms of q and k."""
+    lib = lib or load_library()
+    a = Q4kQkvArgs(_ptr(wq), _ptr(wk), _ptr(wv), n_head, n_head_kv, cols, n, _ptr(x), _ptr(norm),
+                   eps, _ptr(q_norm), _ptr(k_norm), _ptr(q_out), _ptr(k_out), _ptr(v_out))
+    msg = ctypes.create_string_buffer(512)
+    _raise_msg(lib.hkv_q4k_qkv(ctypes.byref(a), _stream(stream), msg, len(msg)), msg)
+
+
+class Backbone:
+    """hkv_backbone: the Q4_K decode step around an engine.  `weights` maps
+    names to device tensors (kept referenced here): per layer l
+    "blk.{l}.attn_q" ... "blk.{l}.attn_k_norm", plus "token_embd",
+    "a.token_embd", "output_norm", "a.output"."""
+
+    LAYER_KEYS = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down",
+                  "attn_norm", "ffn_norm", "attn_q_norm", "attn_k_norm")
+
+    def __init__(self, engine: "Engine", weights: dict, hidden: int = 2560, ffn: int = 9728,
+                 text_vocab: int = 151936, n_codebooks: int = 8, codebook_size: int = 1026,
+                 rms_eps: float = 1e-6, max_batch: int = 1):
+        self.engine = engine
+        self.lib = engine.lib
+        self.weights = weights
+        n_layers = engine.cfg.n_layers
+        self._layers = (BackboneLayer * n_layers)()
+        for l in range(n_layers):
+            for key in self.LAYER_KEYS:
+                setattr(self._layers[l], key, _ptr(weights[f"blk.{l}.{key}"]))
+        self._w = BackboneWeights(hidden, ffn, text_vocab, n_codebooks, codebook_size, rms_eps,
+                                  self._layers, _ptr(weights["token_embd"]),
+                                  _ptr(weights["a.token_embd"]), _ptr(weights["output_norm"]),
+                                  _ptr(weights["a.output"]))
+        h = ctypes.c_void_p()
+        st = self.lib.hkv_backbone_create(engine.handle, ctypes.byref(self._w), max_batch,
+                                          ctypes.byref(h))
+        if st != HKV_OK:
+            raise HkvError(st, f"hkv_backbone_create failed: status {st}")
+        self.handle = h
+        self.n_codebooks, self.codebook_size, self.hidden = n_codebooks, codebook_size, hidden
+        hp, lp, cp = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        self.lib.hkv_backbone_buffers(self.handle, ctypes.byref(hp), ctypes.byref(lp),
+                                      ctypes.byref(cp))
+        self.hidden_ptr, self.logits_ptr, self.codes_ptr = hp.value, lp.value, cp.value
+
+    def _check(self, st: int) -> None:
+        if st != HKV_OK:
+            msg = self.lib.hkv_backbone_last_error(self.handle).decode()
+            cls = HkvRangeError if st == HKV_ERR_RANGE else HkvError
+            raise cls(st, msg)
+
+    def embed_text(self, ids: Sequence[int], stream=None) -> None:
+        n, arr = _slots_arg(ids)
+        self._check(self.lib.hkv_backbone_embed_text(self.handle, n, arr, _stream(stream)))
+
+    def embed_codes(self, n: int, codes=None, stream=None) -> None:
+        self._check(self.lib.hkv_backbone_embed_codes(self.handle, n, _ptr(codes), _stream(stream)))
+
+    def decode(self, slots: Sequence[int], want_logits: bool = True, stream=None) -> None:
+        n, arr = _slots_arg(slots)
+        self._check(self.lib.hkv_backbone_decode(self.handle, n, arr, 1 if want_logits else 0,
+                                                 _stream(stream)))
+
+    def sync_check(self, stream=None) -> None:
+        self._check(self.lib.hkv_backbone_sync_check(self.handle, _stream(stream)))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.hkv_backbone_destroy(self.handle)
+            self.handle = None
 
 
 def header_functions(header: Path) -> list:

@@ -20,7 +20,8 @@ REPO = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libhkv.so"
-SOURCES = [CSRC / "hkv_kernels.cu", CSRC / "hkv_engine.cpp", CSRC / "hkv_noalloc.cu"]
+SOURCES = [CSRC / "hkv_kernels.cu", CSRC / "hkv_engine.cpp", CSRC / "hkv_noalloc.cu",
+           CSRC / "hkv_backbone.cu"]
 HEADERS = [CSRC / "hkv_internal.h", CSRC / "hkv_plan.h", REPO / "include" / "hkv.h"]
 
 NVCC_FLAGS = [

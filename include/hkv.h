@@ -109,7 +109,9 @@ typedef enum hkv_kernel_id {
                                kernels, so nothing is recorded under this id    */
     HKV_KERNEL_GATHER = 3,  /* hkv_gather                                         */
     HKV_KERNEL_STEP = 4,    /* hkv_decode_step (append + attention, one launch)   */
-    HKV_KERNEL_COUNT = 5
+    HKV_KERNEL_GEMV = 5,    /* Q4_K projections (hkv_q4k_*, hkv_backbone_decode)  */
+    HKV_KERNEL_EMBED = 6,   /* embedding rows (hkv_backbone_embed_*)              */
+    HKV_KERNEL_COUNT = 7
 } hkv_kernel_id;
 
 /* ------------------------------------------------------------ engine -- */
@@ -122,6 +124,8 @@ int hkv_config_default(hkv_config *cfg);
  * ensure_backend_kv_rope_tables, :1606-1622) and the split-partial buffer. */
 int hkv_engine_create(const hkv_config *cfg, hkv_engine **out);
 int hkv_engine_destroy(hkv_engine *eng);
+/* The configuration the engine was created with. */
+int hkv_engine_config(const hkv_engine *eng, hkv_config *out);
 
 /* Message of the last failed call on this engine ("" if none). */
 const char *hkv_last_error(const hkv_engine *eng);
@@ -300,6 +304,116 @@ int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer, int32_t n
                             const int32_t *pos, const int32_t *page_off, const int32_t *pages,
                             const float *q_prerope, float *out, hkv_stream stream,
                             char *err_msg, size_t err_len);
+
+/* ------------------------------------------- Q4_K backbone projections -- */
+/* The projections around the KV path in the reference's decode graph
+ * (src/higgs_pipeline.cpp:5709-5733 q/k/v with per-head RMSNorm, :5790-5791
+ * o_proj + residual, :5806-5843 SwiGLU FFN + residual, :5858-5863 output head),
+ * each mul_mat_f32 (:465-469) over GGUF Q4_K weights.  Weights: Q4_K blocks
+ * (256 weights in 144 bytes: f16 d, f16 dmin, 12 bytes of 6-bit sub-block
+ * scales and mins, 128 bytes of 4-bit quants), a row of `cols` weights being
+ * cols/256 consecutive blocks; every pointer 16-byte aligned device memory.
+ * As in GGML's CPU backend, each activation row is quantised to Q8_K (blocks
+ * of 256 int8 with an F32 scale) before the integer dot products.  Calls are
+ * ordered on `stream`; on failure they return a status and write a message
+ * into err_msg (may be NULL). */
+
+/* y = [residual +] W . x'  or, with w_up, y = silu(W . x') * (W_up . x'),
+ * where x' = rms_norm(x) * norm when norm is given (eps inside the root). */
+typedef struct hkv_q4k_gemv_args {
+    const void *w;          /* Q4_K [rows][cols / 256 blocks]                   */
+    const void *w_up;       /* NULL, or the up matrix of a SwiGLU pair (w = gate) */
+    int64_t rows;
+    int64_t cols;           /* multiple of 256, at most 16384                   */
+    int32_t n;              /* activation vectors                               */
+    const float *x;         /* [n][cols]                                        */
+    const float *norm;      /* NULL or [cols]                                   */
+    float eps;
+    const float *residual;  /* NULL or [n][rows]; may equal y (in place)         */
+    float *y;               /* [n][rows]                                        */
+} hkv_q4k_gemv_args;
+int hkv_q4k_gemv(const hkv_q4k_gemv_args *args, hkv_stream stream, char *err_msg,
+                 size_t err_len);
+
+/* q, k, v projections of x' = rms_norm(x) * norm in one launch, with the
+ * per-head rms_norm(.) * q_norm / k_norm of q and k (:5711-5733); RoPE is
+ * left to the decode call, which applies it to q and to the appended k. */
+typedef struct hkv_q4k_qkv_args {
+    const void *wq, *wk, *wv;   /* Q4_K [n_head*128][cols], [n_head_kv*128][cols] x2 */
+    int32_t n_head, n_head_kv;
+    int64_t cols;
+    int32_t n;
+    const float *x;             /* [n][cols]                                     */
+    const float *norm;          /* NULL or [cols] (attn_norm)                    */
+    float eps;
+    const float *q_norm;        /* [128]                                         */
+    const float *k_norm;        /* [128]                                         */
+    float *q_out;               /* [n][n_head*128]                               */
+    float *k_out, *v_out;       /* [n][n_head_kv*128]                            */
+} hkv_q4k_qkv_args;
+int hkv_q4k_qkv(const hkv_q4k_qkv_args *args, hkv_stream stream, char *err_msg, size_t err_len);
+
+/* The repo's Q4_K encoder (the reference quantises offline with GGML's tools,
+ * scripts/quantize_higgs_gguf_q4_k.py): F32 [rows][cols] -> Q4_K blocks. */
+int hkv_q4k_quantize(const float *w, int64_t rows, int64_t cols, void *blocks, hkv_stream stream,
+                     char *err_msg, size_t err_len);
+
+/* ------------------------------------------------- backbone decode step -- */
+/* A whole decode step of the 36-layer backbone for a batch of slots on one
+ * engine: the reference's per-frame graph (run_reference_text_code_frames_
+ * backend_kv, :4785-5200, whose per-frame graph is run_kv_decode_graph_all_
+ * layers_with_backend_cache_ex, :5629-5863) with the engine's paged KV path
+ * in place of the slot cache.  Per layer: hkv_q4k_qkv, hkv_decode_step
+ * (RoPE, append, attention), o_proj + residual, SwiGLU FFN + residual; then
+ * the output head and greedy codes.  Weights are borrowed (caller-owned). */
+typedef struct hkv_backbone hkv_backbone;
+
+typedef struct hkv_backbone_layer {
+    const void *attn_q, *attn_k, *attn_v, *attn_output;  /* Q4_K */
+    const void *ffn_gate, *ffn_up, *ffn_down;             /* Q4_K */
+    const float *attn_norm, *ffn_norm;                     /* [hidden] */
+    const float *attn_q_norm, *attn_k_norm;                /* [128]    */
+} hkv_backbone_layer;
+
+typedef struct hkv_backbone_weights {
+    int32_t hidden;            /* 2560                                          */
+    int32_t ffn;               /* 9728                                          */
+    int64_t text_vocab;        /* rows of token_embd (151936)                   */
+    int32_t n_codebooks;       /* 8   (k_num_codebooks, include/higgs_audio.h:15) */
+    int32_t codebook_size;     /* 1026 (k_codebook_vocab_size, :17)            */
+    float rms_eps;
+    const hkv_backbone_layer *layers; /* host array, one per engine layer       */
+    const void *token_embd;    /* Q4_K [text_vocab][hidden]                     */
+    const void *audio_embd;    /* Q4_K [n_codebooks*codebook_size][hidden] (a.token_embd) */
+    const float *output_norm;  /* [hidden]                                      */
+    const void *audio_output;  /* Q4_K [n_codebooks*codebook_size][hidden] (a.output) */
+} hkv_backbone_weights;
+
+/* Binds weights to an engine (q/k/v head counts from its config) and
+ * allocates activation buffers for up to max_batch slots. */
+int hkv_backbone_create(hkv_engine *kv, const hkv_backbone_weights *w, int32_t max_batch,
+                        hkv_backbone **out);
+void hkv_backbone_destroy(hkv_backbone *bb);
+const char *hkv_backbone_last_error(const hkv_backbone *bb);
+
+/* hidden[e] = token_embd[ids[e]] (host ids; text prompt tokens, :2912). */
+int hkv_backbone_embed_text(hkv_backbone *bb, int32_t n, const int32_t *ids, hkv_stream stream);
+/* hidden[e] = sum over c of a.token_embd[c * codebook_size + codes[e][c]]
+ * (:2915-2924, fuse_audio_ids_for_embedding :2546-2562); codes is a DEVICE
+ * [n][n_codebooks] array, or NULL for the codes of the last decode. */
+int hkv_backbone_embed_codes(hkv_backbone *bb, int32_t n, const int32_t *codes,
+                             hkv_stream stream);
+/* Runs every layer on hidden[0..n) for slots[e] (appending one row each),
+ * advances the slots by one position, and, when want_logits, computes
+ * logits = a.output(rms_norm(hidden) * output_norm) and the greedy code of
+ * each codebook (the first maximum). */
+int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32_t want_logits,
+                        hkv_stream stream);
+/* Device buffers: hidden [max_batch][hidden], logits
+ * [max_batch][n_codebooks*codebook_size], codes [max_batch][n_codebooks]. */
+int hkv_backbone_buffers(const hkv_backbone *bb, float **hidden, float **logits, int32_t **codes);
+/* Synchronises `stream` and reports a bad embedding id recorded on the GPU. */
+int hkv_backbone_sync_check(hkv_backbone *bb, hkv_stream stream);
 
 /* ---------------------------------------------------------- profiling -- */
 

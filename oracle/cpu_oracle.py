@@ -254,3 +254,82 @@ def max_threads() -> int:
 
 def set_threads(n: int) -> None:
     lib().hkvo_set_threads(n)
+
+
+class BackboneOracle:
+    """The reference's per-frame decode graph on the CPU
+    (run_kv_decode_graph_all_layers_with_backend_cache_ex,
+    src/higgs_pipeline.cpp:5629-5863) with Q4_K weights and the engine's F16
+    KV rows: rms_norm * attn_norm -> Q4_K q/k/v (Q8_K activations) -> per-head
+    rms_norm * q_norm / k_norm -> RoPE -> append -> attention -> h + Wo attn ->
+    rms_norm * ffn_norm -> silu(Wg m) * (Wu m) -> h + Wd g; then
+    a.output(rms_norm(h) * output_norm) and the first maximum per codebook.
+
+    `weights` maps the GGUF names to numpy arrays: Q4_K matrices as uint8
+    [rows][cols/256*144], norms as float32."""
+
+    def __init__(self, weights: dict, n_layers: int, hidden: int = 2560, ffn: int = 9728,
+                 n_head: int = 32, n_head_kv: int = 8, head_dim: int = 128, n_codebooks: int = 8,
+                 codebook_size: int = 1026, eps: float = 1e-6, cos=None, sin=None):
+        self.w = weights
+        self.L, self.hidden, self.ffn = n_layers, hidden, ffn
+        self.H, self.G, self.D = n_head, n_head_kv, head_dim
+        self.nc, self.cs, self.eps = n_codebooks, codebook_size, eps
+        if cos is None:
+            cos, sin = rope_table(key_length=head_dim)
+        self.cos, self.sin = cos, sin
+        self.caches = {}  # (slot, layer) -> (k rows, v rows) as uint16 [R][G][D]
+
+    def embed_text(self, ids) -> np.ndarray:
+        t = self.w["token_embd"]
+        return np.stack([q4k_dequant(t[i], self.hidden)[0] for i in ids]).astype(np.float32)
+
+    def embed_codes(self, codes) -> np.ndarray:
+        t = self.w["a.token_embd"]
+        out = []
+        for row in np.asarray(codes).reshape(-1, self.nc):
+            acc = None
+            for c, code in enumerate(row):
+                r = q4k_dequant(t[c * self.cs + int(code)], self.hidden)[0]
+                acc = r if acc is None else (acc + r).astype(np.float32)
+            out.append(acc)
+        return np.stack(out).astype(np.float32)
+
+    def _gemv(self, name: str, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+        return q4k_gemv(self.w[name], rows, cols, x)
+
+    def decode(self, h: np.ndarray, slots, pos, want_logits: bool = True):
+        """One token per slot at positions `pos`; returns (h, logits, codes)."""
+        n = h.shape[0]
+        H, G, D, eps = self.H, self.G, self.D, self.eps
+        h = np.ascontiguousarray(h, np.float32)
+        for l in range(self.L):
+            p = f"blk.{l}."
+            xn = rms_norm_mul(h, eps, self.w[p + "attn_norm"])
+            q = self._gemv(p + "attn_q", H * D, self.hidden, xn).reshape(n, H, D)
+            k = self._gemv(p + "attn_k", G * D, self.hidden, xn).reshape(n, G, D)
+            v = self._gemv(p + "attn_v", G * D, self.hidden, xn).reshape(n, G, D)
+            q = rms_norm_mul(q, eps, self.w[p + "attn_q_norm"])
+            k = rms_norm_mul(k, eps, self.w[p + "attn_k_norm"])
+            k16, v16 = append_rows(k, v, np.asarray(pos), self.cos, self.sin)
+            ks, vs, qr = [], [], []
+            for e, s in enumerate(slots):
+                kc, vc = self.caches.get((s, l), (np.zeros((0, G, D), np.uint16),) * 2)
+                kc = np.concatenate([kc[:pos[e]], k16[e:e + 1]])
+                vc = np.concatenate([vc[:pos[e]], v16[e:e + 1]])
+                self.caches[(s, l)] = (kc, vc)
+                ks.append(kc)
+                vs.append(vc)
+                qr.append(rope_neox(q[e], self.cos[pos[e]], self.sin[pos[e]]))
+            attn = decode_attn(np.stack(qr), ks, vs)
+            h = (h + self._gemv(p + "attn_output", self.hidden, H * D, attn)).astype(np.float32)
+            m = rms_norm_mul(h, eps, self.w[p + "ffn_norm"])
+            g = silu_mul(self._gemv(p + "ffn_gate", self.ffn, self.hidden, m),
+                         self._gemv(p + "ffn_up", self.ffn, self.hidden, m))
+            h = (h + self._gemv(p + "ffn_down", self.hidden, self.ffn, g)).astype(np.float32)
+        if not want_logits:
+            return h, None, None
+        logits = self._gemv("a.output", self.nc * self.cs, self.hidden,
+                            rms_norm_mul(h, eps, self.w["output_norm"]))
+        codes = logits.reshape(n, self.nc, self.cs).argmax(-1).astype(np.int32)
+        return h, logits, codes
