@@ -730,7 +730,7 @@ def bench_backbone(args):
                                  device_id=torch.device("cuda", local))
         dist = tdist
     dev = f"cuda:{local}"
-    text_vocab, prompt_len = 151936, 1024
+    text_vocab, prompt_len = 151936, args.prompt_len
     weights, weight_bytes = make_backbone_weights(hkv, N_LAYERS, text_vocab, dev, 1234 + rank)
     total = prompt_len + args.warmup + args.steps + args.e2e_steps + 4
     eng = hkv.Engine(n_layers=N_LAYERS, n_pages=total // 16 + 4, max_slots=1, device=local,
@@ -761,11 +761,13 @@ def bench_backbone(args):
     clocks.start()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     ev0.record(stream)
     with torch.cuda.stream(stream):
         for _ in range(args.steps):
             step()
     ev1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms_local = ev0.elapsed_time(ev1)
@@ -947,6 +949,9 @@ def main():
                          "replacement slot into a shared partial page: copy-on-write)")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
                     help="headsplit: how the per-head outputs reach every rank")
+    ap.add_argument("--prompt-len", type=int, default=1024,
+                    help="backbone: prompt tokens before the greedy steps (1024 for every "
+                         "reported number; fewer only for profiler captures)")
     ap.add_argument("--layers", type=int, default=36,
                     help="layers per step (36 for every reported number; fewer only for "
                          "profiler captures of the same per-launch sizes)")

@@ -73,7 +73,18 @@ struct GemvParams {
     float *y[3];              // outputs, [n][y_rows[m]] each
     int32_t y_rows[3];
     const float *head_norm[2];  // kQkv: q_norm, k_norm [128]
+    int32_t rows_per_cta;     // contiguous weight rows of one CTA
+    int32_t chunk_rows;       // rows per ring stage (a power of two, <= 64)
+    DeviceError *err;         // bounded-wait timeouts are recorded here
 };
+
+constexpr int kStages = 4;                  // weight ring depth per CTA
+constexpr int kStageBytes = 24 * 1024;      // bytes per ring stage
+constexpr int kRingBytes = kStages * kStageBytes;
+constexpr int kBarBytes = 64;               // kStages full + kStages empty mbarriers
+constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
+constexpr int kQkvRows = 32;                // rows per CTA in the q/k/v launch (4 per head)
+static_assert(2 * kStages * 8 <= kBarBytes, "mbarrier area too small");
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
@@ -82,6 +93,56 @@ __device__ __forceinline__ void pdl_trigger() {
 
 __device__ __forceinline__ int4 ld_stream(const uint8_t *p) {
     return __ldcs(reinterpret_cast<const int4 *>(p));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// True when the phase with `parity` completed within the budget.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (clock64() - t0 < kWaitBudgetCycles) {
+        if (mbar_try_wait(bar, parity)) return true;
+    }
+    return false;
+}
+// 1-D bulk copy global -> this CTA's shared memory (no tensor map, no
+// multicast); completion counted in transaction bytes on `bar`.  Weights
+// are read once per step: evict-first in L2.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
 }
 
 __device__ __forceinline__ float half_bits(uint32_t bits16) {
@@ -150,281 +211,426 @@ __device__ inline Q8View carve_q8(unsigned char *smem, int n, int cols) {
     return v;
 }
 
-// Q8_K quantisation of the n activation vectors (GGML's quantize_row_q8_K:
-// iscale = -127 / (element of largest magnitude, the first on ties),
-// q = min(127, round-half-even(iscale * x)), d = 1 / iscale), optionally of
-// rms_norm(x) * norm (sum of squares in double, mean rounded to float,
-// scale = 1 / sqrtf(mean + eps)).  Ends with a CTA barrier.
-__device__ void quantize_activations(const GemvParams &p, const Q8View &a) {
-    const int nsb = p.cols / kQK;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = 0; e < p.n; ++e) {
-        const float *x = p.x + static_cast<size_t>(e) * p.cols;
-        float scale = 1.0f;
-        if (p.norm != nullptr) {
-            double s = 0.0;
-            for (int i = threadIdx.x; i < p.cols; i += kThreads) {
-                const float v = x[i];
-                s += static_cast<double>(__fmul_rn(v, v));
-            }
-            s = warp_sum_double(s);
-            if (lane == 0) a.red[warp] = s;
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                double t = 0.0;
-                for (int w = 0; w < kWarps; ++w) t += a.red[w];
-                a.red[kWarps] = t;
-            }
-            __syncthreads();
-            const float mean = static_cast<float>(a.red[kWarps] / static_cast<double>(p.cols));
-            scale = 1.0f / sqrtf(mean + p.eps);
-            __syncthreads();  // a.red is reused by the next vector
-        }
-        for (int b = warp; b < nsb; b += kWarps) {
-            const int base = b * kQK + lane * 8;
-            const float4 u0 = *reinterpret_cast<const float4 *>(x + base);
-            const float4 u1 = *reinterpret_cast<const float4 *>(x + base + 4);
-            float v[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-            if (p.norm != nullptr) {
-                const float4 w0 = *reinterpret_cast<const float4 *>(p.norm + base);
-                const float4 w1 = *reinterpret_cast<const float4 *>(p.norm + base + 4);
-                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+// Barrier of the kWarps consumer warps only (the producer warp never joins).
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");
+}
+
+// Q8_K quantisation of one 256-element block held 8 per lane across a warp
+// (GGML's quantize_row_q8_K: iscale = -127 / (element of largest magnitude,
+// the first on ties), q = min(127, round-half-even(iscale * x)),
+// d = 1 / iscale), written to the shared-memory image.
+__device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View &a, int cols, int nsb,
+                                               int e, int b, int lane) {
+    float am = 0.0f, mx = 0.0f;
+    int idx = 0x7fffffff;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], scale), w[i]);
-            }
-            float am = 0.0f, mx = 0.0f;
-            int idx = 0x7fffffff;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float ax = fabsf(v[i]);
-                if (ax > am) {
-                    am = ax;
-                    mx = v[i];
-                    idx = lane * 8 + i;
-                }
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const float oa = __shfl_xor_sync(0xffffffffu, am, off);
-                const float om = __shfl_xor_sync(0xffffffffu, mx, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
-                if (oa > am || (oa == am && oi < idx)) {
-                    am = oa;
-                    mx = om;
-                    idx = oi;
-                }
-            }
-            int q[8];
-            float d = 0.0f;
-            if (am == 0.0f) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) q[i] = 0;
-            } else {
-                const float iscale = -127.0f / mx;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, v[i])));
-                d = 1.0f / iscale;
-            }
-            uint32_t lo = 0, hi = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                lo |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
-                hi |= (static_cast<uint32_t>(q[i + 4]) & 0xFFu) << (8 * i);
-            }
-            *reinterpret_cast<uint2 *>(a.q + static_cast<size_t>(e) * p.cols + base) = make_uint2(lo, hi);
-            int qs = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) qs += q[i];
-            qs += __shfl_xor_sync(0xffffffffu, qs, 1);
-            qs += __shfl_xor_sync(0xffffffffu, qs, 2);
-            if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
-            if (lane == 0) a.d[e * nsb + b] = d;
+    for (int i = 0; i < 8; ++i) {
+        const float ax = fabsf(v[i]);
+        if (ax > am) {
+            am = ax;
+            mx = v[i];
+            idx = lane * 8 + i;
         }
     }
-    __syncthreads();
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, am, off);
+        const float om = __shfl_xor_sync(0xffffffffu, mx, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (oa > am || (oa == am && oi < idx)) {
+            am = oa;
+            mx = om;
+            idx = oi;
+        }
+    }
+    int q[8];
+    float d = 0.0f;
+    if (am == 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = 0;
+    } else {
+        const float iscale = -127.0f / mx;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, v[i])));
+        d = 1.0f / iscale;
+    }
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
+        hi |= (static_cast<uint32_t>(q[i + 4]) & 0xFFu) << (8 * i);
+    }
+    *reinterpret_cast<uint2 *>(a.q + static_cast<size_t>(e) * cols + b * kQK + lane * 8) = make_uint2(lo, hi);
+    int qs = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qs += q[i];
+    qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+    qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+    if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
+    if (lane == 0) a.d[e * nsb + b] = d;
 }
 
-// One thread's share of a Q4_K block: the 16-byte header and the 32 bytes of
-// quants of sub-block pair `part` (sub-blocks 2*part and 2*part + 1).
-struct BlockPart {
-    int4 hdr, q0, q1;
+constexpr int kSlabMax = 5;  // 2048-element slabs held in registers (cols <= 10240)
+
+// Q8_K image of the n activation vectors, optionally of rms_norm(x) * norm
+// (sum of squares in double, mean rounded to float, scale = 1 / sqrtf(mean +
+// eps), y = (x * scale) * norm as GGML rounds it).  Thread t holds elements
+// [8t, 8t + 8) of every 2048-element slab, so warp w holds block 8s + w of
+// slab s: one batch of loads, one barrier for the norm, then every block is
+// quantised from registers.  Run by the kWarps consumer warps; ends with
+// their barrier.
+__device__ void quantize_activations(const GemvParams &p, const Q8View &a, double *red) {
+    const int nsb = p.cols / kQK;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_slabs = (nsb + kWarps - 1) / kWarps;
+    for (int e = 0; e < p.n; ++e) {
+        const float *x = p.x + static_cast<size_t>(e) * p.cols;
+        if (n_slabs <= kSlabMax) {
+            float v[kSlabMax][8];
+#pragma unroll
+            for (int sl = 0; sl < kSlabMax; ++sl) {
+                const int b = sl * kWarps + warp;
+                if (sl < n_slabs && b < nsb) {
+                    const float4 u0 = *reinterpret_cast<const float4 *>(x + b * kQK + lane * 8);
+                    const float4 u1 = *reinterpret_cast<const float4 *>(x + b * kQK + lane * 8 + 4);
+                    v[sl][0] = u0.x; v[sl][1] = u0.y; v[sl][2] = u0.z; v[sl][3] = u0.w;
+                    v[sl][4] = u1.x; v[sl][5] = u1.y; v[sl][6] = u1.z; v[sl][7] = u1.w;
+                }
+            }
+            if (p.norm != nullptr) {
+                double ss = 0.0;
+#pragma unroll
+                for (int sl = 0; sl < kSlabMax; ++sl) {
+                    const int b = sl * kWarps + warp;
+                    if (sl < n_slabs && b < nsb) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ss += static_cast<double>(__fmul_rn(v[sl][i], v[sl][i]));
+                    }
+                }
+                ss = warp_sum_double(ss);
+                if (lane == 0) red[warp] = ss;
+                consumer_sync();
+                double t = 0.0;
+                for (int w = 0; w < kWarps; ++w) t += red[w];
+                const float mean = static_cast<float>(t / static_cast<double>(p.cols));
+                const float scale = 1.0f / sqrtf(mean + p.eps);
+#pragma unroll
+                for (int sl = 0; sl < kSlabMax; ++sl) {
+                    const int b = sl * kWarps + warp;
+                    if (sl < n_slabs && b < nsb) {
+                        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(p.norm + b * kQK + lane * 8));
+                        const float4 w1 = __ldg(reinterpret_cast<const float4 *>(p.norm + b * kQK + lane * 8 + 4));
+                        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[sl][i] = __fmul_rn(__fmul_rn(v[sl][i], scale), wv[i]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int sl = 0; sl < kSlabMax; ++sl) {
+                const int b = sl * kWarps + warp;
+                if (sl < n_slabs && b < nsb) quantize_block(v[sl], a, p.cols, nsb, e, b, lane);
+            }
+            consumer_sync();  // red[] is reused by the next vector
+        } else {
+            // wider rows: two passes over x
+            float scale = 1.0f;
+            if (p.norm != nullptr) {
+                double ss = 0.0;
+#pragma unroll 4
+                for (int i = threadIdx.x; i < p.cols; i += kThreads) {
+                    const float xv = x[i];
+                    ss += static_cast<double>(__fmul_rn(xv, xv));
+                }
+                ss = warp_sum_double(ss);
+                if (lane == 0) red[warp] = ss;
+                consumer_sync();
+                double t = 0.0;
+                for (int w = 0; w < kWarps; ++w) t += red[w];
+                const float mean = static_cast<float>(t / static_cast<double>(p.cols));
+                scale = 1.0f / sqrtf(mean + p.eps);
+                consumer_sync();
+            }
+            for (int b = warp; b < nsb; b += kWarps) {
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float xv = x[b * kQK + lane * 8 + i];
+                    v[i] = p.norm != nullptr ? __fmul_rn(__fmul_rn(xv, scale), p.norm[b * kQK + lane * 8 + i]) : xv;
+                }
+                quantize_block(v, a, p.cols, nsb, e, b, lane);
+            }
+            consumer_sync();
+        }
+    }
+}
+
+// Scales and mins of sub-blocks 2*part and 2*part+1 from the packed words
+// (bytes 4..15 of a block), branch-free: words of the 6-bit values of
+// sub-blocks 0-3 and 4-7, then the two bytes of this pair.
+__device__ __forceinline__ void pair_scales(uint32_t s0, uint32_t s1, uint32_t s2, int part, int &sc0,
+                                            int &sc1, int &m0, int &m1) {
+    const uint32_t sc_lo = s0 & 0x3F3F3F3Fu, mn_lo = s1 & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (s2 & 0x0F0F0F0Fu) | (((s0 >> 6) & 0x03030303u) << 4);
+    const uint32_t mn_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | (((s1 >> 6) & 0x03030303u) << 4);
+    const uint32_t scw = part < 2 ? sc_lo : sc_hi, mnw = part < 2 ? mn_lo : mn_hi;
+    const int sh = 16 * (part & 1);
+    sc0 = static_cast<int>((scw >> sh) & 0xFFu);
+    sc1 = static_cast<int>((scw >> (sh + 8)) & 0xFFu);
+    m0 = static_cast<int>((mnw >> sh) & 0xFFu);
+    m1 = static_cast<int>((mnw >> (sh + 8)) & 0xFFu);
+}
+
+// Q8_K activations of one (block, sub-block pair) column, held in registers.
+struct ActPart {
+    int lo[8], hi[8];  // 32 + 32 int8, four per word
+    int s0, s1;        // sums over the two sub-blocks
+    float d;
 };
 
-__device__ __forceinline__ void load_part(BlockPart &b, const uint8_t *blk, int part) {
-    b.hdr = ld_stream(blk);
-    b.q0 = ld_stream(blk + 16 + 32 * part);
-    b.q1 = ld_stream(blk + 32 + 32 * part);
+__device__ __forceinline__ void load_act(ActPart &x, const Q8View &a, int cols, int nsb, int sb, int part,
+                                         int e) {
+    const int4 *ap = reinterpret_cast<const int4 *>(a.q + static_cast<size_t>(e) * cols + sb * kQK + 64 * part);
+    const int4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
+    x.lo[0] = a0.x; x.lo[1] = a0.y; x.lo[2] = a0.z; x.lo[3] = a0.w;
+    x.lo[4] = a1.x; x.lo[5] = a1.y; x.lo[6] = a1.z; x.lo[7] = a1.w;
+    x.hi[0] = a2.x; x.hi[1] = a2.y; x.hi[2] = a2.z; x.hi[3] = a2.w;
+    x.hi[4] = a3.x; x.hi[5] = a3.y; x.hi[6] = a3.z; x.hi[7] = a3.w;
+    const int2 ss = *reinterpret_cast<const int2 *>(a.s + (e * nsb + sb) * 8 + 2 * part);
+    x.s0 = ss.x;
+    x.s1 = ss.y;
+    x.d = a.d[e * nsb + sb];
 }
 
-// Partial dot product of one block part with activation vector e.
-__device__ __forceinline__ float dot_part(const BlockPart &b, const Q8View &a, int cols, int nsb,
-                                          int sb, int part, int e) {
-    const uint32_t h0 = static_cast<uint32_t>(b.hdr.x);
-    const float d4 = half_bits(h0);
-    const float dm4 = half_bits(h0 >> 16);
-    int sc0, m0, sc1, m1;
-    const uint32_t s0 = b.hdr.y, s1 = b.hdr.z, s2 = b.hdr.w;
-    scale_min(s0, s1, s2, 2 * part, sc0, m0);
-    scale_min(s0, s1, s2, 2 * part + 1, sc1, m1);
-    const int4 *ap = reinterpret_cast<const int4 *>(a.q + static_cast<size_t>(e) * cols + sb * kQK +
-                                                    64 * part);
-    const int4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
-    const uint32_t qw[8] = {(uint32_t)b.q0.x, (uint32_t)b.q0.y, (uint32_t)b.q0.z, (uint32_t)b.q0.w,
-                            (uint32_t)b.q1.x, (uint32_t)b.q1.y, (uint32_t)b.q1.z, (uint32_t)b.q1.w};
-    const int alo[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const int ahi[8] = {a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
+// (d4 d8) * sum(sc * q4 . q8) - (dmin4 d8) * sum(m * bsum) of one block part.
+__device__ __forceinline__ float dot_act(const unsigned char *blk, int part, const ActPart &x) {
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * part);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * part);
+    int sc0, sc1, m0, m1;
+    pair_scales(hdr.y, hdr.z, hdr.w, part, sc0, sc1, m0, m1);
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     int sum0 = 0, sum1 = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        sum0 = __dp4a(static_cast<int>(qw[k] & 0x0F0F0F0Fu), alo[k], sum0);
-        sum1 = __dp4a(static_cast<int>((qw[k] >> 4) & 0x0F0F0F0Fu), ahi[k], sum1);
+        sum0 = __dp4a(static_cast<int>(qw[k] & 0x0F0F0F0Fu), x.lo[k], sum0);
+        sum1 = __dp4a(static_cast<int>((qw[k] >> 4) & 0x0F0F0F0Fu), x.hi[k], sum1);
     }
     const int isum = sc0 * sum0 + sc1 * sum1;
-    const int32_t *ss = a.s + (e * nsb + sb) * 8 + 2 * part;
-    const int msum = m0 * ss[0] + m1 * ss[1];
-    const float d8 = a.d[e * nsb + sb];
-    return __fmul_rn(d4, d8) * static_cast<float>(isum) - __fmul_rn(dm4, d8) * static_cast<float>(msum);
+    const int msum = m0 * x.s0 + m1 * x.s1;
+    return __fmul_rn(half_bits(hdr.x), x.d) * static_cast<float>(isum) -
+           __fmul_rn(half_bits(hdr.x >> 16), x.d) * static_cast<float>(msum);
 }
 
-// TPR threads per weight row (8 or 32); NB activation vectors (1 or kMaxVec).
-template <int TPR, int MODE, int NB>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvParams p) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    constexpr int kRowsPerWarp = 32 / TPR;
-    constexpr int kRows = kWarps * kRowsPerWarp;
-    constexpr int kStep = TPR / 4;  // blocks per row per iteration
+// One CTA streams its p.rows_per_cta contiguous weight rows (of each matrix)
+// through a kStages-deep ring of bulk copies into shared memory, issued by a
+// producer warp: the first stages before waiting for the previous kernel,
+// the rest as stages are released.  Dependents are released at once, so
+// consecutive projections overlap their weight streams with each other's
+// activation prologue and tail.  Each of the kWarps consumer warps owns whole
+// rows, four at a time, 8 lanes per row; a lane's items are independent
+// dot products kept in four accumulators (the latency of one Q4_K x Q8_K
+// item is the limit at batch 1, not bandwidth); the row sum is a fixed-order
+// shuffle reduction (deterministic), and the row's stage slot is released by
+// one arrival on the stage's "empty" barrier -- no CTA-wide barrier in the
+// loop.  NB activation vectors (1 or kMaxVec).
+template <int MODE, int NB>
+__global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
     constexpr int kMats = MODE == kSwiglu ? 2 : 1;
     const int nsb = p.cols / kQK;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int local_row = warp * kRowsPerWarp + lane / TPR;
-    const int row = blockIdx.x * kRows + local_row;
-    const int t = lane % TPR;
-    const int sb0 = t >> 2, part = t & 3;
-    const bool ok = row < p.rows;
-    int m = 0, row_in = row;
+    const int row_bytes = nsb * kQ4Bytes;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool producer = warp == kWarps;
+    const int row0 = blockIdx.x * p.rows_per_cta;
+    const int nrows = max(0, min(p.rows, row0 + p.rows_per_cta) - row0);
+    const int R = p.chunk_rows;
+    const int n_chunks = (nrows + R - 1) / R;
+    unsigned char *ring = smem;
+    const uint32_t full0 = smem_u32(smem + kRingBytes);
+    const uint32_t empty0 = full0 + 8 * kStages;
+    int m = 0, mrow0 = row0;
     if (MODE == kQkv) {
-        m = row < p.row_end[0] ? 0 : (row < p.row_end[1] ? 1 : 2);
-        row_in = row - (m == 0 ? 0 : p.row_end[m - 1]);
+        m = row0 < p.row_end[0] ? 0 : (row0 < p.row_end[1] ? 1 : 2);
+        mrow0 = row0 - (m == 0 ? 0 : p.row_end[m - 1]);
     }
-    const size_t row_bytes = static_cast<size_t>(nsb) * kQ4Bytes;
-    const uint8_t *wr[kMats];
-#pragma unroll
-    for (int k = 0; k < kMats; ++k) {
-        wr[k] = ok ? p.w[MODE == kSwiglu ? k : m] + static_cast<size_t>(row_in) * row_bytes : nullptr;
-    }
-
-    // Weights do not depend on the previous kernel: start streaming them
-    // before waiting for it.
-    BlockPart cur[2][kMats], nxt[2][kMats];
-    auto load2 = [&](int base, BlockPart (&buf)[2][kMats]) {
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int sb = base + u * kStep;
-            if (ok && sb < nsb) {
-#pragma unroll
-                for (int k = 0; k < kMats; ++k) load_part(buf[u][k], wr[k] + sb * kQ4Bytes, part);
-            }
+    if (tid == 0) {
+        for (int st = 0; st < kStages; ++st) {
+            mbar_init(full0 + 8 * st, 1);
+            mbar_init(empty0 + 8 * st, static_cast<uint32_t>(R));
         }
-    };
-    load2(sb0, cur);
-
-    pdl_wait();
-    const Q8View a = carve_q8(smem, p.n, p.cols);
-    quantize_activations(p, a);
-
-    float acc[kMats][NB];
-#pragma unroll
-    for (int k = 0; k < kMats; ++k)
-#pragma unroll
-        for (int e = 0; e < NB; ++e) acc[k][e] = 0.0f;
-
-    for (int base = sb0; base < nsb; base += 2 * kStep) {
-        if (base + 2 * kStep < nsb) load2(base + 2 * kStep, nxt);
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int sb = base + u * kStep;
-            if (ok && sb < nsb) {
-#pragma unroll
-                for (int k = 0; k < kMats; ++k)
-#pragma unroll
-                    for (int e = 0; e < NB; ++e)
-                        if (e < p.n) acc[k][e] += dot_part(cur[u][k], a, p.cols, nsb, sb, part, e);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-            for (int k = 0; k < kMats; ++k) cur[u][k] = nxt[u][k];
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    __syncthreads();
+    // Weights never depend on earlier kernels: the next kernel may start its
+    // own weight stream now.
     pdl_trigger();
 
-#pragma unroll
-    for (int k = 0; k < kMats; ++k)
-#pragma unroll
-        for (int e = 0; e < NB; ++e)
-#pragma unroll
-            for (int off = TPR / 2; off > 0; off >>= 1)
-                acc[k][e] += __shfl_xor_sync(0xffffffffu, acc[k][e], off);
+    unsigned char *after_ring = smem + kRingBytes + kBarBytes;
+    const Q8View a = carve_q8(after_ring, p.n, p.cols);
+    float *res = reinterpret_cast<float *>(after_ring + q8_smem_bytes(p.n, p.cols));  // kQkv [NB][32]
+    bool bad = false;
 
-    if (MODE == kPlain) {
-        if (ok && t == 0) {
+    if (producer) {
+        if (lane == 0) {
+            const uint64_t policy = evict_first_policy();
+            const uint8_t *wbase[kMats];
 #pragma unroll
-            for (int e = 0; e < NB; ++e) {
-                if (e < p.n) {
-                    const size_t o = static_cast<size_t>(e) * p.rows + row;
-                    p.y[0][o] = p.residual != nullptr ? p.residual[o] + acc[0][e] : acc[0][e];
-                }
+            for (int k = 0; k < kMats; ++k) {
+                wbase[k] = p.w[MODE == kSwiglu ? k : m] + static_cast<size_t>(mrow0) * row_bytes;
             }
-        }
-    } else if (MODE == kSwiglu) {
-        if (ok && t == 0) {
-#pragma unroll
-            for (int e = 0; e < NB; ++e) {
-                if (e < p.n) {
-                    const float g = acc[0][e];
-                    const float s = g / (1.0f + expf(-g));
-                    p.y[0][static_cast<size_t>(e) * p.rows + row] = s * acc[1][e];
+            int issued = 0;
+            for (int c = 0; c < n_chunks; ++c) {
+                if (c >= kStages) {  // wait until every row of chunk c - kStages is done
+                    const int prev = c - kStages;
+                    if (!mbar_wait_bounded(empty0 + 8 * (prev % kStages),
+                                           static_cast<uint32_t>((prev / kStages) & 1))) {
+                        if (p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
+                            p.err->where = HKV_KERNEL_GEMV;
+                            p.err->a = blockIdx.x;
+                            p.err->b = c;
+                        }
+                        break;
+                    }
                 }
+                const int r0 = c * R;
+                const uint32_t bytes = static_cast<uint32_t>(min(R, nrows - r0) * row_bytes);
+                const uint32_t stage = smem_u32(ring + (c % kStages) * kStageBytes);
+                const uint32_t bar = full0 + 8 * (c % kStages);
+                mbar_arrive_expect_tx(bar, bytes * kMats);
+#pragma unroll
+                for (int k = 0; k < kMats; ++k) {
+                    bulk_load(stage + k * R * row_bytes, wbase[k] + static_cast<size_t>(r0) * row_bytes,
+                              bytes, bar, policy);
+                }
+                issued = c + 1;
+            }
+            // the CTA must not exit with copies in flight: wait (bounded) for
+            // the last copy issued into each stage
+            for (int c = max(0, issued - kStages); c < issued; ++c) {
+                mbar_wait_bounded(full0 + 8 * (c % kStages), static_cast<uint32_t>((c / kStages) & 1));
             }
         }
     } else {
-        // q / k / v rows; the 4 CTAs of a cluster hold the 128 rows of one head.
-        float *res = reinterpret_cast<float *>(smem + q8_smem_bytes(p.n, p.cols));  // [NB][kRows]
-        double *part_ss = reinterpret_cast<double *>(res + NB * kRows);             // [NB]
-        if (t == 0) {
+        pdl_wait();  // x (and y, residual) belong to the kernels before
+        quantize_activations(p, a, a.red);
+        // 8 lanes per row: lane group q = lane / 8 of warp w takes CTA rows
+        // 4w + q, 4w + q + 32, ...; within a row, lane l8 = lane % 8 takes
+        // items l8, l8 + 8, ... with four independent accumulators.
+        const int items = nsb * 4;
+        const int qg = lane >> 3, l8 = lane & 7;
+        for (int base = 0; base < nrows && !bad; base += 4 * kWarps) {
+            const int r = base + 4 * warp + qg;
+            const bool has_row = r < nrows;
+            const int c = has_row ? r / R : 0, rs = has_row ? r % R : 0;
+            const uint32_t full = full0 + 8 * (c % kStages);
+            const bool ok = !has_row || mbar_wait_bounded(full, static_cast<uint32_t>((c / kStages) & 1));
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
+                    p.err->where = HKV_KERNEL_GEMV;
+                    p.err->a = blockIdx.x;
+                    p.err->b = c;
+                }
+                bad = true;
+                break;
+            }
+            const unsigned char *stage = ring + (c % kStages) * kStageBytes;
+            float acc[kMats][NB][4];
 #pragma unroll
-            for (int e = 0; e < NB; ++e)
-                if (e < p.n) res[e * kRows + local_row] = acc[0][e];
+            for (int k = 0; k < kMats; ++k)
+#pragma unroll
+                for (int e = 0; e < NB; ++e)
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) acc[k][e][u] = 0.0f;
+            if (has_row) {
+                for (int j0 = l8; j0 < items; j0 += 32) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = j0 + 8 * u;
+                        if (j < items) {
+                            const int sb = j >> 2, part = j & 3;
+#pragma unroll
+                            for (int e = 0; e < NB; ++e) {
+                                if (e < p.n) {
+                                    ActPart ax;
+                                    load_act(ax, a, p.cols, nsb, sb, part, e);
+#pragma unroll
+                                    for (int k = 0; k < kMats; ++k) {
+                                        acc[k][e][u] += dot_act(stage + (k * R + rs) * row_bytes + sb * kQ4Bytes,
+                                                                part, ax);
+                                    }
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (has_row && l8 == 0) mbar_arrive(empty0 + 8 * (c % kStages));  // the row's bytes are read
+            float t[kMats][NB];
+#pragma unroll
+            for (int k = 0; k < kMats; ++k)
+#pragma unroll
+                for (int e = 0; e < NB; ++e) {
+                    float v = (acc[k][e][0] + acc[k][e][1]) + (acc[k][e][2] + acc[k][e][3]);
+#pragma unroll
+                    for (int off = 4; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                    t[k][e] = v;
+                }
+            if (has_row && l8 == 0) {
+                const int grow = row0 + r;
+#pragma unroll
+                for (int e = 0; e < NB; ++e) {
+                    if (e >= p.n) continue;
+                    if (MODE == kPlain) {
+                        const size_t o = static_cast<size_t>(e) * p.rows + grow;
+                        p.y[0][o] = p.residual != nullptr ? p.residual[o] + t[0][e] : t[0][e];
+                    } else if (MODE == kSwiglu) {
+                        const float g = t[0][e];
+                        const float sl = g / (1.0f + expf(-g));
+                        p.y[0][static_cast<size_t>(e) * p.rows + grow] = sl * t[kMats - 1][e];
+                    } else {
+                        res[e * kQkvRows + r] = t[0][e];
+                    }
+                }
+            }
         }
-        __syncthreads();
+    }
+
+    if (MODE == kQkv) {
+        // q / k / v rows; the 4 CTAs of a cluster hold the 128 rows of one
+        // head.  Every thread of every CTA takes the barriers, even after a
+        // timeout.
+        bad = __syncthreads_or(bad) != 0;
+        double *part_ss = reinterpret_cast<double *>(res + NB * kQkvRows);  // [NB]
         cg::cluster_group cl = cg::this_cluster();
         const bool normed = m < 2;  // the same for every CTA of the cluster
         if (normed && warp == 0) {
             for (int e = 0; e < p.n; ++e) {
-                const float v = res[e * kRows + lane];
-                const double s = warp_sum_double(static_cast<double>(__fmul_rn(v, v)));
-                if (lane == 0) part_ss[e] = s;
+                const float v = bad ? 0.0f : res[e * kQkvRows + lane];
+                const double ss = warp_sum_double(static_cast<double>(__fmul_rn(v, v)));
+                if (lane == 0) part_ss[e] = ss;
             }
         }
         cl.sync();
         __shared__ float scale_s[NB];
-        if (normed && threadIdx.x < p.n) {
-            const int e = threadIdx.x;
+        if (normed && tid < p.n) {
             double total = 0.0;
-            for (int r = 0; r < kClusterCtas; ++r) total += *cl.map_shared_rank(part_ss + e, r);
+            for (int r = 0; r < kClusterCtas; ++r) total += *cl.map_shared_rank(part_ss + tid, r);
             const float mean = static_cast<float>(total / static_cast<double>(kHeadDim));
-            scale_s[e] = 1.0f / sqrtf(mean + p.eps);
+            scale_s[tid] = 1.0f / sqrtf(mean + p.eps);
         }
         cl.sync();  // every CTA has read its peers' sums before any of them exits
-        const int dim0 = static_cast<int>(cl.block_rank()) * kRows;
-        const int row0 = blockIdx.x * kRows;
-        const int mrow0 = row0 - (m == 0 ? 0 : p.row_end[m - 1]);
-        for (int i = threadIdx.x; i < p.n * kRows; i += kThreads) {
-            const int e = i / kRows, r = i % kRows;
-            if (row0 + r < p.rows) {
-                float v = res[e * kRows + r];
-                if (normed) v = __fmul_rn(__fmul_rn(v, scale_s[e]), p.head_norm[m][dim0 + r]);
-                p.y[m][static_cast<size_t>(e) * p.y_rows[m] + mrow0 + r] = v;
+        if (!bad) {
+            const int dim0 = static_cast<int>(cl.block_rank()) * kQkvRows;
+            for (int i = tid; i < p.n * kQkvRows; i += kThreads + 32) {
+                const int e = i / kQkvRows, r = i % kQkvRows;
+                if (r < nrows) {
+                    float v = res[e * kQkvRows + r];
+                    if (normed) v = __fmul_rn(__fmul_rn(v, scale_s[e]), p.head_norm[m][dim0 + r]);
+                    p.y[m][static_cast<size_t>(e) * p.y_rows[m] + mrow0 + r] = v;
+                }
             }
         }
     }
@@ -515,45 +721,41 @@ __global__ void q4k_quantize_kernel(const float *w, int64_t n_blocks, uint8_t *o
 // ----------------------------------------------------------- embeddings
 // out[e] = sum over j < k of row ids[e*k + j] of a Q4_K table (+ j * stride),
 // decoded like GGML's dequantize_row_q4_K (d*sc and dmin*m rounded first),
-// summed in j order (the reference's chain of ggml_add, :2919-2924).
-__global__ void embed_kernel(const uint8_t *table, int64_t table_rows, int32_t cols,
-                             const int32_t *ids, int32_t k, int32_t id_stride, int32_t n,
-                             float *out, DeviceError *err) {
+// summed in j order (the reference's chain of ggml_add, :2919-2924).  One CTA
+// per (256-column block, entry), one thread per column.
+__global__ void __launch_bounds__(kQK) embed_kernel(const uint8_t *table, int64_t table_rows,
+                                                     int32_t cols, const int32_t *ids, int32_t k,
+                                                     int32_t id_stride, int32_t n, float *out,
+                                                     DeviceError *err) {
     pdl_wait();
-    const int e = blockIdx.x;
-    if (e >= n) return;
+    const int sb = blockIdx.x, e = blockIdx.y;
     const int nsb = cols / kQK;
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) {
-        const int sb = i / kQK, pos = i % kQK;
-        const int pair = pos >> 6, hi = (pos >> 5) & 1, l = pos & 31;
-        float acc = 0.0f;
-        for (int j = 0; j < k; ++j) {
-            const int32_t code = ids[e * k + j];
-            const int64_t id = static_cast<int64_t>(code) + static_cast<int64_t>(j) * id_stride;
-            if (code < 0 || (k > 1 && code >= id_stride) || id >= table_rows) {
-                if (atomicCAS(&err->code, 0, kErrBadIndex) == 0) {
-                    err->where = HKV_KERNEL_EMBED;
-                    err->a = e;
-                    err->b = static_cast<int32_t>(id);
-                }
-                continue;
+    if (e >= n || sb >= nsb) return;
+    const int pos = threadIdx.x;
+    const int pair = pos >> 6, hi = (pos >> 5) & 1, l = pos & 31;
+    float acc = 0.0f;
+    for (int j = 0; j < k; ++j) {
+        const int32_t code = ids[e * k + j];
+        const int64_t id = static_cast<int64_t>(code) + static_cast<int64_t>(j) * id_stride;
+        if (code < 0 || (k > 1 && code >= id_stride) || id >= table_rows) {
+            if (pos == 0 && atomicCAS(&err->code, 0, kErrBadIndex) == 0) {
+                err->where = HKV_KERNEL_EMBED;
+                err->a = e;
+                err->b = static_cast<int32_t>(id);
             }
-            const uint8_t *blk = table + (id * nsb + sb) * kQ4Bytes;
-            uint16_t dbits, mbits;
-            memcpy(&dbits, blk, 2);
-            memcpy(&mbits, blk + 2, 2);
-            const float d = __half2float(__ushort_as_half(dbits));
-            const float dmin = __half2float(__ushort_as_half(mbits));
-            int sc, m;
-            const uint32_t *sw = reinterpret_cast<const uint32_t *>(blk + 4);
-            scale_min(sw[0], sw[1], sw[2], 2 * pair + hi, sc, m);
-            const uint32_t q = (blk[16 + 32 * pair + l] >> (4 * hi)) & 0x0Fu;
-            const float v = __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q)),
-                                      __fmul_rn(dmin, static_cast<float>(m)));
-            acc = j == 0 ? v : __fadd_rn(acc, v);
+            continue;
         }
-        out[static_cast<size_t>(e) * cols + i] = acc;
+        const uint8_t *blk = table + (id * nsb + sb) * kQ4Bytes;
+        const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+        const float d = half_bits(hdr.x), dmin = half_bits(hdr.x >> 16);
+        int sc, m;
+        scale_min(hdr.y, hdr.z, hdr.w, 2 * pair + hi, sc, m);
+        const uint32_t q = (blk[16 + 32 * pair + l] >> (4 * hi)) & 0x0Fu;
+        const float v = __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q)),
+                                  __fmul_rn(dmin, static_cast<float>(m)));
+        acc = j == 0 ? v : __fadd_rn(acc, v);
     }
+    out[static_cast<size_t>(e) * cols + sb * kQK + pos] = acc;
 }
 
 // codes[e][c] = the first index of the largest of logits[e][c*size .. +size).
@@ -585,21 +787,47 @@ __global__ void argmax_kernel(const float *logits, int32_t n_books, int32_t size
 }
 
 // ------------------------------------------------------------- launchers
-size_t gemv_smem(int mode, int nb, int n, int cols, int tpr) {
-    size_t b = q8_smem_bytes(n, cols);
-    if (mode == kQkv) {
-        const int rows = kWarps * (32 / tpr);
-        b += static_cast<size_t>(nb) * rows * sizeof(float) + static_cast<size_t>(nb) * sizeof(double) + 16;
-    }
+size_t gemv_smem(int mode, int nb, int n, int cols, int chunk_rows) {
+    (void)chunk_rows;
+    size_t b = kRingBytes + kBarBytes + q8_smem_bytes(n, cols);
+    if (mode == kQkv) b += static_cast<size_t>(nb) * kQkvRows * sizeof(float) + nb * sizeof(double) + 16;
     return b;
 }
 
-template <int TPR, int MODE, int NB>
+// Dynamic shared memory a launch may use on `dev` (the opt-in maximum less
+// room for the kernel's static shared memory).
+int smem_cap_of(int dev) {
+    static std::mutex mu;
+    static int cap[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) return 227 * 1024 - 1024;
+    if (cap[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0) {
+            v = 227 * 1024;
+        }
+        cap[dev] = v - 1024;
+    }
+    return cap[dev];
+}
+
+int num_sms_of(int dev) {
+    static std::mutex mu;
+    static int sms[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) return 148;
+    if (sms[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        sms[dev] = v;
+    }
+    return sms[dev];
+}
+
+template <int MODE, int NB>
 cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
-    constexpr int kRows = kWarps * (32 / TPR);
-    auto kern = gemv_kernel<TPR, MODE, NB>;
-    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, TPR);
-    // Opt in to the largest dynamic shared memory once per device.
+    auto kern = gemv_kernel<MODE, NB>;
+    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.chunk_rows);
     static std::mutex mu;
     static bool done[64] = {};
     int dev = 0;
@@ -608,15 +836,14 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     {
         std::lock_guard<std::mutex> lock(mu);
         if (dev < 64 && !done[dev]) {
-            st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(q8_smem_bytes(kMaxVec, kMaxCols) + 64 * 1024));
+            st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_cap_of(dev));
             if (st != cudaSuccess) return st;
             done[dev] = true;
         }
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((p.rows + kRows - 1) / kRows));
-    cfg.blockDim = dim3(kThreads);
+    cfg.gridDim = dim3(static_cast<unsigned>((p.rows + p.rows_per_cta - 1) / p.rows_per_cta));
+    cfg.blockDim = dim3(kThreads + 32);  // kWarps consumer warps + one producer warp
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -635,30 +862,41 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+// Ring plan: CTAs of rows_per_cta contiguous rows (one per SM; 32 for q/k/v,
+// a quarter head each), stages of as many whole rows as fit kStageBytes.
+void plan_rows(GemvParams &p, int mode, int dev) {
+    const int mats = mode == kSwiglu ? 2 : 1;
+    const int row_bytes = p.cols / kQK * kQ4Bytes;
+    if (mode == kQkv) {
+        p.rows_per_cta = kQkvRows;
+    } else {
+        const int sms = num_sms_of(dev);
+        p.rows_per_cta = std::max(1, (p.rows + sms - 1) / sms);
+    }
+    p.chunk_rows = std::max(1, std::min(p.rows_per_cta, kStageBytes / (row_bytes * mats)));
+}
+
 template <int MODE>
 cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
-    // Chunks of at most kMaxVec vectors; one vector takes the NB = 1 kernel.
+    int dev = 0;
+    cudaError_t st = cudaGetDevice(&dev);
+    if (st != cudaSuccess) return st;
+    plan_rows(p, MODE, dev);
+    // vectors per launch: at most kMaxVec, and as many as shared memory holds
+    int vmax = kMaxVec;
+    const size_t cap = static_cast<size_t>(smem_cap_of(dev));
+    while (vmax > 1 && gemv_smem(MODE, kMaxVec, vmax, p.cols, p.chunk_rows) > cap) --vmax;
+    if (gemv_smem(MODE, 1, 1, p.cols, p.chunk_rows) > cap) return cudaErrorInvalidValue;
     const int n_total = p.n;
-    for (int e0 = 0; e0 < n_total; e0 += kMaxVec) {
+    for (int e0 = 0; e0 < n_total; e0 += vmax) {
         GemvParams q = p;
-        q.n = std::min(kMaxVec, n_total - e0);
+        q.n = std::min(vmax, n_total - e0);
         q.x = p.x + static_cast<size_t>(e0) * p.cols;
         if (q.residual) q.residual += static_cast<size_t>(e0) * p.rows;
         for (int k = 0; k < 3; ++k) {
             if (q.y[k]) q.y[k] += static_cast<size_t>(e0) * (MODE == kQkv ? p.y_rows[k] : p.rows);
         }
-        cudaError_t st;
-        // Rows per CTA: 32 (8 threads per row) for tall matrices, 8 (a warp per
-        // row) when 32-row CTAs would leave SMs idle.
-        const bool tall = MODE == kQkv || p.rows >= 4096;
-        if (q.n == 1) {
-            st = tall ? launch_one<8, MODE, 1>(q, stream)
-                      : (MODE == kQkv ? cudaErrorInvalidValue : launch_one<32, MODE == kQkv ? kPlain : MODE, 1>(q, stream));
-        } else {
-            st = tall ? launch_one<8, MODE, kMaxVec>(q, stream)
-                      : (MODE == kQkv ? cudaErrorInvalidValue
-                                      : launch_one<32, MODE == kQkv ? kPlain : MODE, kMaxVec>(q, stream));
-        }
+        st = q.n == 1 ? launch_one<MODE, 1>(q, stream) : launch_one<MODE, kMaxVec>(q, stream);
         if (st != cudaSuccess) return st;
     }
     return cudaSuccess;
@@ -828,8 +1066,8 @@ cudaError_t launch_embed(const uint8_t *table, int64_t table_rows, int32_t cols,
                          int32_t k, int32_t id_stride, int32_t n, float *out, DeviceError *err,
                          cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(n));
-    cfg.blockDim = dim3(kThreads);
+    cfg.gridDim = dim3(static_cast<unsigned>(cols / kQK), static_cast<unsigned>(n));
+    cfg.blockDim = dim3(kQK);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -914,8 +1152,10 @@ void free_buffers(hkv_backbone *bb) {
 }
 
 GemvParams plain_params(const void *w, int32_t rows, int32_t cols, int32_t n, const float *x,
-                        const float *norm, float eps, const float *residual, float *y) {
+                        const float *norm, float eps, const float *residual, float *y,
+                        hkv::DeviceError *err) {
     GemvParams p = {};
+    p.err = err;
     p.w[0] = static_cast<const uint8_t *>(w);
     p.rows = rows;
     p.row_end[0] = p.row_end[1] = p.row_end[2] = rows;
@@ -1097,6 +1337,7 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
         p.y_rows[1] = p.y_rows[2] = bb->kv_rows;
         p.head_norm[0] = L.attn_q_norm;
         p.head_norm[1] = L.attn_k_norm;
+        p.err = bb->err;
         int st = bb_cuda(bb, launch_gemv<kQkv>(p, s), "hkv_backbone_decode: q/k/v");
         if (st != HKV_OK) return st;
         // RoPE + append + attention (:5734-5786)
@@ -1106,18 +1347,18 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
         }
         // h = h + Wo attn (:5790-5791)
         st = bb_cuda(bb, launch_gemv<kPlain>(plain_params(L.attn_output, w.hidden, bb->q_rows, n, bb->attn,
-                                                          nullptr, eps, bb->hidden, bb->hidden), s),
+                                                          nullptr, eps, bb->hidden, bb->hidden, bb->err), s),
                      "hkv_backbone_decode: o_proj");
         if (st != HKV_OK) return st;
         // g = silu(Wg m) * (Wu m), m = rms_norm(h) * ffn_norm (:5806-5822)
         GemvParams f = plain_params(L.ffn_gate, w.ffn, w.hidden, n, bb->hidden, L.ffn_norm, eps, nullptr,
-                                    bb->gated);
+                                    bb->gated, bb->err);
         f.w[1] = static_cast<const uint8_t *>(L.ffn_up);
         st = bb_cuda(bb, launch_gemv<kSwiglu>(f, s), "hkv_backbone_decode: gate/up");
         if (st != HKV_OK) return st;
         // h = h + Wd g (:5823, :5843)
         st = bb_cuda(bb, launch_gemv<kPlain>(plain_params(L.ffn_down, w.hidden, w.ffn, n, bb->gated, nullptr,
-                                                          eps, bb->hidden, bb->hidden), s),
+                                                          eps, bb->hidden, bb->hidden, bb->err), s),
                      "hkv_backbone_decode: down");
         if (st != HKV_OK) return st;
     }
@@ -1129,7 +1370,7 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
         // logits = a.output (rms_norm(h) * output_norm) (:5858-5863), greedy codes
         st = bb_cuda(bb, launch_gemv<kPlain>(plain_params(w.audio_output, bb->logit_rows, w.hidden, n,
                                                           bb->hidden, w.output_norm, eps, nullptr,
-                                                          bb->logits), s),
+                                                          bb->logits, bb->err), s),
                      "hkv_backbone_decode: output head");
         if (st != HKV_OK) return st;
         st = bb_cuda(bb, launch_argmax(bb->logits, w.n_codebooks, w.codebook_size, n, bb->codes, s),
@@ -1157,6 +1398,9 @@ int hkv_backbone_sync_check(hkv_backbone *bb, hkv_stream stream) {
     if (st != HKV_OK) return st;
     if (e.code != 0) {
         cudaMemset(bb->err, 0, sizeof(e));
+        if (e.code == kErrTimeout) {
+            return bb_fail(bb, HKV_ERR_TIMEOUT, "weight copy of CTA %d, stage %d did not complete", e.a, e.b);
+        }
         return bb_fail(bb, HKV_ERR_DEVICE, "embedding id %d of entry %d outside the table", e.b, e.a);
     }
     return HKV_OK;
