@@ -763,9 +763,11 @@ def bench_backbone(args):
     ev1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     ev0.record(stream)
+    h0 = time.perf_counter()
     with torch.cuda.stream(stream):
         for _ in range(args.steps):
             step()
+    host_ms = (time.perf_counter() - h0) * 1e3
     ev1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -849,6 +851,7 @@ def bench_backbone(args):
                          "peak_kind": peak_kind},
             "cpu_baseline": cpu, "clocks": clk, "e2e": e2e,
             "gpu_launches": (3 + 5 * N_LAYERS) * args.steps,
+            "host_enqueue_ms_per_step": host_ms / args.steps,
         }), flush=True)
     bb.close()
     eng.close()

@@ -838,6 +838,12 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
         if (dev < 64 && !done[dev]) {
             st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_cap_of(dev));
             if (st != cudaSuccess) return st;
+            // All of the SM's unified memory as shared memory: a CTA of the
+            // next projection (launched early, see pdl_trigger) then fits
+            // beside one of this kernel and streams its weights meanwhile.
+            st = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared);
+            if (st != cudaSuccess) return st;
             done[dev] = true;
         }
     }
