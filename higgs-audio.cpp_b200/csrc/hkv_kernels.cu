@@ -428,6 +428,114 @@ __device__ __forceinline__ void merge_partials(const float *part_o, const float 
     }
 }
 
+// The same merge with every load of kBatch partials issued before their
+// weighted sums (a merge is a chain of L2 round trips, so the batch size sets
+// its latency); the sums are taken in the same partial order.  Used for the
+// merges of a warp's last segment, after its main loop, where the registers
+// of the loop are free.
+__device__ __forceinline__ void merge_partials_wide(const float *part_o, const float *part_ml, int p0,
+                                               int nparts, int lane, Merged &res) {
+    constexpr int kBatch = 8;  // partial outputs in flight per lane
+    float mx[kGqa];
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        mx[j] = -INFINITY;
+    }
+    // (m, l) of partial lane (kept for the weights: at most 32 partials are
+    // merged at once in practice; more take another pass)
+    float4 ml_a = make_float4(-INFINITY, 0.f, -INFINITY, 0.f), ml_b = ml_a;
+    for (int p = lane; p < nparts; p += 32) {
+        const float4 *pm = reinterpret_cast<const float4 *>(part_ml + static_cast<int64_t>(p0 + p) * (2 * kGqa));
+        const float4 a = __ldcg(pm);
+        const float4 b = __ldcg(pm + 1);
+        if (p == lane) {
+            ml_a = a;
+            ml_b = b;
+        }
+        mx[0] = fmaxf(mx[0], a.x);
+        mx[1] = fmaxf(mx[1], a.z);
+        mx[2] = fmaxf(mx[2], b.x);
+        mx[3] = fmaxf(mx[3], b.z);
+    }
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], off));
+        }
+    }
+    float4 acc[kGqa];
+    float den[kGqa];
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        den[j] = 0.f;
+    }
+    for (int base = 0; base < nparts; base += 32) {
+        // weights of the partials base .. base+31, one per lane
+        float w[kGqa] = {0.f, 0.f, 0.f, 0.f};
+        if (base + lane < nparts) {
+            float4 a = ml_a, b = ml_b;
+            if (base > 0) {
+                const float4 *pm = reinterpret_cast<const float4 *>(
+                    part_ml + static_cast<int64_t>(p0 + base + lane) * (2 * kGqa));
+                a = __ldcg(pm);
+                b = __ldcg(pm + 1);
+            }
+            w[0] = exp2f(a.x - mx[0]);
+            w[1] = exp2f(a.z - mx[1]);
+            w[2] = exp2f(b.x - mx[2]);
+            w[3] = exp2f(b.z - mx[3]);
+            den[0] += w[0] * a.y;
+            den[1] += w[1] * a.w;
+            den[2] += w[2] * b.y;
+            den[3] += w[3] * b.w;
+        }
+        const int cnt = min(32, nparts - base);
+        for (int t0 = 0; t0 < cnt; t0 += kBatch) {
+            // all loads of the batch first, then the weighted sums in order
+            float4 ov[kBatch][kGqa];
+#pragma unroll
+            for (int t = 0; t < kBatch; ++t) {
+                if (t0 + t < cnt) {
+                    const float4 *po = reinterpret_cast<const float4 *>(
+                        part_o + static_cast<int64_t>(p0 + base + t0 + t) * (kGqa * kHeadDim));
+#pragma unroll
+                    for (int j = 0; j < kGqa; ++j) {
+                        ov[t][j] = __ldcg(po + j * (kHeadDim / 4) + lane);
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < kBatch; ++t) {
+                if (t0 + t < cnt) {
+#pragma unroll
+                    for (int j = 0; j < kGqa; ++j) {
+                        const float wt = __shfl_sync(0xffffffffu, w[j], t0 + t);
+                        acc[j].x += wt * ov[t][j].x;
+                        acc[j].y += wt * ov[t][j].y;
+                        acc[j].z += wt * ov[t][j].z;
+                        acc[j].w += wt * ov[t][j].w;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            den[j] += __shfl_xor_sync(0xffffffffu, den[j], off);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        res.o[j] = acc[j];
+        res.m[j] = mx[j];
+        res.l[j] = den[j];
+    }
+}
+
 __device__ __forceinline__ float4 normalised(const Merged &r, int j) {
     const float inv = 1.f / r.l[j];
     return make_float4(r.o[j].x * inv, r.o[j].y * inv, r.o[j].z * inv, r.o[j].w * inv);
@@ -547,7 +655,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
     int seg_e = 0, seg_h = 0, seg_pos = 0, part = 0, nparts = 1, ntok = 0;
 
-    auto flush = [&]() {
+    auto flush = [&](bool after_loop) {
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
 #pragma unroll
@@ -631,7 +739,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             if (ticket == nparts - 1) {
                 __threadfence();
                 Merged res;
-                merge_partials(part_o, part_ml, p_first, nparts, lane, res);
+                if (after_loop) {
+                    merge_partials_wide(part_o, part_ml, p_first, nparts, lane, res);
+                } else {
+                    merge_partials(part_o, part_ml, p_first, nparts, lane, res);
+                }
                 finish(res);
             }
             return;
@@ -650,7 +762,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
         __threadfence();
         Merged grp;
-        merge_partials(part_o, part_ml, p_first + g * gsz, g_size, lane, grp);
+        if (after_loop) {
+            merge_partials_wide(part_o, part_ml, p_first + g * gsz, g_size, lane, grp);
+        } else {
+            merge_partials(part_o, part_ml, p_first + g * gsz, g_size, lane, grp);
+        }
         {
             // the group partial, stored after the level-1 partials
             const int gp = batch.n_parts + g_index;
@@ -678,7 +794,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         if (ticket == n_groups - 1) {
             __threadfence();
             Merged res;
-            merge_partials(part_o, part_ml, batch.n_parts + batch.part2_off[eh], n_groups, lane, res);
+            if (after_loop) {
+                merge_partials_wide(part_o, part_ml, batch.n_parts + batch.part2_off[eh], n_groups, lane, res);
+            } else {
+                merge_partials(part_o, part_ml, batch.n_parts + batch.part2_off[eh], n_groups, lane, res);
+            }
             finish(res);
         }
     };
@@ -688,7 +808,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         const uint32_t parity = static_cast<uint32_t>(k / kAttnStages) & 1u;
         if (u == u_begin || cons.i == 0) {
             if (u != u_begin) {
-                flush();
+                flush(false);
             }
             // ---- new (entry, KV head) share: stage RoPE'd q as F16 hi/lo rows
             seg_e = cons.e;
@@ -876,7 +996,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     // Let the next launch in the stream start its prologue while this CTA
     // finishes its tail.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    flush();
+    flush(true);
 }
 
 // ===================================================================== gather
