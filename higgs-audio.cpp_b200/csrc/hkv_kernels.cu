@@ -41,6 +41,11 @@ constexpr int kQcBytes = 8 * kQcStride * 2;        // 8 rows: 4 heads x {hi, lo}
 constexpr int kPBufBytes = 16 * 16;                // 16 tokens x 8 halves
 constexpr int kBarBytes = (kAttnStages * 8 + 15) / 16 * 16;  // one 8-byte mbarrier per stage
 constexpr int kWarpSmem = kAttnStages * kStageBytes + kQcBytes + kPBufBytes + kBarBytes;
+// CTA-level partials: two slots per warp (the run a warp does not start, and
+// the run it starts), each o[4][128] + (m, l)[4]; then one ticket per run.
+constexpr int kCtaPartFloats = kGqa * kHeadDim + 2 * kGqa;
+constexpr int kCtaPartBytes = kCtaPartFloats * 4;
+constexpr int kCtaSmem = kAttnWarps * 2 * kCtaPartBytes + 32;
 constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int kWhereAppend = 0;
 constexpr int kWhereAttn = 1;
@@ -49,7 +54,9 @@ constexpr int kWhereSplitWait = 5;
 
 static_assert(kWarpSmem % 16 == 0, "per-warp shared region must keep 16-byte alignment");
 static_assert(kBarBytes >= 8 * kAttnStages, "every stage needs its mbarrier inside the warp's region");
-static_assert(kAttnWarps * kWarpSmem <= 227 * 1024, "attention CTA exceeds shared memory");
+static_assert(kAttnWarps * kWarpSmem + kCtaSmem <= 227 * 1024, "attention CTA exceeds shared memory");
+static_assert(kCtaPartBytes % 16 == 0, "CTA partial slots must keep 16-byte alignment");
+static_assert(kAttnWarps <= 8, "one run ticket per warp in 32 bytes");
 
 __device__ __forceinline__ void record_error(DeviceError *err, int code, int where, int a, int b) {
     if (atomicCAS(&err->code, 0, code) == 0) {
@@ -536,6 +543,44 @@ __device__ __forceinline__ void merge_partials_wide(const float *part_o, const f
     }
 }
 
+// Merge of the m partials a run of warps left in shared memory (slot of warp
+// k: 1 for the run's first warp, 0 for the others), in warp order.
+__device__ __forceinline__ void merge_cta(const float *slots, int w0, int m, int lane, Merged &res) {
+    auto base = [&](int k) { return slots + (2 * (w0 + k) + (k == 0 ? 1 : 0)) * kCtaPartFloats; };
+    float mx[kGqa];
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        mx[j] = -INFINITY;
+    }
+    for (int k = 0; k < m; ++k) {
+        const float *ml = base(k) + kGqa * kHeadDim;
+#pragma unroll
+        for (int j = 0; j < kGqa; ++j) {
+            mx[j] = fmaxf(mx[j], ml[2 * j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kGqa; ++j) {
+        res.o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        res.l[j] = 0.f;
+        res.m[j] = mx[j];
+    }
+    for (int k = 0; k < m; ++k) {
+        const float *pk = base(k);
+        const float *ml = pk + kGqa * kHeadDim;
+#pragma unroll
+        for (int j = 0; j < kGqa; ++j) {
+            const float w = exp2f(ml[2 * j] - mx[j]);
+            res.l[j] += w * ml[2 * j + 1];
+            const float4 ov = reinterpret_cast<const float4 *>(pk + j * kHeadDim)[lane];
+            res.o[j].x += w * ov.x;
+            res.o[j].y += w * ov.y;
+            res.o[j].z += w * ov.z;
+            res.o[j].w += w * ov.w;
+        }
+    }
+}
+
 __device__ __forceinline__ float4 normalised(const Merged &r, int j) {
     const float inv = 1.f / r.l[j];
     return make_float4(r.o[j].x * inv, r.o[j].y * inv, r.o[j].z * inv, r.o[j].w * inv);
@@ -580,6 +625,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     const int G = pool.n_head_kv;
     const int64_t U = batch.total_units;
     const int64_t W = batch.n_warps;
+    float *cta_slots = reinterpret_cast<float *>(smem + kAttnWarps * kWarpSmem);
+    int *run_ticket = reinterpret_cast<int *>(smem + kAttnWarps * kWarpSmem + kAttnWarps * 2 * kCtaPartBytes);
+    if (threadIdx.x < kAttnWarps) {
+        run_ticket[threadIdx.x] = 0;
+    }
+    __syncthreads();  // the only CTA barrier: before any warp can leave
     if (gw >= W) {
         return;
     }
@@ -654,6 +705,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     uint32_t qb[8][2];
     float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
     int seg_e = 0, seg_h = 0, seg_pos = 0, part = 0, nparts = 1, ntok = 0;
+    int run_w0 = wid, run_m = 1;  // this CTA's warps of the current segment: w0 .. w0 + m - 1
 
     auto flush = [&](bool after_loop) {
 #pragma unroll
@@ -672,7 +724,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         const int ha = (lane & 1) * 2;
         const int d0 = lane >> 2;
         const int n_dst = xchg.n_ranks == 0 ? 1 : xchg.n_ranks;
-        if (nparts == 1) {
+        if (nparts == 1 && run_m == 1) {
             // The whole (slot, KV head) was this warp's: write the output.
             if (!lo_side) {
                 const float ia = 1.f / l_a;
@@ -691,8 +743,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             signal_arrival(xchg, layer, lane);
             return;
         }
+        // This warp's (o, m, l): into its shared-memory slot when other warps
+        // of the CTA share the segment, else straight to the global partial.
+        float *po;
+        float *pm;
+        if (run_m > 1) {
+            po = cta_slots + (2 * wid + (wid == run_w0 ? 1 : 0)) * kCtaPartFloats;
+            pm = po + kGqa * kHeadDim;
+        } else {
+            po = part_o + static_cast<int64_t>(part) * (kGqa * kHeadDim);
+            pm = part_ml + static_cast<int64_t>(part) * (2 * kGqa);
+        }
         if (!lo_side) {
-            float *po = part_o + static_cast<int64_t>(part) * (kGqa * kHeadDim);
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) {
                 po[ha * kHeadDim + 16 * mt + d0] = o[mt][0];
@@ -701,18 +763,58 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 po[(ha + 1) * kHeadDim + 16 * mt + d0 + 8] = o[mt][3];
             }
             if (d0 == 0) {
-                float *pm = part_ml + static_cast<int64_t>(part) * (2 * kGqa);
                 pm[ha * 2] = m_a;
                 pm[ha * 2 + 1] = l_a;
                 pm[ha * 2 + 2] = m_b;
                 pm[ha * 2 + 3] = l_b;
             }
         }
+        const int eh = seg_e * G + seg_h;
+        if (run_m > 1) {
+            __threadfence_block();
+            __syncwarp();
+            int rt = 0;
+            if (lane == 0) {
+                rt = atomicAdd(run_ticket + run_w0, 1);
+            }
+            rt = __shfl_sync(0xffffffffu, rt, 0);
+            if (rt != run_m - 1) {
+                return;  // another warp of the run merges
+            }
+            __threadfence_block();
+            Merged cres;
+            merge_cta(cta_slots, run_w0, run_m, lane, cres);
+            if (nparts == 1) {
+                // the whole segment lived in this CTA: the output
+                for (int r = 0; r < n_dst; ++r) {
+                    float4 *ob = reinterpret_cast<float4 *>(out_slice(out, xchg, r, layer, seg_e, seg_h, G));
+#pragma unroll
+                    for (int j = 0; j < kGqa; ++j) {
+                        ob[j * (kHeadDim / 4) + lane] = normalised(cres, j);
+                    }
+                }
+                signal_arrival(xchg, layer, lane);
+                return;
+            }
+            // the CTA's partial of the segment
+            float4 *gpo = reinterpret_cast<float4 *>(part_o + static_cast<int64_t>(part) * (kGqa * kHeadDim));
+#pragma unroll
+            for (int j = 0; j < kGqa; ++j) {
+                gpo[j * (kHeadDim / 4) + lane] = cres.o[j];
+            }
+            if (lane == 0) {
+                float *gpm = part_ml + static_cast<int64_t>(part) * (2 * kGqa);
+#pragma unroll
+                for (int j = 0; j < kGqa; ++j) {
+                    gpm[2 * j] = cres.m[j];
+                    gpm[2 * j + 1] = cres.l[j];
+                }
+            }
+        }
         // Publish the partial; the last of a group of partials merges the
         // group, and the last group (or the only one) produces the output.
         __threadfence();
         __syncwarp();
-        const int eh = seg_e * G + seg_h;
         const int p_first = batch.part_off[eh];
         const int j_part = part - p_first;
         const int n_groups = merge_groups(nparts);
@@ -817,9 +919,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             ntok = seg_pos + 1;
             {
                 const int64_t a = batch.unit_off[seg_e] + static_cast<int64_t>(seg_h) * cons.np;
+                // partials are per CTA: the warps of one CTA that share the
+                // segment merge theirs in shared memory first
                 const int first = warp_of(a, U, W);
-                nparts = warp_of(a + cons.np - 1, U, W) - first + 1;
-                part = batch.part_off[seg_e * G + seg_h] + (gw - first);
+                const int last = warp_of(a + cons.np - 1, U, W);
+                const int cta = static_cast<int>(blockIdx.x);
+                const int cta_first = first / kAttnWarps;
+                nparts = last / kAttnWarps - cta_first + 1;
+                part = batch.part_off[seg_e * G + seg_h] + (cta - cta_first);
+                const int run_lo = max(first, cta * kAttnWarps);
+                const int run_hi = min(last, cta * kAttnWarps + kAttnWarps - 1);
+                run_w0 = run_lo - cta * kAttnWarps;
+                run_m = run_hi - run_lo + 1;
             }
             const float *cr = rope.cos_tab + static_cast<int64_t>(seg_pos) * (kHeadDim / 2);
             const float *sr = rope.sin_tab + static_cast<int64_t>(seg_pos) * (kHeadDim / 2);
@@ -1033,7 +1144,7 @@ __global__ void gather_kernel(PoolView pool, const int32_t *__restrict__ slot_pa
 
 }  // namespace
 
-size_t attention_smem_bytes() { return static_cast<size_t>(kAttnWarps) * kWarpSmem; }
+size_t attention_smem_bytes() { return static_cast<size_t>(kAttnWarps) * kWarpSmem + kCtaSmem; }
 
 void launch_append(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
                    const float *k, const float *v, bool apply_rope, DeviceError *err,

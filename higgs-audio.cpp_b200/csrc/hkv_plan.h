@@ -8,7 +8,9 @@
 //     share(w) = [floor(w U / W), floor((w + 1) U / W))
 // and the warp holding unit a is warp_of(a) = ceil((a + 1) W / U) - 1.
 // Each (entry, KV head) segment [a, a + np) is covered by warps
-// warp_of(a) .. warp_of(a + np - 1), one partial result each.
+// warp_of(a) .. warp_of(a + np - 1); the warps of one CTA (kAttnWarps
+// consecutive warps) merge theirs in shared memory, so the segment has one
+// partial result per CTA it spans.
 //
 // A segment with more than kMergeSingleMax partials is merged in two levels:
 // groups of merge_group_size() partials are merged by the last warp of each
@@ -84,7 +86,8 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         unit_off[e + 1] = unit_off[e] + np * G;
         for (int32_t h = 0; h < G; ++h) {
             const int64_t a = unit_off[e] + static_cast<int64_t>(h) * np;
-            const int64_t parts = plan_warp_of(a + np - 1, U, W) - plan_warp_of(a, U, W) + 1;
+            const int64_t parts = plan_warp_of(a + np - 1, U, W) / kAttnWarps -
+                                  plan_warp_of(a, U, W) / kAttnWarps + 1;
             part_off[e * G + h + 1] = part_off[e * G + h] + static_cast<int32_t>(parts);
             part2_off[e * G + h + 1] =
                 part2_off[e * G + h] + merge_groups(static_cast<int32_t>(parts));

@@ -7,18 +7,25 @@ exactly once.
 
 Restates the plan's formulas -- W = min(U, grid warps) equal shares
 floor(w U / W) .. floor((w + 1) U / W), warp_of(a) = ceil((a + 1) W / U) - 1,
-part_off from the warps a (slot, KV head) segment touches, warp_entry -- and
-walks every warp the way attention_kernel does, checking that each segment's
-partials are written exactly once and merged exactly once (or written
-directly when one warp holds the whole segment).  Empty shares would break
-this (a segment would count a partial that never arrives), which is why W is
-capped at U.
+part_off from the CTAs (WPC consecutive warps) a (slot, KV head) segment
+touches, warp_entry -- and walks every warp the way attention_kernel does:
+the warps of one CTA that share a segment leave their partials in shared
+memory (slot 1 for the run's first warp, 0 for the others), the last of them
+(run ticket) merges and publishes the CTA's partial.  Checks that every
+shared-memory slot and run ticket is used by one run only, that each
+segment's CTA partials are written exactly once and merged exactly once (or
+the output written directly when one CTA holds the whole segment).  Empty
+shares would break this (a segment would count a partial that never
+arrives), which is why W is capped at U.
 """
 from __future__ import annotations
 
 import random
 
 import pytest
+
+
+WPC = 6  # warps per CTA (kAttnWarps)
 
 
 def plan(npages, G, w_full):
@@ -33,7 +40,7 @@ def plan(npages, G, w_full):
     for e, np_ in enumerate(npages):
         for h in range(G):
             a = unit_off[e] + h * np_
-            part_off.append(part_off[-1] + warp_of(a + np_ - 1) - warp_of(a) + 1)
+            part_off.append(part_off[-1] + warp_of(a + np_ - 1) // WPC - warp_of(a) // WPC + 1)
     warp_entry, e = [], 0
     for k in range(W):
         ub = k * U // W
@@ -64,6 +71,7 @@ def walk(npages, G=8, w_full=148 * 6):
     assert sum(n_groups) <= (W + len(npages) * G) // 8 + len(npages) * G
     written, tickets, merges, direct = {}, {}, {}, {}
     group_tickets, group_merges = {}, {}
+    slots_used, run_tickets, run_owner = {}, {}, {}
     for gw in range(W):
         ub, ue = gw * U // W, (gw + 1) * U // W
         assert ub < ue, "empty share"
@@ -74,8 +82,18 @@ def walk(npages, G=8, w_full=148 * 6):
         seg = None
 
         def flush(seg):
-            e_, h_, part, nparts = seg
+            e_, h_, part, nparts, run_lo, run_m = seg
             eh = e_ * G + h_
+            if run_m > 1:
+                slot = (gw, 1 if gw == run_lo else 0)
+                assert slot not in slots_used, "shared-memory slot reused"
+                slots_used[slot] = eh
+                key = (gw // WPC, run_lo % WPC)
+                assert run_owner.setdefault(key, eh) == eh, "run ticket shared by two runs"
+                t = run_tickets.get(key, 0)
+                run_tickets[key] = t + 1
+                if t != run_m - 1:
+                    return
             if nparts == 1:
                 direct[eh] = direct.get(eh, 0) + 1
                 return
@@ -105,8 +123,12 @@ def walk(npages, G=8, w_full=148 * 6):
                 if u != ub:
                     flush(seg)
                 a = unit_off[e] + h * np_
-                first = warp_of(a)
-                seg = (e, h, part_off[e * G + h] + (gw - first), warp_of(a + np_ - 1) - first + 1)
+                first, last = warp_of(a), warp_of(a + np_ - 1)
+                cta = gw // WPC
+                run_lo = max(first, cta * WPC)
+                run_hi = min(last, cta * WPC + WPC - 1)
+                seg = (e, h, part_off[e * G + h] + (cta - first // WPC),
+                       last // WPC - first // WPC + 1, run_lo, run_hi - run_lo + 1)
             i += 1
             if i == np_:
                 i, h = 0, h + 1
