@@ -900,10 +900,80 @@ def cpu_baseline_backbone(weights, ctx: int, budget_s: float = 12.0):
                       f"({budget_s:.0f} s), scaled to 36 layers + the output head"}
 
 
+def random_q4k_host(rng, rows, cols):
+    """Random well-formed Q4_K blocks (test data: random quants and 6-bit
+    scales, positive f16 super-scales of N(0, 0.02)-like magnitude)."""
+    b = rng.integers(0, 256, size=(rows, cols // 256, 144), dtype=np.uint8)
+    d = rng.uniform(2e-4, 1e-3, (rows, cols // 256)).astype(np.float16)
+    b[:, :, 0:2] = d.view(np.uint8).reshape(rows, cols // 256, 2)
+    b[:, :, 2:4] = d.view(np.uint8).reshape(rows, cols // 256, 2)
+    return b.reshape(rows, -1)
+
+
+def reference_backbone(args):
+    """The reference arm of the backbone workload: the oracle's restatement of
+    the GGML CPU graph (Q4_K x Q8_K projections, F16 KV attention) on the host
+    cores, 2 of the 36 layers timed and scaled, at the same context."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import cpu_oracle
+    cpu_oracle.build()
+    rng = np.random.default_rng(0)
+    L, ctx = 2, 1024 + args.warmup + args.steps // 2
+    host = {}
+    for l in range(L):
+        p = f"blk.{l}."
+        for name, rows, cols in (("attn_q", 4096, 2560), ("attn_k", 1024, 2560), ("attn_v", 1024, 2560),
+                                 ("attn_output", 2560, 4096), ("ffn_gate", 9728, 2560),
+                                 ("ffn_up", 9728, 2560), ("ffn_down", 2560, 9728)):
+            host[p + name] = random_q4k_host(rng, rows, cols)
+        for name, size in (("attn_norm", 2560), ("ffn_norm", 2560), ("attn_q_norm", 128),
+                           ("attn_k_norm", 128)):
+            host[p + name] = (1.0 + 0.1 * rng.standard_normal(size)).astype(np.float32)
+    host["a.token_embd"] = random_q4k_host(rng, 8 * 1026, 2560)
+    host["a.output"] = random_q4k_host(rng, 8 * 1026, 2560)
+    host["output_norm"] = np.ones(2560, np.float32)
+    ref = cpu_oracle.BackboneOracle(host, L)
+    for l in range(L):
+        kc = rng.integers(0x3000, 0x3800, (ctx, 8, 128)).astype(np.uint16)
+        ref.caches[(0, l)] = (kc, kc.copy())
+    h = ref.embed_codes(np.zeros((1, 8), np.int32))
+    ref.decode(h, [0], [ctx], want_logits=False)
+    budget = max(3.0, 1.0 * (args.steps + args.warmup))
+    t0 = time.perf_counter()
+    steps = 0
+    while time.perf_counter() - t0 < budget or steps < 2:
+        ref.decode(h, [0], [ctx], want_logits=False)
+        steps += 1
+    per_layer = (time.perf_counter() - t0) / steps / L
+    t1 = time.perf_counter()
+    ref.decode(h, [0], [ctx], want_logits=True)
+    head = max(0.0, time.perf_counter() - t1 - per_layer * L)
+    step_s = per_layer * 36 + head
+    value = 1.0 / step_s
+    cores = cpu_oracle.max_threads()
+    print(json.dumps({
+        "metric": "backbone decode tokens/s (36-layer Q4_K step incl. KV append + attention)",
+        "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights x q8_k activations, f32",
+        "data": "synthetic random Q4_K blocks", "impl": "reference",
+        "config": {"workload": f"backbone decode, batch 1, context {ctx}", "global_batch": 1,
+                   "layers": 36, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps} decode steps of 2 of the 36 layers, scaled"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference's GGML CPU graph cannot be built here (ggml submodule absent); "
+                 "this times its restatement in oracle/ on the host cores"),
+    }), flush=True)
+
+
 def bench_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
+        return
+    if args.workload == "backbone":
+        reference_backbone(args)
         return
     lens = []
     for r in range(world):
