@@ -228,6 +228,26 @@ def test_ragged_decode(harness, lengths):
         h.check_cache(s)
 
 
+def test_last_context_position(harness):
+    """A slot filled to 32,766 rows decodes its last two positions (32,766 and
+    32,767, the final rows of the RoPE table and of the context), next to a
+    short slot in the same batch; one more step is refused."""
+    import hkv
+    h = harness(n_layers=1, n_pages=2048 + 8)
+    long_slot = h.new_slot(32768)
+    h.prefill(long_slot, 32766, seed=71)
+    short = h.new_slot(40)
+    h.prefill(short, 21, seed=72)
+    for step in range(2):
+        check_outputs(h.decode([long_slot, short], seed=400 + step))
+    assert h.eng.length(long_slot) == 32768
+    with pytest.raises(hkv.HkvRangeError):
+        h.decode([long_slot], seed=500)
+    k, v = h.gather(long_slot, 0, 32760, 8)
+    rk, rv = h.logical(long_slot, 0)
+    assert np.array_equal(k, rk[32760:]) and np.array_equal(v, rv[32760:])
+
+
 def test_config1_single_slot_512_prefill_120_steps(harness):
     """Single slot, one layer: 512 prefilled positions, then 120 steps each
     appending one row and attending a fresh query (the reference's CPU case)."""
