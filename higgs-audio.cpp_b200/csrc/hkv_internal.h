@@ -62,6 +62,8 @@ struct BatchView {
     int32_t total_units;      // sum of npages * n_head_kv: one unit = one head block of K and V
     int32_t n_warps;          // warps the units are shared among (grid * kAttnWarps)
     int32_t n_parts;
+    int32_t cta_merge;        // 1: the warps of a CTA pre-merge in shared memory (one
+                              // partial per CTA); 0: one partial per warp
 };
 
 // Partials of one (entry, KV head) are merged by one warp when there are at
@@ -153,6 +155,6 @@ void launch_split_wait(const uint32_t *flag, uint32_t target, DeviceError *err,
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
                    int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
                    cudaStream_t stream);
-size_t attention_smem_bytes();
+size_t attention_smem_bytes(bool cta_merge);
 
 }  // namespace hkv

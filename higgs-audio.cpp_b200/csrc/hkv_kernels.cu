@@ -611,7 +611,7 @@ __device__ __forceinline__ void signal_arrival(const Exchange &x, int layer, int
     }
 }
 
-template <bool kAppend>
+template <bool kAppend, bool kCtaMerge>
 __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     attention_kernel(PoolView pool, RopeView rope, BatchView batch, int layer,
                      const float *__restrict__ q, const float *__restrict__ k_new,
@@ -627,10 +627,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     const int64_t W = batch.n_warps;
     float *cta_slots = reinterpret_cast<float *>(smem + kAttnWarps * kWarpSmem);
     int *run_ticket = reinterpret_cast<int *>(smem + kAttnWarps * kWarpSmem + kAttnWarps * 2 * kCtaPartBytes);
-    if (threadIdx.x < kAttnWarps) {
-        run_ticket[threadIdx.x] = 0;
+    if (kCtaMerge) {
+        if (threadIdx.x < kAttnWarps) {
+            run_ticket[threadIdx.x] = 0;
+        }
+        __syncthreads();  // the only CTA barrier: before any warp can leave
     }
-    __syncthreads();  // the only CTA barrier: before any warp can leave
     if (gw >= W) {
         return;
     }
@@ -923,14 +925,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 // segment merge theirs in shared memory first
                 const int first = warp_of(a, U, W);
                 const int last = warp_of(a + cons.np - 1, U, W);
-                const int cta = static_cast<int>(blockIdx.x);
-                const int cta_first = first / kAttnWarps;
-                nparts = last / kAttnWarps - cta_first + 1;
-                part = batch.part_off[seg_e * G + seg_h] + (cta - cta_first);
-                const int run_lo = max(first, cta * kAttnWarps);
-                const int run_hi = min(last, cta * kAttnWarps + kAttnWarps - 1);
-                run_w0 = run_lo - cta * kAttnWarps;
-                run_m = run_hi - run_lo + 1;
+                if (kCtaMerge) {
+                    const int cta = static_cast<int>(blockIdx.x);
+                    const int cta_first = first / kAttnWarps;
+                    nparts = last / kAttnWarps - cta_first + 1;
+                    part = batch.part_off[seg_e * G + seg_h] + (cta - cta_first);
+                    const int run_lo = max(first, cta * kAttnWarps);
+                    const int run_hi = min(last, cta * kAttnWarps + kAttnWarps - 1);
+                    run_w0 = run_lo - cta * kAttnWarps;
+                    run_m = run_hi - run_lo + 1;
+                } else {
+                    nparts = last - first + 1;
+                    part = batch.part_off[seg_e * G + seg_h] + (gw - first);
+                    run_m = 1;
+                }
             }
             const float *cr = rope.cos_tab + static_cast<int64_t>(seg_pos) * (kHeadDim / 2);
             const float *sr = rope.sin_tab + static_cast<int64_t>(seg_pos) * (kHeadDim / 2);
@@ -1144,7 +1152,9 @@ __global__ void gather_kernel(PoolView pool, const int32_t *__restrict__ slot_pa
 
 }  // namespace
 
-size_t attention_smem_bytes() { return static_cast<size_t>(kAttnWarps) * kWarpSmem + kCtaSmem; }
+size_t attention_smem_bytes(bool cta_merge) {
+    return static_cast<size_t>(kAttnWarps) * kWarpSmem + (cta_merge ? kCtaSmem : 0);
+}
 
 void launch_append(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
                    const float *k, const float *v, bool apply_rope, DeviceError *err,
@@ -1175,7 +1185,7 @@ void launch_append_range(const PoolView &pool, const RopeView &rope, const int32
     }
 }
 
-template <bool kAppend>
+template <bool kAppend, bool kCtaMerge>
 void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchView &batch,
                         int layer, const float *q, const float *k_new, const float *v_new,
                         float *part_o, float *part_ml, int32_t *counters, float *out,
@@ -1186,8 +1196,8 @@ void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchV
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaFuncSetAttribute(attention_kernel<kAppend>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(attention_smem_bytes()));
+        cudaFuncSetAttribute(attention_kernel<kAppend, kCtaMerge>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(attention_smem_bytes(kCtaMerge)));
         if (dev >= 0 && dev < 64) {
             configured[dev] = true;
         }
@@ -1196,15 +1206,15 @@ void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchV
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
     cfg.blockDim = dim3(kAttnWarps * 32);
-    cfg.dynamicSmemBytes = attention_smem_bytes();
+    cfg.dynamicSmemBytes = attention_smem_bytes(kCtaMerge);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = overlap_previous ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, attention_kernel<kAppend>, pool, rope, batch, layer, q, k_new, v_new,
-                       part_o, part_ml, counters, out, xchg, scale_log2, err);
+    cudaLaunchKernelEx(&cfg, attention_kernel<kAppend, kCtaMerge>, pool, rope, batch, layer, q, k_new,
+                       v_new, part_o, part_ml, counters, out, xchg, scale_log2, err);
 }
 
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
@@ -1212,12 +1222,22 @@ void launch_attention(const PoolView &pool, const RopeView &rope, const BatchVie
                       float *part_ml, int32_t *counters, float *out, const Exchange &xchg,
                       float scale_log2, DeviceError *err, bool overlap_previous,
                       cudaStream_t stream) {
-    if (k_new != nullptr && v_new != nullptr) {
-        launch_attention_t<true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
-                                 counters, out, xchg, scale_log2, err, overlap_previous, stream);
+    const bool append = k_new != nullptr && v_new != nullptr;
+    if (!append) {
+        k_new = v_new = nullptr;
+    }
+    if (append && batch.cta_merge) {
+        launch_attention_t<true, true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                       counters, out, xchg, scale_log2, err, overlap_previous, stream);
+    } else if (append) {
+        launch_attention_t<true, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                        counters, out, xchg, scale_log2, err, overlap_previous, stream);
+    } else if (batch.cta_merge) {
+        launch_attention_t<false, true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                        counters, out, xchg, scale_log2, err, overlap_previous, stream);
     } else {
-        launch_attention_t<false>(pool, rope, batch, layer, q, nullptr, nullptr, part_o, part_ml,
-                                  counters, out, xchg, scale_log2, err, overlap_previous, stream);
+        launch_attention_t<false, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                         counters, out, xchg, scale_log2, err, overlap_previous, stream);
     }
 }
 

@@ -8,9 +8,11 @@
 //     share(w) = [floor(w U / W), floor((w + 1) U / W))
 // and the warp holding unit a is warp_of(a) = ceil((a + 1) W / U) - 1.
 // Each (entry, KV head) segment [a, a + np) is covered by warps
-// warp_of(a) .. warp_of(a + np - 1); the warps of one CTA (kAttnWarps
-// consecutive warps) merge theirs in shared memory, so the segment has one
-// partial result per CTA it spans.
+// warp_of(a) .. warp_of(a + np - 1), one partial result each -- or, when
+// segments are long (plan_cta_merge: at least two CTAs' worth of warps per
+// segment on average), the warps of one CTA (kAttnWarps consecutive warps)
+// merge theirs in shared memory first and the segment has one partial per CTA
+// it spans.
 //
 // A segment with more than kMergeSingleMax partials is merged in two levels:
 // groups of merge_group_size() partials are merged by the last warp of each
@@ -44,6 +46,11 @@ inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
     return static_cast<int32_t>(total_units < max_warps ? total_units : max_warps);
 }
 
+// CTA-level pre-merge pays when a segment spans many warps (a few long
+// requests); with many short segments it only adds shared-memory traffic
+// and footprint.
+inline bool plan_cta_merge(int64_t n_segments, int64_t W) { return W >= 2 * kAttnWarps * n_segments; }
+
 constexpr int kWarpStartWords = 8;
 
 inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
@@ -56,6 +63,7 @@ struct PlanSummary {
     int64_t total_units = 0;
     int32_t n_parts = 0;   // level-1 partials
     int32_t n_groups = 0;  // group partials (and group counters)
+    bool cta_merge = false;
 };
 
 // Fills `w` (plan_words(...) words, 16-byte aligned).  page_lists[e] points
@@ -65,7 +73,9 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
     PlanSummary s;
     s.total_pages = total_pages;
     s.total_units = total_pages * G;
+    s.cta_merge = plan_cta_merge(static_cast<int64_t>(n) * G, W);
     const int64_t U = s.total_units;
+    const int64_t span = s.cta_merge ? kAttnWarps : 1;  // warps per partial
     int32_t *warp_start = w;
     int32_t *pos = warp_start + kWarpStartWords * W;
     int32_t *ntok = pos + n;
@@ -86,8 +96,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         unit_off[e + 1] = unit_off[e] + np * G;
         for (int32_t h = 0; h < G; ++h) {
             const int64_t a = unit_off[e] + static_cast<int64_t>(h) * np;
-            const int64_t parts = plan_warp_of(a + np - 1, U, W) / kAttnWarps -
-                                  plan_warp_of(a, U, W) / kAttnWarps + 1;
+            const int64_t parts = plan_warp_of(a + np - 1, U, W) / span - plan_warp_of(a, U, W) / span + 1;
             part_off[e * G + h + 1] = part_off[e * G + h] + static_cast<int32_t>(parts);
             part2_off[e * G + h + 1] =
                 part2_off[e * G + h] + merge_groups(static_cast<int32_t>(parts));
@@ -147,6 +156,7 @@ inline BatchView bind_plan(const int32_t *d, int32_t n, int32_t G, const PlanSum
     b.total_units = static_cast<int32_t>(s.total_units);
     b.n_warps = W;
     b.n_parts = s.n_parts;
+    b.cta_merge = s.cta_merge ? 1 : 0;
     return b;
 }
 

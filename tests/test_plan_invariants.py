@@ -28,26 +28,29 @@ import pytest
 WPC = 6  # warps per CTA (kAttnWarps)
 
 
-def plan(npages, G, w_full):
+def plan(npages, G, w_full, cta_merge=None):
     n = len(npages)
     unit_off = [0]
     for np_ in npages:
         unit_off.append(unit_off[-1] + np_ * G)
     U = unit_off[-1]
     W = min(U, w_full)
+    if cta_merge is None:  # plan_cta_merge: two CTAs' worth of warps per segment
+        cta_merge = W >= 2 * WPC * n * G
+    span = WPC if cta_merge else 1
     warp_of = lambda a: ((a + 1) * W + U - 1) // U - 1  # noqa: E731
     part_off = [0]
     for e, np_ in enumerate(npages):
         for h in range(G):
             a = unit_off[e] + h * np_
-            part_off.append(part_off[-1] + warp_of(a + np_ - 1) // WPC - warp_of(a) // WPC + 1)
+            part_off.append(part_off[-1] + warp_of(a + np_ - 1) // span - warp_of(a) // span + 1)
     warp_entry, e = [], 0
     for k in range(W):
         ub = k * U // W
         while e + 1 < n and unit_off[e + 1] <= ub:
             e += 1
         warp_entry.append(e)
-    return unit_off, part_off, warp_entry, U, W, warp_of
+    return unit_off, part_off, warp_entry, U, W, warp_of, cta_merge
 
 
 SINGLE_MAX = 16
@@ -64,8 +67,9 @@ def n_groups_of(nparts):
     return 0 if nparts <= SINGLE_MAX else -(-nparts // group_size(nparts))
 
 
-def walk(npages, G=8, w_full=148 * 6):
-    unit_off, part_off, warp_entry, U, W, warp_of = plan(npages, G, w_full)
+def walk(npages, G=8, w_full=148 * 6, cta_merge=None):
+    unit_off, part_off, warp_entry, U, W, warp_of, cta_merge = plan(npages, G, w_full, cta_merge)
+    span = WPC if cta_merge else 1
     assert part_off[-1] <= W + len(npages) * G  # the engine's partial capacity
     n_groups = [n_groups_of(part_off[i + 1] - part_off[i]) for i in range(len(npages) * G)]
     assert sum(n_groups) <= (W + len(npages) * G) // 8 + len(npages) * G
@@ -88,7 +92,7 @@ def walk(npages, G=8, w_full=148 * 6):
                 slot = (gw, 1 if gw == run_lo else 0)
                 assert slot not in slots_used, "shared-memory slot reused"
                 slots_used[slot] = eh
-                key = (gw // WPC, run_lo % WPC)
+                key = (gw // span, run_lo % span)
                 assert run_owner.setdefault(key, eh) == eh, "run ticket shared by two runs"
                 t = run_tickets.get(key, 0)
                 run_tickets[key] = t + 1
@@ -124,11 +128,11 @@ def walk(npages, G=8, w_full=148 * 6):
                     flush(seg)
                 a = unit_off[e] + h * np_
                 first, last = warp_of(a), warp_of(a + np_ - 1)
-                cta = gw // WPC
-                run_lo = max(first, cta * WPC)
-                run_hi = min(last, cta * WPC + WPC - 1)
-                seg = (e, h, part_off[e * G + h] + (cta - first // WPC),
-                       last // WPC - first // WPC + 1, run_lo, run_hi - run_lo + 1)
+                cta = gw // span
+                run_lo = max(first, cta * span)
+                run_hi = min(last, cta * span + span - 1)
+                seg = (e, h, part_off[e * G + h] + (cta - first // span),
+                       last // span - first // span + 1, run_lo, run_hi - run_lo + 1)
             i += 1
             if i == np_:
                 i, h = 0, h + 1
@@ -148,14 +152,25 @@ def walk(npages, G=8, w_full=148 * 6):
                 assert group_merges.get((eh, g)) == 1
 
 
+@pytest.mark.parametrize("cta_merge", [None, False, True])
 @pytest.mark.parametrize("npages", [[3, 1], [1] * 4, [1] * 300, [3, 19, 63], [2048],
                                     [1, 1000, 1, 1000], [40], [33, 2048]])
-def test_plan_partitions_every_segment(npages):
-    walk(npages)
+def test_plan_partitions_every_segment(npages, cta_merge):
+    walk(npages, cta_merge=cta_merge)
 
 
-def test_plan_random_batches():
+@pytest.mark.parametrize("cta_merge", [None, False, True])
+def test_plan_random_batches(cta_merge):
     rng = random.Random(0)
     for _ in range(30):
         walk([rng.randint(1, 1025) for _ in range(rng.randint(1, 64))],
-             G=rng.choice([1, 2, 4, 8]))
+             G=rng.choice([1, 2, 4, 8]), cta_merge=cta_merge)
+
+
+def test_cta_merge_rule():
+    # long segments (one request near the context limit) merge per CTA;
+    # many short ones (16 slots) keep one partial per warp
+    assert plan([2048], 8, 148 * 6)[-1]
+    assert plan([2048], 1, 148 * 6)[-1]
+    assert not plan([100] * 16, 8, 148 * 6)[-1]
+    assert not plan([600] * 32, 8, 148 * 6)[-1]
