@@ -1396,7 +1396,8 @@ int hkv_split_wait(hkv_engine *eng, int32_t layer, hkv_stream stream_h) {
     if (!eng->split_connected) {
         return fail(eng, HKV_ERR_INVALID, "hkv_split_connect first");
     }
-    ++eng->enqueue_seq;
+    // The wait writes neither the pool nor a plan, so the next decode launch
+    // may still overlap it (enqueue_seq stays).
     launch_split_wait(reinterpret_cast<const uint32_t *>(eng->xchg) + layer,
                       eng->split_target[layer], eng->d_err, static_cast<cudaStream_t>(stream_h));
     return launch_status(eng, "split wait launch");

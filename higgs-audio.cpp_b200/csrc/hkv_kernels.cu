@@ -596,17 +596,20 @@ __device__ __forceinline__ float *out_slice(float *out, const Exchange &x, int r
            kGqa * h * kHeadDim;
 }
 
-// After a warp has stored a finished slice everywhere: make the stores
-// visible system-wide, then count one arrival at every rank for this layer.
+// After a warp has stored a finished slice everywhere: the warp barrier
+// orders every lane's stores before lane 0, whose system-scope release fence
+// (cumulative) orders them before its arrival counts; the counts are
+// fire-and-forget reductions, one per rank, so the warp does not wait for
+// their round trips.
 __device__ __forceinline__ void signal_arrival(const Exchange &x, int layer, int lane) {
     if (x.n_ranks == 0) {
         return;
     }
-    __threadfence_system();
     __syncwarp();
     if (lane == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int r = 0; r < x.n_ranks; ++r) {
-            atomicAdd_system(x.flags[r] + layer, 1u);
+            asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(x.flags[r] + layer) : "memory");
         }
     }
 }
@@ -1243,6 +1246,10 @@ void launch_attention(const PoolView &pool, const RopeView &rope, const BatchVie
 
 // =================================================================== split wait
 __global__ void split_wait_kernel(const uint32_t *flag, uint32_t target, DeviceError *err) {
+    // The next decode launch may start its prologue (plan and page reads of
+    // its own layer) while this wait spins; its griddepcontrol.wait still
+    // holds everything else until the arrivals are complete.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const long long t0 = clock64();
     const volatile uint32_t *f = flag;
     while (static_cast<int32_t>(*f - target) < 0) {
@@ -1251,14 +1258,28 @@ __global__ void split_wait_kernel(const uint32_t *flag, uint32_t target, DeviceE
                          static_cast<int>(target));
             return;
         }
-        __nanosleep(200);
+        __nanosleep(32);
     }
     __threadfence_system();
 }
 
+// Launched as a dependent of the decode launch before it: it may start while
+// that kernel's tail still runs.  It completes only when every slice of the
+// layer has arrived, and on every rank a slice's arrival comes after all reads
+// of that (slot, head)'s partials and the reset of its counters, so the next
+// decode launch (which waits for this one) never races the previous one.
 void launch_split_wait(const uint32_t *flag, uint32_t target, DeviceError *err,
                        cudaStream_t stream) {
-    split_wait_kernel<<<1, 1, 0, stream>>>(flag, target, err);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, split_wait_kernel, flag, target, err);
 }
 
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
