@@ -81,10 +81,10 @@ struct GemvParams {
 constexpr int kStages = 4;                  // weight ring depth per CTA
 constexpr int kStageBytes = 24 * 1024;      // bytes per ring stage
 constexpr int kRingBytes = kStages * kStageBytes;
-constexpr int kBarBytes = 64;               // kStages full + kStages empty mbarriers
+constexpr int kBarBytes = 80;               // kStages full + kStages empty + 1 norm mbarrier
 constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int kQkvRows = 32;                // rows per CTA in the q/k/v launch (4 per head)
-static_assert(2 * kStages * 8 <= kBarBytes, "mbarrier area too small");
+static_assert(2 * kStages * 8 + 8 <= kBarBytes, "mbarrier area too small");
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
@@ -176,6 +176,12 @@ __device__ __forceinline__ double warp_sum_double(double v) {
     return v;
 }
 
+// Byte offset of 16-byte chunk c (0..3) of 64-byte item j (a block's
+// sub-block pair) in a vector's Q8 image.  The chunks of an item are stored
+// rotated by (j / 2) mod 4, so the 8 lanes of a load phase, which read the
+// same chunk of 8 consecutive items, hit 8 different bank groups.
+__device__ __forceinline__ int q8_offset(int j, int c) { return j * 64 + ((c ^ ((j >> 1) & 3)) << 4); }
+
 // Shared-memory image of the Q8_K activations.
 struct Q8View {
     int8_t *q;   // [n][cols]
@@ -261,7 +267,8 @@ __device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View
         lo |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
         hi |= (static_cast<uint32_t>(q[i + 4]) & 0xFFu) << (8 * i);
     }
-    *reinterpret_cast<uint2 *>(a.q + static_cast<size_t>(e) * cols + b * kQK + lane * 8) = make_uint2(lo, hi);
+    *reinterpret_cast<uint2 *>(a.q + static_cast<size_t>(e) * cols + q8_offset(b * 4 + (lane >> 3), (lane & 7) >> 1) +
+                               (lane & 1) * 8) = make_uint2(lo, hi);
     int qs = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) qs += q[i];
@@ -280,7 +287,13 @@ constexpr int kSlabMax = 5;  // 2048-element slabs held in registers (cols <= 10
 // slab s: one batch of loads, one barrier for the norm, then every block is
 // quantised from registers.  Run by the kWarps consumer warps; ends with
 // their barrier.
-__device__ void quantize_activations(const GemvParams &p, const Q8View &a, double *red) {
+__device__ bool quantize_activations(const GemvParams &p, const Q8View &a, double *red, const float *normbuf,
+                                     uint32_t normbar) {
+    if (p.norm != nullptr) {
+        // the norm weights were copied into shared memory before the kernel
+        // waited for its predecessor
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(normbar, 0))) return false;
+    }
     const int nsb = p.cols / kQK;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_slabs = (nsb + kWarps - 1) / kWarps;
@@ -319,8 +332,8 @@ __device__ void quantize_activations(const GemvParams &p, const Q8View &a, doubl
                 for (int sl = 0; sl < kSlabMax; ++sl) {
                     const int b = sl * kWarps + warp;
                     if (sl < n_slabs && b < nsb) {
-                        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(p.norm + b * kQK + lane * 8));
-                        const float4 w1 = __ldg(reinterpret_cast<const float4 *>(p.norm + b * kQK + lane * 8 + 4));
+                        const float4 w0 = *reinterpret_cast<const float4 *>(normbuf + b * kQK + lane * 8);
+                        const float4 w1 = *reinterpret_cast<const float4 *>(normbuf + b * kQK + lane * 8 + 4);
                         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                         for (int i = 0; i < 8; ++i) v[sl][i] = __fmul_rn(__fmul_rn(v[sl][i], scale), wv[i]);
@@ -357,13 +370,14 @@ __device__ void quantize_activations(const GemvParams &p, const Q8View &a, doubl
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const float xv = x[b * kQK + lane * 8 + i];
-                    v[i] = p.norm != nullptr ? __fmul_rn(__fmul_rn(xv, scale), p.norm[b * kQK + lane * 8 + i]) : xv;
+                    v[i] = p.norm != nullptr ? __fmul_rn(__fmul_rn(xv, scale), normbuf[b * kQK + lane * 8 + i]) : xv;
                 }
                 quantize_block(v, a, p.cols, nsb, e, b, lane);
             }
             consumer_sync();
         }
     }
+    return true;
 }
 
 // Scales and mins of sub-blocks 2*part and 2*part+1 from the packed words
@@ -391,8 +405,12 @@ struct ActPart {
 
 __device__ __forceinline__ void load_act(ActPart &x, const Q8View &a, int cols, int nsb, int sb, int part,
                                          int e) {
-    const int4 *ap = reinterpret_cast<const int4 *>(a.q + static_cast<size_t>(e) * cols + sb * kQK + 64 * part);
-    const int4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
+    const int8_t *base = a.q + static_cast<size_t>(e) * cols;
+    const int j = sb * 4 + part;
+    const int4 a0 = *reinterpret_cast<const int4 *>(base + q8_offset(j, 0));
+    const int4 a1 = *reinterpret_cast<const int4 *>(base + q8_offset(j, 1));
+    const int4 a2 = *reinterpret_cast<const int4 *>(base + q8_offset(j, 2));
+    const int4 a3 = *reinterpret_cast<const int4 *>(base + q8_offset(j, 3));
     x.lo[0] = a0.x; x.lo[1] = a0.y; x.lo[2] = a0.z; x.lo[3] = a0.w;
     x.lo[4] = a1.x; x.lo[5] = a1.y; x.lo[6] = a1.z; x.lo[7] = a1.w;
     x.hi[0] = a2.x; x.hi[1] = a2.y; x.hi[2] = a2.z; x.hi[3] = a2.w;
@@ -450,6 +468,7 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
     unsigned char *ring = smem;
     const uint32_t full0 = smem_u32(smem + kRingBytes);
     const uint32_t empty0 = full0 + 8 * kStages;
+    const uint32_t normbar = empty0 + 8 * kStages;
     int m = 0, mrow0 = row0;
     if (MODE == kQkv) {
         m = row0 < p.row_end[0] ? 0 : (row0 < p.row_end[1] ? 1 : 2);
@@ -460,6 +479,7 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             mbar_init(full0 + 8 * st, 1);
             mbar_init(empty0 + 8 * st, static_cast<uint32_t>(R));
         }
+        mbar_init(normbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -469,12 +489,22 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
 
     unsigned char *after_ring = smem + kRingBytes + kBarBytes;
     const Q8View a = carve_q8(after_ring, p.n, p.cols);
-    float *res = reinterpret_cast<float *>(after_ring + q8_smem_bytes(p.n, p.cols));  // kQkv [NB][32]
+    float *normbuf = reinterpret_cast<float *>(after_ring + q8_smem_bytes(p.n, p.cols));  // [cols] if p.norm
+    float *res = normbuf + (p.norm != nullptr ? p.cols : 0);  // kQkv [NB][32]
     bool bad = false;
 
     if (producer) {
         if (lane == 0) {
             const uint64_t policy = evict_first_policy();
+            if (p.norm != nullptr) {  // the RMSNorm weights, before any weight stage
+                const uint32_t bytes = static_cast<uint32_t>(p.cols) * 4u;
+                mbar_arrive_expect_tx(normbar, bytes);
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        smem_u32(normbuf)),
+                    "l"(p.norm), "r"(bytes), "r"(normbar)
+                    : "memory");
+            }
             const uint8_t *wbase[kMats];
 #pragma unroll
             for (int k = 0; k < kMats; ++k) {
@@ -511,10 +541,18 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             for (int c = max(0, issued - kStages); c < issued; ++c) {
                 mbar_wait_bounded(full0 + 8 * (c % kStages), static_cast<uint32_t>((c / kStages) & 1));
             }
+            if (p.norm != nullptr) mbar_wait_bounded(normbar, 0);
         }
     } else {
         pdl_wait();  // x (and y, residual) belong to the kernels before
-        quantize_activations(p, a, a.red);
+        if (!quantize_activations(p, a, a.red, normbuf, normbar)) {
+            if (tid == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
+                p.err->where = HKV_KERNEL_GEMV;
+                p.err->a = blockIdx.x;
+                p.err->b = -1;
+            }
+            bad = true;
+        }
         // 8 lanes per row: lane group q = lane / 8 of warp w takes CTA rows
         // 4w + q, 4w + q + 32, ...; within a row, lane l8 = lane % 8 takes
         // items l8, l8 + 8, ... with four independent accumulators.
@@ -787,9 +825,9 @@ __global__ void argmax_kernel(const float *logits, int32_t n_books, int32_t size
 }
 
 // ------------------------------------------------------------- launchers
-size_t gemv_smem(int mode, int nb, int n, int cols, int chunk_rows) {
+size_t gemv_smem(int mode, int nb, int n, int cols, int chunk_rows, bool has_norm) {
     (void)chunk_rows;
-    size_t b = kRingBytes + kBarBytes + q8_smem_bytes(n, cols);
+    size_t b = kRingBytes + kBarBytes + q8_smem_bytes(n, cols) + (has_norm ? static_cast<size_t>(cols) * 4 : 0);
     if (mode == kQkv) b += static_cast<size_t>(nb) * kQkvRows * sizeof(float) + nb * sizeof(double) + 16;
     return b;
 }
@@ -827,7 +865,7 @@ int num_sms_of(int dev) {
 template <int MODE, int NB>
 cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     auto kern = gemv_kernel<MODE, NB>;
-    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.chunk_rows);
+    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.chunk_rows, p.norm != nullptr);
     static std::mutex mu;
     static bool done[64] = {};
     int dev = 0;
@@ -891,8 +929,8 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
     // vectors per launch: at most kMaxVec, and as many as shared memory holds
     int vmax = kMaxVec;
     const size_t cap = static_cast<size_t>(smem_cap_of(dev));
-    while (vmax > 1 && gemv_smem(MODE, kMaxVec, vmax, p.cols, p.chunk_rows) > cap) --vmax;
-    if (gemv_smem(MODE, 1, 1, p.cols, p.chunk_rows) > cap) return cudaErrorInvalidValue;
+    while (vmax > 1 && gemv_smem(MODE, kMaxVec, vmax, p.cols, p.chunk_rows, p.norm != nullptr) > cap) --vmax;
+    if (gemv_smem(MODE, 1, 1, p.cols, p.chunk_rows, p.norm != nullptr) > cap) return cudaErrorInvalidValue;
     const int n_total = p.n;
     for (int e0 = 0; e0 < n_total; e0 += vmax) {
         GemvParams q = p;
