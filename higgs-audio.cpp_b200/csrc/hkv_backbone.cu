@@ -963,6 +963,28 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 using namespace hkv;
 using namespace hkv::bb;
 
+// Device error word of the standalone projection calls (hkv_q4k_gemv /
+// hkv_q4k_qkv): a bounded wait that gave up is recorded here and reported
+// by hkv_q4k_sync_check.  Host code only takes its address, per device.
+static __device__ hkv::DeviceError g_q4k_err;
+
+namespace {
+std::mutex g_q4k_err_mu;
+hkv::DeviceError *g_q4k_err_ptr[64] = {};
+
+hkv::DeviceError *q4k_err_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_q4k_err_mu);
+    if (g_q4k_err_ptr[dev] == nullptr) {
+        void *ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_q4k_err) != cudaSuccess) return nullptr;
+        g_q4k_err_ptr[dev] = static_cast<hkv::DeviceError *>(ptr);
+    }
+    return g_q4k_err_ptr[dev];
+}
+}  // namespace
+
 // ============================================================== C ABI
 extern "C" int hkv_q4k_quantize(const float *w, int64_t rows, int64_t cols, void *blocks,
                                 hkv_stream stream, char *err_msg, size_t err_len) {
@@ -1049,6 +1071,7 @@ extern "C" int hkv_q4k_gemv(const hkv_q4k_gemv_args *a, hkv_stream stream, char 
     p.residual = a->residual;
     p.y[0] = a->y;
     p.y_rows[0] = p.rows;
+    p.err = q4k_err_word();
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     return finish(swiglu ? launch_gemv<kSwiglu>(p, s) : launch_gemv<kPlain>(p, s), err_msg, err_len, who);
 }
@@ -1099,7 +1122,26 @@ extern "C" int hkv_q4k_qkv(const hkv_q4k_qkv_args *a, hkv_stream stream, char *e
     p.y_rows[1] = p.y_rows[2] = static_cast<int32_t>(rk);
     p.head_norm[0] = a->q_norm;
     p.head_norm[1] = a->k_norm;
+    p.err = q4k_err_word();
     return finish(launch_gemv<kQkv>(p, static_cast<cudaStream_t>(stream)), err_msg, err_len, who);
+}
+
+extern "C" int hkv_q4k_sync_check(hkv_stream stream, char *err_msg, size_t err_len) {
+    const char *who = "hkv_q4k_sync_check";
+    cudaError_t st = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (st != cudaSuccess) return finish(st, err_msg, err_len, who);
+    hkv::DeviceError *w = q4k_err_word();
+    if (w == nullptr) return finish(cudaErrorInvalidSymbol, err_msg, err_len, who);
+    hkv::DeviceError e{};
+    st = cudaMemcpy(&e, w, sizeof(e), cudaMemcpyDeviceToHost);
+    if (st != cudaSuccess) return finish(st, err_msg, err_len, who);
+    if (e.code != 0) {
+        const hkv::DeviceError zero{};
+        cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+        set_msg(err_msg, err_len, "%s: a weight copy of CTA %d did not complete", who, e.a);
+        return HKV_ERR_TIMEOUT;
+    }
+    return HKV_OK;
 }
 
 // Internal launchers used by the backbone driver (hkv_backbone_host.cpp).

@@ -177,6 +177,7 @@ SIGNATURES = {
                      ctypes.c_int),
     "hkv_q4k_qkv": ([ctypes.POINTER(Q4kQkvArgs), _P, ctypes.c_char_p, ctypes.c_size_t],
                     ctypes.c_int),
+    "hkv_q4k_sync_check": ([_P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
     "hkv_backbone_create": ([_P, ctypes.POINTER(BackboneWeights), _I32, ctypes.POINTER(_P)],
                             ctypes.c_int),
     "hkv_backbone_destroy": ([_P], None),
@@ -511,6 +512,13 @@ def q4k_qkv(wq, wk, wv, cols: int, x, q_norm, k_norm, q_out, k_out, v_out, n: in
                    eps, _ptr(q_norm), _ptr(k_norm), _ptr(q_out), _ptr(k_out), _ptr(v_out))
     msg = ctypes.create_string_buffer(512)
     _raise_msg(lib.hkv_q4k_qkv(ctypes.byref(a), _stream(stream), msg, len(msg)), msg)
+
+
+def q4k_sync_check(stream=None, lib=None) -> None:
+    """hkv_q4k_sync_check: synchronise and report a timed-out projection launch."""
+    lib = lib or load_library()
+    msg = ctypes.create_string_buffer(512)
+    _raise_msg(lib.hkv_q4k_sync_check(_stream(stream), msg, len(msg)), msg)
 
 
 class Backbone:

@@ -353,6 +353,11 @@ typedef struct hkv_q4k_qkv_args {
 } hkv_q4k_qkv_args;
 int hkv_q4k_qkv(const hkv_q4k_qkv_args *args, hkv_stream stream, char *err_msg, size_t err_len);
 
+/* Synchronises `stream`; reports (and clears) a bounded device-side wait of a
+ * hkv_q4k_gemv / hkv_q4k_qkv launch on the current device that gave up
+ * (HKV_ERR_TIMEOUT; the output of that launch is not written). */
+int hkv_q4k_sync_check(hkv_stream stream, char *err_msg, size_t err_len);
+
 /* The repo's Q4_K encoder (the reference quantises offline with GGML's tools,
  * scripts/quantize_higgs_gguf_q4_k.py): F32 [rows][cols] -> Q4_K blocks. */
 int hkv_q4k_quantize(const float *w, int64_t rows, int64_t cols, void *blocks, hkv_stream stream,

@@ -81,6 +81,7 @@ def test_gemv_matches_oracle(hkv_lib, oracle, rows, cols, n, use_norm, use_res):
     got = y.cpu().numpy()
     assert np.all(np.isfinite(got))
     assert rel_err(got, ref) <= PROJ_TOL
+    hkv.q4k_sync_check()  # no bounded wait gave up
 
 
 def test_gemv_in_place_residual(hkv_lib, oracle):
