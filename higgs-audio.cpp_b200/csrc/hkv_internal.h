@@ -53,10 +53,12 @@ struct BatchView {
     const int32_t *npages;    // [n]   pages covering [0, used]
     const int32_t *page_off;  // [n+1] prefix sum of npages into pages[]
     const int32_t *unit_off;  // [n+1] prefix sum of npages * n_head_kv
-    const int32_t *part_off;  // [n*n_head_kv + 1] first partial of each (entry, kv head)
     const int32_t *part2_off; // [n*n_head_kv + 1] first group partial / group counter of each
-    const int4 *warp_start;   // [n_warps][2] per warp: {entry, kv head, page index, pages of
-                              // the entry}, {page_off[entry], first three physical pages}
+    const int4 *seg;          // [n*n_head_kv] per (entry, kv head): {first partial, partials,
+                              // first warp, last warp}
+    const int4 *warp_start;   // [n_warps][3] per warp: {entry, kv head, page index, pages of
+                              // the entry}, {page_off[entry], first three physical pages},
+                              // {first unit, end unit, 0, 0}
     const int32_t *pages;     // [page_off[n]] physical pages, entry-major
     int32_t n;
     int32_t total_units;      // sum of npages * n_head_kv: one unit = one head block of K and V

@@ -273,11 +273,6 @@ struct Cursor {
     int pbase;  // page_off[e]
 };
 
-// The warp whose share holds unit a (shares are floor(w U / W) .. floor((w+1) U / W)).
-__device__ __forceinline__ int warp_of(int64_t a, int64_t U, int64_t W) {
-    return static_cast<int>(((a + 1) * W + U - 1) / U - 1);
-}
-
 __device__ __forceinline__ void advance(const BatchView &b, int G, Cursor &c) {
     if (++c.i == c.np) {
         c.i = 0;
@@ -626,8 +621,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     const int wid = threadIdx.x >> 5;
     const int gw = blockIdx.x * kAttnWarps + wid;
     const int G = pool.n_head_kv;
-    const int64_t U = batch.total_units;
-    const int64_t W = batch.n_warps;
+    const int W = batch.n_warps;
     float *cta_slots = reinterpret_cast<float *>(smem + kAttnWarps * kWarpSmem);
     int *run_ticket = reinterpret_cast<int *>(smem + kAttnWarps * kWarpSmem + kAttnWarps * 2 * kCtaPartBytes);
     if (kCtaMerge) {
@@ -639,8 +633,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     if (gw >= W) {
         return;
     }
-    const int u_begin = static_cast<int>(gw * U / W);
-    const int u_end = static_cast<int>((gw + 1) * U / W);
+    // The plan hands each warp its share, its starting cursor and the
+    // physical pages of its first units in three 16-byte records, so the
+    // first copies go out without a chain of dependent loads.
+    const int4 ws0 = batch.warp_start[3 * gw];
+    const int4 ws1 = batch.warp_start[3 * gw + 1];
+    const int4 ws2 = batch.warp_start[3 * gw + 2];
+    const int u_begin = ws2.x;
+    const int u_end = ws2.y;
     if (u_begin >= u_end) {
         return;
     }
@@ -659,11 +659,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     }
     __syncwarp();
 
-    // The plan hands each warp its starting cursor and the physical pages of
-    // its first units in two 16-byte records, so the first copies go out
-    // without a chain of dependent loads.
-    const int4 ws0 = batch.warp_start[2 * gw];
-    const int4 ws1 = batch.warp_start[2 * gw + 1];
     Cursor cons;
     cons.e = ws0.x;
     cons.h = ws0.y;
@@ -709,7 +704,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     float o[8][4];
     uint32_t qb[8][2];
     float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
-    int seg_e = 0, seg_h = 0, seg_pos = 0, part = 0, nparts = 1, ntok = 0;
+    int seg_e = 0, seg_h = 0, seg_pos = 0, part = 0, p_first = 0, nparts = 1, ntok = 0;
     int run_w0 = wid, run_m = 1;  // this CTA's warps of the current segment: w0 .. w0 + m - 1
 
     auto flush = [&](bool after_loop) {
@@ -820,7 +815,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         // group, and the last group (or the only one) produces the output.
         __threadfence();
         __syncwarp();
-        const int p_first = batch.part_off[eh];
         const int j_part = part - p_first;
         const int n_groups = merge_groups(nparts);
         const int n_seg = batch.n * G;  // segment counters come first, then group counters
@@ -923,23 +917,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             seg_pos = batch.pos[seg_e];
             ntok = seg_pos + 1;
             {
-                const int64_t a = batch.unit_off[seg_e] + static_cast<int64_t>(seg_h) * cons.np;
-                // partials are per CTA: the warps of one CTA that share the
-                // segment merge theirs in shared memory first
-                const int first = warp_of(a, U, W);
-                const int last = warp_of(a + cons.np - 1, U, W);
+                // {first partial, partials, first warp, last warp} of the segment
+                const int4 sg = batch.seg[seg_e * G + seg_h];
+                p_first = sg.x;
+                nparts = sg.y;
                 if (kCtaMerge) {
+                    // partials are per CTA: the warps of one CTA that share
+                    // the segment merge theirs in shared memory first
                     const int cta = static_cast<int>(blockIdx.x);
-                    const int cta_first = first / kAttnWarps;
-                    nparts = last / kAttnWarps - cta_first + 1;
-                    part = batch.part_off[seg_e * G + seg_h] + (cta - cta_first);
-                    const int run_lo = max(first, cta * kAttnWarps);
-                    const int run_hi = min(last, cta * kAttnWarps + kAttnWarps - 1);
+                    part = sg.x + (cta - sg.z / kAttnWarps);
+                    const int run_lo = max(sg.z, cta * kAttnWarps);
+                    const int run_hi = min(sg.w, cta * kAttnWarps + kAttnWarps - 1);
                     run_w0 = run_lo - cta * kAttnWarps;
                     run_m = run_hi - run_lo + 1;
                 } else {
-                    nparts = last - first + 1;
-                    part = batch.part_off[seg_e * G + seg_h] + (gw - first);
+                    part = sg.x + (gw - sg.z);
                     run_m = 1;
                 }
             }

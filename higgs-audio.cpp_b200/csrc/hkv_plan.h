@@ -2,17 +2,22 @@
 //
 // A batch of n slots attending pos[e] + 1 rows each is cut into units (one
 // unit = one 16-row page of one KV head, 8 KiB of K and V).  Units are
-// ordered (entry, KV head, page); the range [0, U) is split into W equal
-// shares, one per warp, W = min(U, warps of a full grid) so that no share is
-// empty:
-//     share(w) = [floor(w U / W), floor((w + 1) U / W))
-// and the warp holding unit a is warp_of(a) = ceil((a + 1) W / U) - 1.
-// Each (entry, KV head) segment [a, a + np) is covered by warps
-// warp_of(a) .. warp_of(a + np - 1), one partial result each -- or, when
-// segments are long (plan_cta_merge: at least two CTAs' worth of warps per
-// segment on average), the warps of one CTA (kAttnWarps consecutive warps)
-// merge theirs in shared memory first and the segment has one partial per CTA
-// it spans.
+// ordered (entry, KV head, page) and the range [0, U) is cut into at most W
+// consecutive shares, one per warp, W = min(U, warps of a full grid).
+// Shares are balanced by cost, not by unit count: a unit costs kCostUnit,
+// and a warp that moves on to another (entry, KV head) segment inside its
+// share pays for publishing the segment it leaves and staging the next
+// one's queries (kCostLeaveWhole when it held that segment from its first
+// page, kCostLeaveShared when an earlier warp holds part of it, since then
+// a partial result is published and a merge ticket taken).  The smallest
+// per-share budget B for which a greedy cut needs no more than W shares is
+// found by bisection; warps past the last share have empty shares and no
+// segment counts them.
+// Each (entry, KV head) segment is covered by warps first .. last, one
+// partial result each -- or, when segments are long (plan_cta_merge: at
+// least two CTAs' worth of warps per segment on average), the warps of one
+// CTA (kAttnWarps consecutive warps) merge theirs in shared memory first and
+// the segment has one partial per CTA it spans.
 //
 // A segment with more than kMergeSingleMax partials is merged in two levels:
 // groups of merge_group_size() partials are merged by the last warp of each
@@ -21,27 +26,27 @@
 // n_parts partials) and its first group counter (after the n*G segment
 // counters).
 //
-// Device descriptor (int32 words, uploaded in one copy):
-//   warp_start[W][8]  per warp {entry, kv head, page index, pages of the entry}
+// Device descriptor (int32 words, uploaded in one copy; the 16-byte records
+// first, so each stays aligned):
+//   warp_start[W][12] per warp {entry, kv head, page index, pages of the entry}
 //                     {page_off[entry], physical pages of its first 3 units}
-//                     (first, so each record is 16-byte aligned)
-//   pos[n] ntok[n] npages[n] page_off[n+1] unit_off[n+1] part_off[n*G+1]
-//   part2_off[n*G+1] pages[total_pages]
+//                     {first unit, end unit, 0, 0}
+//   seg[n*G][4]       per segment {first partial, partials, first warp, last warp}
+//   pos[n] ntok[n] npages[n] page_off[n+1] unit_off[n+1] part2_off[n*G+1]
+//   pages[total_pages]
 #pragma once
 
 #include <stdint.h>
 
+#include <algorithm>
 #include <cstring>
+#include <vector>
 
 #include "hkv_internal.h"
 
 namespace hkv {
 
-inline int64_t plan_warp_of(int64_t a, int64_t U, int64_t W) { return ((a + 1) * W + U - 1) / U - 1; }
-
-// Warps to share U units among: every share must hold at least one unit (a
-// segment's partial count is the number of warps its range touches, so an
-// empty share in the middle would be counted but never arrive).
+// Warps to share U units among (at most one per unit).
 inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
     return static_cast<int32_t>(total_units < max_warps ? total_units : max_warps);
 }
@@ -51,11 +56,63 @@ inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
 // and footprint.
 inline bool plan_cta_merge(int64_t n_segments, int64_t W) { return W >= 2 * kAttnWarps * n_segments; }
 
-constexpr int kWarpStartWords = 8;
+// Share costs in sixteenths of a unit, from per-warp timestamps of the
+// attention kernel on B200 (16 slots of 256-4096 positions): a unit takes
+// about 0.95 us of a warp's time, leaving a segment held whole about 1 us
+// (output stores, next queries), leaving a shared one about 3.3 us (partial
+// stores, fence, ticket round trip, next queries).
+constexpr int64_t kCostUnit = 16;
+constexpr int64_t kCostLeaveWhole = 16;
+constexpr int64_t kCostLeaveShared = 56;
+
+// Greedy cut of the segments (segment s has npg[s / G] units) into shares of
+// cost at most B (B >= kCostUnit, so every share holds a unit).  Returns the
+// number of shares, or max_shares + 1 as soon as more are needed; writes each
+// share's first unit to starts[] when starts is not null.
+inline int64_t plan_cut(const int32_t *npg, int32_t G, int64_t S, int64_t B, int64_t max_shares,
+                        int32_t *starts) {
+    int64_t k = 0, s = 0, i = 0, u = 0;  // shares, segment, unit within it, flat unit
+    while (s < S) {
+        if (k == max_shares) {
+            return max_shares + 1;
+        }
+        if (starts != nullptr) {
+            starts[k] = static_cast<int32_t>(u);
+        }
+        ++k;
+        int64_t budget = B;
+        bool from_first_page = i == 0;
+        for (;;) {
+            const int64_t np = npg[s / G];
+            const int64_t take = std::min(np - i, budget / kCostUnit);
+            i += take;
+            u += take;
+            budget -= take * kCostUnit;
+            if (i < np) {
+                break;  // the share ends inside this segment
+            }
+            ++s;
+            i = 0;
+            if (s == S) {
+                break;
+            }
+            const int64_t leave = from_first_page ? kCostLeaveWhole : kCostLeaveShared;
+            if (budget - leave < kCostUnit) {
+                break;  // the next segment opens the next share
+            }
+            budget -= leave;
+            from_first_page = true;
+        }
+    }
+    return k;
+}
+
+constexpr int kWarpStartWords = 12;
+constexpr int kSegWords = 4;
 
 inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
-    return static_cast<size_t>(kWarpStartWords * W + 3 * n + 2 * (n + 1) + 2 * (n * G + 1) +
-                               total_pages);
+    return static_cast<size_t>(kWarpStartWords * W + kSegWords * n * G + 3 * n + 2 * (n + 1) +
+                               (n * G + 1) + total_pages);
 }
 
 struct PlanSummary {
@@ -63,6 +120,8 @@ struct PlanSummary {
     int64_t total_units = 0;
     int32_t n_parts = 0;   // level-1 partials
     int32_t n_groups = 0;  // group partials (and group counters)
+    int32_t shares = 0;    // non-empty shares (<= W)
+    int64_t budget = 0;    // the cost bound B of every share
     bool cta_merge = false;
 };
 
@@ -75,17 +134,18 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
     s.total_units = total_pages * G;
     s.cta_merge = plan_cta_merge(static_cast<int64_t>(n) * G, W);
     const int64_t U = s.total_units;
+    const int64_t S = static_cast<int64_t>(n) * G;
     const int64_t span = s.cta_merge ? kAttnWarps : 1;  // warps per partial
     int32_t *warp_start = w;
-    int32_t *pos = warp_start + kWarpStartWords * W;
+    int32_t *seg = warp_start + kWarpStartWords * W;
+    int32_t *pos = seg + kSegWords * S;
     int32_t *ntok = pos + n;
     int32_t *npg = ntok + n;
     int32_t *page_off = npg + n;
     int32_t *unit_off = page_off + (n + 1);
-    int32_t *part_off = unit_off + (n + 1);
-    int32_t *part2_off = part_off + (n * G + 1);
-    int32_t *pages = part2_off + (n * G + 1);
-    page_off[0] = unit_off[0] = part_off[0] = part2_off[0] = 0;
+    int32_t *part2_off = unit_off + (n + 1);
+    int32_t *pages = part2_off + (S + 1);
+    page_off[0] = unit_off[0] = part2_off[0] = 0;
     for (int32_t e = 0; e < n; ++e) {
         const int32_t np = pos_in[e] / kPageTokens + 1;
         pos[e] = pos_in[e];
@@ -94,22 +154,72 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         std::memcpy(pages + page_off[e], page_lists[e], static_cast<size_t>(np) * sizeof(int32_t));
         page_off[e + 1] = page_off[e] + np;
         unit_off[e + 1] = unit_off[e] + np * G;
-        for (int32_t h = 0; h < G; ++h) {
-            const int64_t a = unit_off[e] + static_cast<int64_t>(h) * np;
-            const int64_t parts = plan_warp_of(a + np - 1, U, W) / span - plan_warp_of(a, U, W) / span + 1;
-            part_off[e * G + h + 1] = part_off[e * G + h] + static_cast<int32_t>(parts);
-            part2_off[e * G + h + 1] =
-                part2_off[e * G + h] + merge_groups(static_cast<int32_t>(parts));
+    }
+
+    // ---- shares: the smallest budget that fits W warps (bisection)
+    const int64_t per = (U + W - 1) / W;
+    int64_t bad = kCostUnit * per - 1;  // W shares of fewer than per units cannot hold U
+    int64_t good = kCostUnit * per + kCostLeaveShared * (S + 1);
+    while (plan_cut(npg, G, S, good, W, nullptr) > W) {
+        good *= 2;
+    }
+    while (good - bad > 1) {
+        const int64_t mid = bad + (good - bad) / 2;
+        if (plan_cut(npg, G, S, mid, W, nullptr) > W) {
+            bad = mid;
+        } else {
+            good = mid;
         }
     }
+    s.budget = good;
+    // share starts go to word 8 of each record; the loop below fills the rest
+    std::vector<int32_t> starts(static_cast<size_t>(W) + 1);
+    s.shares = static_cast<int32_t>(plan_cut(npg, G, S, good, W, starts.data()));
+    for (int64_t k = s.shares; k <= W; ++k) {
+        starts[k] = static_cast<int32_t>(U);
+    }
+
+    // ---- segments: warps first .. last, partials
+    int32_t parts = 0;
+    int32_t k = 0;  // the share holding unit a
+    for (int64_t sg = 0; sg < S; ++sg) {
+        const int32_t e = static_cast<int32_t>(sg / G);
+        const int64_t a = unit_off[e] + (sg % G) * npg[e];
+        while (starts[k + 1] <= a) {
+            ++k;
+        }
+        int32_t last = k;
+        while (starts[last + 1] <= a + npg[e] - 1) {
+            ++last;
+        }
+        const int32_t np_parts = static_cast<int32_t>(last / span - k / span + 1);
+        int32_t *rec = seg + kSegWords * sg;
+        rec[0] = parts;
+        rec[1] = np_parts;
+        rec[2] = k;
+        rec[3] = last;
+        parts += np_parts;
+        part2_off[sg + 1] = part2_off[sg] + merge_groups(np_parts);
+    }
+
+    // ---- per-warp records
     int32_t e = 0;
-    for (int32_t k = 0; k < W; ++k) {
-        const int64_t ub = static_cast<int64_t>(k) * U / W;
-        const int64_t ue = static_cast<int64_t>(k + 1) * U / W;
+    for (int32_t kw = 0; kw < W; ++kw) {
+        const int64_t ub = starts[kw];
+        const int64_t ue = starts[kw + 1];
+        int32_t *ws = warp_start + kWarpStartWords * kw;
+        ws[8] = static_cast<int32_t>(ub);
+        ws[9] = static_cast<int32_t>(ue);
+        ws[10] = ws[11] = 0;
+        if (ub >= ue) {
+            for (int j = 0; j < 8; ++j) {
+                ws[j] = 0;
+            }
+            continue;
+        }
         while (e + 1 < n && unit_off[e + 1] <= ub) {
             ++e;
         }
-        int32_t *ws = warp_start + kWarpStartWords * k;
         const int32_t np = npg[e];
         const int32_t rem = static_cast<int32_t>(ub - unit_off[e]);
         ws[0] = e;
@@ -134,8 +244,8 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
             }
         }
     }
-    s.n_parts = part_off[n * G];
-    s.n_groups = part2_off[n * G];
+    s.n_parts = parts;
+    s.n_groups = part2_off[S];
     return s;
 }
 
@@ -144,13 +254,13 @@ inline BatchView bind_plan(const int32_t *d, int32_t n, int32_t G, const PlanSum
                            int32_t W) {
     BatchView b;
     b.warp_start = reinterpret_cast<const int4 *>(d);
-    b.pos = d + kWarpStartWords * W;
+    b.seg = reinterpret_cast<const int4 *>(d + kWarpStartWords * W);
+    b.pos = d + kWarpStartWords * W + kSegWords * n * G;
     b.ntok = b.pos + n;
     b.npages = b.ntok + n;
     b.page_off = b.npages + n;
     b.unit_off = b.page_off + (n + 1);
-    b.part_off = b.unit_off + (n + 1);
-    b.part2_off = b.part_off + (n * G + 1);
+    b.part2_off = b.unit_off + (n + 1);
     b.pages = b.part2_off + (n * G + 1);
     b.n = n;
     b.total_units = static_cast<int32_t>(s.total_units);

@@ -1,56 +1,127 @@
 """Invariants of the stream-K plan (higgs-audio.cpp_b200/csrc/hkv_plan.h), CPU.
 
-Also walks the two-level merge: a segment with more than 16 partials is
-merged in groups of max(8, ceil(sqrt(n))) by the last warp of each group,
-and the last group merges the group partials; every segment must finish
-exactly once.
+The plan builder itself is compiled from its header (tests/cpp/plan_dump.cpp
+prints its descriptor) and checked against a restatement here:
+- shares: the unit range [0, U) is cut greedily into consecutive shares of
+  cost at most B (a unit costs 16, leaving a segment inside a share costs 16
+  when the share held it from its first page, 56 otherwise; a share never
+  enters a segment it cannot take a unit of), and B is the smallest budget
+  that needs at most W = min(U, grid warps) shares;
+- segments: each (slot, KV head) segment records its first and last warp
+  and its partial count (warps, or CTAs of WPC warps with the CTA merge).
 
-Restates the plan's formulas -- W = min(U, grid warps) equal shares
-floor(w U / W) .. floor((w + 1) U / W), warp_of(a) = ceil((a + 1) W / U) - 1,
-part_off from the CTAs (WPC consecutive warps) a (slot, KV head) segment
-touches, warp_entry -- and walks every warp the way attention_kernel does:
-the warps of one CTA that share a segment leave their partials in shared
-memory (slot 1 for the run's first warp, 0 for the others), the last of them
-(run ticket) merges and publishes the CTA's partial.  Checks that every
-shared-memory slot and run ticket is used by one run only, that each
-segment's CTA partials are written exactly once and merged exactly once (or
-the output written directly when one CTA holds the whole segment).  Empty
-shares would break this (a segment would count a partial that never
-arrives), which is why W is capped at U.
+Then every warp is walked the way attention_kernel does, with the two-level
+merge (a segment with more than 16 partials is merged in groups of
+max(8, ceil(sqrt(n))) by the last warp of each group, and the last group
+merges the group partials): the warps of one CTA that share a segment leave
+their partials in shared memory (slot 1 for the run's first warp, 0 for the
+others), the last of them (run ticket) merges and publishes the CTA's
+partial.  Checks that every shared-memory slot and run ticket is used by one
+run only, that each segment's partials are written exactly once and merged
+exactly once (or the output written directly when one warp or CTA holds the
+whole segment), and that no share past the last non-empty one is counted.
 """
 from __future__ import annotations
 
 import random
+import shutil
+import subprocess
+from pathlib import Path
 
 import pytest
 
-
+REPO = Path(__file__).resolve().parents[1]
 WPC = 6  # warps per CTA (kAttnWarps)
+UNIT, LEAVE_WHOLE, LEAVE_SHARED = 16, 16, 56
 
 
-def plan(npages, G, w_full, cta_merge=None):
-    n = len(npages)
-    unit_off = [0]
-    for np_ in npages:
-        unit_off.append(unit_off[-1] + np_ * G)
-    U = unit_off[-1]
+@pytest.fixture(scope="module")
+def plan_dump(tmp_path_factory):
+    gxx = shutil.which("g++", path="/usr/bin:/bin")
+    cuda_inc = Path("/usr/local/cuda/include")
+    if gxx is None or not (cuda_inc / "cuda_runtime.h").exists():
+        pytest.skip("no system g++ or CUDA headers")
+    exe = tmp_path_factory.mktemp("plan") / "plan_dump"
+    subprocess.run([gxx, "-std=c++17", "-O1", "-Wall", "-Werror",
+                    f"-I{REPO / 'higgs-audio.cpp_b200' / 'csrc'}", f"-I{cuda_inc}",
+                    str(REPO / "tests" / "cpp" / "plan_dump.cpp"), "-o", str(exe)], check=True)
+
+    def run(batches):
+        """batches: list of (G, W, positions); returns one parsed plan each."""
+        text = "".join(f"{G} {W} " + " ".join(map(str, pos)) + "\n" for G, W, pos in batches)
+        out = subprocess.run([str(exe)], input=text, capture_output=True, text=True, check=True,
+                             timeout=120).stdout.splitlines()
+        plans, i = [], 0
+        for G, W, pos in batches:
+            hdr = out[i].split()
+            assert hdr[0] == "plan"
+            shares, budget, cta, n_parts, n_groups = map(int, hdr[1:])
+            starts = list(map(int, out[i + 1].split()[1:]))
+            n_seg = len(pos) * G
+            segs = [tuple(map(int, out[i + 2 + j].split()[1:])) for j in range(n_seg)]
+            part2 = list(map(int, out[i + 2 + n_seg].split()[1:]))
+            warps = list(map(int, out[i + 3 + n_seg].split()[1:]))
+            i += 4 + n_seg
+            plans.append(dict(shares=shares, budget=budget, cta_merge=bool(cta), n_parts=n_parts,
+                              n_groups=n_groups, starts=starts, segs=segs, part2=part2,
+                              warps=[tuple(warps[k:k + 3]) for k in range(0, len(warps), 3)]))
+        return plans
+    return run
+
+
+def cut(npages, G, B, max_shares):
+    """The greedy cut: share starts, or None when more than max_shares are needed."""
+    seg_np = [np_ for np_ in npages for _ in range(G)]
+    starts, s, i, u = [], 0, 0, 0
+    while s < len(seg_np):
+        if len(starts) == max_shares:
+            return None
+        starts.append(u)
+        budget, from_first = B, i == 0
+        while True:
+            take = min(seg_np[s] - i, budget // UNIT)
+            assert take >= 1
+            i, u, budget = i + take, u + take, budget - take * UNIT
+            if i < seg_np[s]:
+                break
+            s, i = s + 1, 0
+            if s == len(seg_np):
+                break
+            leave = LEAVE_WHOLE if from_first else LEAVE_SHARED
+            if budget - leave < UNIT:
+                break
+            budget -= leave
+            from_first = True
+    return starts
+
+
+def restate(npages, G, w_full, cta_merge=None):
+    U = sum(npages) * G
     W = min(U, w_full)
     if cta_merge is None:  # plan_cta_merge: two CTAs' worth of warps per segment
-        cta_merge = W >= 2 * WPC * n * G
+        cta_merge = W >= 2 * WPC * len(npages) * G
+    B = UNIT  # smallest feasible budget, by a plain upward search from the bound
+    B = max(B, UNIT * -(-U // W))
+    while cut(npages, G, B, W) is None:
+        B += 1
+    starts = cut(npages, G, B, W)
+    shares = len(starts)
+    starts = starts + [U] * (W - shares) + [U]
     span = WPC if cta_merge else 1
-    warp_of = lambda a: ((a + 1) * W + U - 1) // U - 1  # noqa: E731
-    part_off = [0]
-    for e, np_ in enumerate(npages):
-        for h in range(G):
-            a = unit_off[e] + h * np_
-            part_off.append(part_off[-1] + warp_of(a + np_ - 1) // span - warp_of(a) // span + 1)
-    warp_entry, e = [], 0
-    for k in range(W):
-        ub = k * U // W
-        while e + 1 < n and unit_off[e + 1] <= ub:
-            e += 1
-        warp_entry.append(e)
-    return unit_off, part_off, warp_entry, U, W, warp_of, cta_merge
+    segs, parts, k = [], 0, 0
+    a = 0
+    for np_ in npages:
+        for _ in range(G):
+            while starts[k + 1] <= a:
+                k += 1
+            last = k
+            while starts[last + 1] <= a + np_ - 1:
+                last += 1
+            n_p = last // span - k // span + 1
+            segs.append((parts, n_p, k, last))
+            parts += n_p
+            a += np_
+    return dict(U=U, W=W, B=B, shares=shares, starts=starts, segs=segs, cta_merge=cta_merge)
 
 
 SINGLE_MAX = 16
@@ -67,27 +138,62 @@ def n_groups_of(nparts):
     return 0 if nparts <= SINGLE_MAX else -(-nparts // group_size(nparts))
 
 
-def walk(npages, G=8, w_full=148 * 6, cta_merge=None):
-    unit_off, part_off, warp_entry, U, W, warp_of, cta_merge = plan(npages, G, w_full, cta_merge)
-    span = WPC if cta_merge else 1
-    assert part_off[-1] <= W + len(npages) * G  # the engine's partial capacity
-    n_groups = [n_groups_of(part_off[i + 1] - part_off[i]) for i in range(len(npages) * G)]
-    assert sum(n_groups) <= (W + len(npages) * G) // 8 + len(npages) * G
+def walk(plan_dump, npages, G=8, w_full=148 * 6):
+    pos = [16 * np_ - 1 - (j % 16) for j, np_ in enumerate(npages)]  # np_ pages each
+    got = plan_dump([(G, min(sum(npages) * G, w_full), pos)])[0]
+    ref = restate(npages, G, w_full)
+    U, W = ref["U"], ref["W"]
+    assert got["budget"] == ref["B"] and got["shares"] == ref["shares"]
+    assert got["starts"] == ref["starts"]
+    assert got["segs"] == ref["segs"] and got["cta_merge"] == ref["cta_merge"]
+    assert got["n_parts"] == sum(n for _, n, _, _ in ref["segs"])
+    n_seg = len(npages) * G
+    n_groups = [n_groups_of(sg[1]) for sg in ref["segs"]]
+    assert got["part2"] == [sum(n_groups[:i]) for i in range(n_seg + 1)]
+    assert got["n_parts"] <= W + n_seg  # the engine's partial capacity
+    assert sum(n_groups) <= (W + n_seg) // 8 + n_seg
+    # the cost bound: no share costs more than B, and B is not loose
+    span = WPC if ref["cta_merge"] else 1
+    starts, segs = ref["starts"], ref["segs"]
+    seg_start = []
+    a = 0
+    for np_ in npages:
+        for _ in range(G):
+            seg_start.append(a)
+            a += np_
+    seg_start.append(U)
+    for k in range(ref["shares"]):
+        ub, ue = starts[k], starts[k + 1]
+        assert ub < ue, "empty share inside the range"
+        crossed = [s for s in range(n_seg) if ub < seg_start[s + 1] < ue]
+        cost = UNIT * (ue - ub)
+        for j, s in enumerate(crossed):
+            held_from_first = (seg_start[s] >= ub) if j == 0 else True
+            cost += LEAVE_WHOLE if held_from_first else LEAVE_SHARED
+        assert cost <= ref["B"]
+    assert ref["B"] == UNIT or cut(npages, G, ref["B"] - 1, W) is None
+
     written, tickets, merges, direct = {}, {}, {}, {}
     group_tickets, group_merges = {}, {}
     slots_used, run_tickets, run_owner = {}, {}, {}
+    warp_records = iter(got["warps"])
+    seg_of = []
+    for s in range(n_seg):
+        seg_of.extend([s] * (seg_start[s + 1] - seg_start[s]))
     for gw in range(W):
-        ub, ue = gw * U // W, (gw + 1) * U // W
-        assert ub < ue, "empty share"
-        e = warp_entry[gw]
-        np_ = npages[e]
-        rem = ub - unit_off[e]
-        h, i = rem // np_, rem % np_
+        ub, ue = starts[gw], starts[gw + 1]
+        if ub >= ue:
+            assert gw >= ref["shares"]
+            assert all(not (f <= gw <= l) for _, _, f, l in segs), "idle warp counted"
+            continue
+        s0 = seg_of[ub]
+        e0, h0, i0 = s0 // G, s0 % G, ub - seg_start[s0]
+        assert next(warp_records) == (e0, h0, i0)
         seg = None
 
         def flush(seg):
-            e_, h_, part, nparts, run_lo, run_m = seg
-            eh = e_ * G + h_
+            eh, part, nparts, run_lo, run_m = seg
+            p_first = segs[eh][0]
             if run_m > 1:
                 slot = (gw, 1 if gw == run_lo else 0)
                 assert slot not in slots_used, "shared-memory slot reused"
@@ -101,7 +207,7 @@ def walk(npages, G=8, w_full=148 * 6, cta_merge=None):
             if nparts == 1:
                 direct[eh] = direct.get(eh, 0) + 1
                 return
-            assert part_off[eh] <= part < part_off[eh + 1]
+            assert p_first <= part < p_first + nparts
             written[part] = written.get(part, 0) + 1
             if nparts <= SINGLE_MAX:
                 t = tickets.get(eh, 0)
@@ -110,7 +216,7 @@ def walk(npages, G=8, w_full=148 * 6, cta_merge=None):
                     merges[eh] = merges.get(eh, 0) + 1
                 return
             gs = group_size(nparts)
-            g = (part - part_off[eh]) // gs
+            g = (part - p_first) // gs
             g_size = min(gs, nparts - g * gs)
             t = group_tickets.get((eh, g), 0)
             group_tickets[(eh, g)] = t + 1
@@ -123,54 +229,61 @@ def walk(npages, G=8, w_full=148 * 6, cta_merge=None):
                 merges[eh] = merges.get(eh, 0) + 1
 
         for u in range(ub, ue):
-            if u == ub or i == 0:
+            s = seg_of[u]
+            if u == ub or u == seg_start[s]:
                 if u != ub:
                     flush(seg)
-                a = unit_off[e] + h * np_
-                first, last = warp_of(a), warp_of(a + np_ - 1)
+                p0, n_p, first, last = segs[s]
+                assert first <= gw <= last
                 cta = gw // span
                 run_lo = max(first, cta * span)
                 run_hi = min(last, cta * span + span - 1)
-                seg = (e, h, part_off[e * G + h] + (cta - first // span),
-                       last // span - first // span + 1, run_lo, run_hi - run_lo + 1)
-            i += 1
-            if i == np_:
-                i, h = 0, h + 1
-                if h == G:
-                    h, e = 0, e + 1
-                    if e < len(npages):
-                        np_ = npages[e]
+                seg = (s, p0 + (cta - first // span), n_p, run_lo, run_hi - run_lo + 1)
         flush(seg)
-    for eh in range(len(npages) * G):
-        if part_off[eh + 1] - part_off[eh] == 1:
+    for eh in range(n_seg):
+        p0, n_p = segs[eh][0], segs[eh][1]
+        if n_p == 1 and segs[eh][2] // span == segs[eh][3] // span:
             assert direct.get(eh) == 1
         else:
             assert merges.get(eh) == 1
-            for p in range(part_off[eh], part_off[eh + 1]):
+            for p in range(p0, p0 + n_p):
                 assert written.get(p) == 1
             for g in range(n_groups[eh]):
                 assert group_merges.get((eh, g)) == 1
 
 
-@pytest.mark.parametrize("cta_merge", [None, False, True])
 @pytest.mark.parametrize("npages", [[3, 1], [1] * 4, [1] * 300, [3, 19, 63], [2048],
-                                    [1, 1000, 1, 1000], [40], [33, 2048]])
-def test_plan_partitions_every_segment(npages, cta_merge):
-    walk(npages, cta_merge=cta_merge)
+                                    [1, 1000, 1, 1000], [40], [33, 2048], [17] * 16,
+                                    [1] * 2000])
+def test_plan_partitions_every_segment(plan_dump, npages):
+    walk(plan_dump, npages)
 
 
-@pytest.mark.parametrize("cta_merge", [None, False, True])
-def test_plan_random_batches(cta_merge):
+def test_plan_random_batches(plan_dump):
     rng = random.Random(0)
-    for _ in range(30):
-        walk([rng.randint(1, 1025) for _ in range(rng.randint(1, 64))],
-             G=rng.choice([1, 2, 4, 8]), cta_merge=cta_merge)
+    for _ in range(40):
+        walk(plan_dump, [rng.randint(1, 1025) for _ in range(rng.randint(1, 64))],
+             G=rng.choice([1, 2, 4, 8]), w_full=rng.choice([148 * 6, 37, 6]))
+
+
+def test_shares_balance_segment_switches():
+    # 16 slots of 256-4096 positions: the shares that move between
+    # segments hold fewer units, and every share costs about the same
+    rng = random.Random(2000)
+    npages = [rng.randint(256, 4096) // 16 + 1 for _ in range(16)]
+    ref = restate(npages, 8, 148 * 6)
+    starts, U = ref["starts"], ref["U"]
+    sizes = [starts[k + 1] - starts[k] for k in range(ref["shares"])]
+    assert ref["shares"] <= 148 * 6
+    assert max(sizes) == ref["B"] // UNIT
+    assert min(sizes[:-1]) >= max(sizes) - LEAVE_SHARED // UNIT - 1
+    assert sum(sizes) == U
 
 
 def test_cta_merge_rule():
     # long segments (one request near the context limit) merge per CTA;
     # many short ones (16 slots) keep one partial per warp
-    assert plan([2048], 8, 148 * 6)[-1]
-    assert plan([2048], 1, 148 * 6)[-1]
-    assert not plan([100] * 16, 8, 148 * 6)[-1]
-    assert not plan([600] * 32, 8, 148 * 6)[-1]
+    assert restate([2048], 8, 148 * 6)["cta_merge"]
+    assert restate([2048], 1, 148 * 6)["cta_merge"]
+    assert not restate([100] * 16, 8, 148 * 6)["cta_merge"]
+    assert not restate([600] * 32, 8, 148 * 6)["cta_merge"]
