@@ -74,17 +74,24 @@ struct GemvParams {
     int32_t y_rows[3];
     const float *head_norm[2];  // kQkv: q_norm, k_norm [128]
     int32_t rows_per_cta;     // contiguous weight rows of one CTA
-    int32_t chunk_rows;       // rows per ring stage (a power of two, <= 64)
+    int32_t chunk_rows;       // rows per ring stage
+    int32_t n_stages;         // ring stages (<= kMaxStages)
+    int32_t stage_bytes;      // chunk_rows * row bytes * matrices
     DeviceError *err;         // bounded-wait timeouts are recorded here
 };
 
-constexpr int kStages = 4;                  // weight ring depth per CTA
-constexpr int kStageBytes = 24 * 1024;      // bytes per ring stage
-constexpr int kRingBytes = kStages * kStageBytes;
-constexpr int kBarBytes = 80;               // kStages full + kStages empty + 1 norm mbarrier
+// Weight ring of a CTA: n_stages stages of chunk_rows whole rows, chosen per
+// launch (plan_rows).  When a CTA's rows fit in kRingCap they are all in
+// flight at once, in up to kMaxStages chunks, before the kernel waits for its
+// predecessor; otherwise stages of about kStreamStageBytes are refilled as
+// the consumer warps release them.
+constexpr int kMaxStages = 12;
+constexpr int kRingCap = 100 * 1024;
+constexpr int kStreamStageBytes = 24 * 1024;
+constexpr int kBarBytes = 208;              // kMaxStages full + kMaxStages empty + 1 norm mbarrier
 constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int kQkvRows = 32;                // rows per CTA in the q/k/v launch (4 per head)
-static_assert(2 * kStages * 8 + 8 <= kBarBytes, "mbarrier area too small");
+static_assert(2 * kMaxStages * 8 + 8 <= kBarBytes && kBarBytes % 16 == 0, "mbarrier area too small");
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
@@ -286,9 +293,9 @@ constexpr int kSlabMax = 5;  // 2048-element slabs held in registers (cols <= 10
 // [8t, 8t + 8) of every 2048-element slab, so warp w holds block 8s + w of
 // slab s: one batch of loads, one barrier for the norm, then every block is
 // quantised from registers.  Run by the kWarps consumer warps; ends with
-// their barrier.
-__device__ bool quantize_activations(const GemvParams &p, const Q8View &a, double *red, const float *normbuf,
-                                     uint32_t normbar) {
+// their barrier.  x0: n_vec vectors of p.cols floats.
+__device__ bool quantize_activations(const GemvParams &p, const float *x0, int n_vec, const Q8View &a,
+                                     double *red, const float *normbuf, uint32_t normbar) {
     if (p.norm != nullptr) {
         // the norm weights were copied into shared memory before the kernel
         // waited for its predecessor
@@ -297,8 +304,8 @@ __device__ bool quantize_activations(const GemvParams &p, const Q8View &a, doubl
     const int nsb = p.cols / kQK;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_slabs = (nsb + kWarps - 1) / kWarps;
-    for (int e = 0; e < p.n; ++e) {
-        const float *x = p.x + static_cast<size_t>(e) * p.cols;
+    for (int e = 0; e < n_vec; ++e) {
+        const float *x = x0 + static_cast<size_t>(e) * p.cols;
         if (n_slabs <= kSlabMax) {
             float v[kSlabMax][8];
 #pragma unroll
@@ -442,7 +449,7 @@ __device__ __forceinline__ float dot_act(const unsigned char *blk, int part, con
 }
 
 // One CTA streams its p.rows_per_cta contiguous weight rows (of each matrix)
-// through a kStages-deep ring of bulk copies into shared memory, issued by a
+// through a ring of p.n_stages bulk-copy stages in shared memory, issued by a
 // producer warp: the first stages before waiting for the previous kernel,
 // the rest as stages are released.  Dependents are released at once, so
 // consecutive projections overlap their weight streams with each other's
@@ -464,18 +471,21 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
     const int row0 = blockIdx.x * p.rows_per_cta;
     const int nrows = max(0, min(p.rows, row0 + p.rows_per_cta) - row0);
     const int R = p.chunk_rows;
+    const int n_stages = p.n_stages;
+    const int stage_bytes = p.stage_bytes;
+    const int ring_bytes = n_stages * stage_bytes;
     const int n_chunks = (nrows + R - 1) / R;
     unsigned char *ring = smem;
-    const uint32_t full0 = smem_u32(smem + kRingBytes);
-    const uint32_t empty0 = full0 + 8 * kStages;
-    const uint32_t normbar = empty0 + 8 * kStages;
+    const uint32_t full0 = smem_u32(smem + ring_bytes);
+    const uint32_t empty0 = full0 + 8 * kMaxStages;
+    const uint32_t normbar = empty0 + 8 * kMaxStages;
     int m = 0, mrow0 = row0;
     if (MODE == kQkv) {
         m = row0 < p.row_end[0] ? 0 : (row0 < p.row_end[1] ? 1 : 2);
         mrow0 = row0 - (m == 0 ? 0 : p.row_end[m - 1]);
     }
     if (tid == 0) {
-        for (int st = 0; st < kStages; ++st) {
+        for (int st = 0; st < n_stages; ++st) {
             mbar_init(full0 + 8 * st, 1);
             mbar_init(empty0 + 8 * st, static_cast<uint32_t>(R));
         }
@@ -487,7 +497,7 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
     // own weight stream now.
     pdl_trigger();
 
-    unsigned char *after_ring = smem + kRingBytes + kBarBytes;
+    unsigned char *after_ring = smem + ring_bytes + kBarBytes;
     const Q8View a = carve_q8(after_ring, p.n, p.cols);
     float *normbuf = reinterpret_cast<float *>(after_ring + q8_smem_bytes(p.n, p.cols));  // [cols] if p.norm
     float *res = normbuf + (p.norm != nullptr ? p.cols : 0);  // kQkv [NB][32]
@@ -512,10 +522,10 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             }
             int issued = 0;
             for (int c = 0; c < n_chunks; ++c) {
-                if (c >= kStages) {  // wait until every row of chunk c - kStages is done
-                    const int prev = c - kStages;
-                    if (!mbar_wait_bounded(empty0 + 8 * (prev % kStages),
-                                           static_cast<uint32_t>((prev / kStages) & 1))) {
+                if (c >= n_stages) {  // wait until every row of chunk c - n_stages is done
+                    const int prev = c - n_stages;
+                    if (!mbar_wait_bounded(empty0 + 8 * (prev % n_stages),
+                                           static_cast<uint32_t>((prev / n_stages) & 1))) {
                         if (p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
                             p.err->where = HKV_KERNEL_GEMV;
                             p.err->a = blockIdx.x;
@@ -526,8 +536,8 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
                 }
                 const int r0 = c * R;
                 const uint32_t bytes = static_cast<uint32_t>(min(R, nrows - r0) * row_bytes);
-                const uint32_t stage = smem_u32(ring + (c % kStages) * kStageBytes);
-                const uint32_t bar = full0 + 8 * (c % kStages);
+                const uint32_t stage = smem_u32(ring + (c % n_stages) * stage_bytes);
+                const uint32_t bar = full0 + 8 * (c % n_stages);
                 mbar_arrive_expect_tx(bar, bytes * kMats);
 #pragma unroll
                 for (int k = 0; k < kMats; ++k) {
@@ -538,14 +548,15 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             }
             // the CTA must not exit with copies in flight: wait (bounded) for
             // the last copy issued into each stage
-            for (int c = max(0, issued - kStages); c < issued; ++c) {
-                mbar_wait_bounded(full0 + 8 * (c % kStages), static_cast<uint32_t>((c / kStages) & 1));
+            for (int c = max(0, issued - n_stages); c < issued; ++c) {
+                mbar_wait_bounded(full0 + 8 * (c % n_stages), static_cast<uint32_t>((c / n_stages) & 1));
             }
             if (p.norm != nullptr) mbar_wait_bounded(normbar, 0);
         }
     } else {
         pdl_wait();  // x (and y, residual) belong to the kernels before
-        if (!quantize_activations(p, a, a.red, normbuf, normbar)) {
+        const bool qok = quantize_activations(p, p.x, p.n, a, a.red, normbuf, normbar);
+        if (!qok) {
             if (tid == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
                 p.err->where = HKV_KERNEL_GEMV;
                 p.err->a = blockIdx.x;
@@ -562,8 +573,8 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             const int r = base + 4 * warp + qg;
             const bool has_row = r < nrows;
             const int c = has_row ? r / R : 0, rs = has_row ? r % R : 0;
-            const uint32_t full = full0 + 8 * (c % kStages);
-            const bool ok = !has_row || mbar_wait_bounded(full, static_cast<uint32_t>((c / kStages) & 1));
+            const uint32_t full = full0 + 8 * (c % n_stages);
+            const bool ok = !has_row || mbar_wait_bounded(full, static_cast<uint32_t>((c / n_stages) & 1));
             if (!__all_sync(0xffffffffu, ok)) {
                 if (lane == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
                     p.err->where = HKV_KERNEL_GEMV;
@@ -573,7 +584,7 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
                 bad = true;
                 break;
             }
-            const unsigned char *stage = ring + (c % kStages) * kStageBytes;
+            const unsigned char *stage = ring + (c % n_stages) * stage_bytes;
             float acc[kMats][NB][4];
 #pragma unroll
             for (int k = 0; k < kMats; ++k)
@@ -605,7 +616,7 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
                 }
             }
             __syncwarp();
-            if (has_row && l8 == 0) mbar_arrive(empty0 + 8 * (c % kStages));  // the row's bytes are read
+            if (has_row && l8 == 0) mbar_arrive(empty0 + 8 * (c % n_stages));  // the row's bytes are read
             float t[kMats][NB];
 #pragma unroll
             for (int k = 0; k < kMats; ++k)
@@ -825,9 +836,9 @@ __global__ void argmax_kernel(const float *logits, int32_t n_books, int32_t size
 }
 
 // ------------------------------------------------------------- launchers
-size_t gemv_smem(int mode, int nb, int n, int cols, int chunk_rows, bool has_norm) {
-    (void)chunk_rows;
-    size_t b = kRingBytes + kBarBytes + q8_smem_bytes(n, cols) + (has_norm ? static_cast<size_t>(cols) * 4 : 0);
+size_t gemv_smem(int mode, int nb, int n, int cols, int ring_bytes, bool has_norm) {
+    size_t b = static_cast<size_t>(ring_bytes) + kBarBytes + q8_smem_bytes(n, cols) +
+               (has_norm ? static_cast<size_t>(cols) * 4 : 0);
     if (mode == kQkv) b += static_cast<size_t>(nb) * kQkvRows * sizeof(float) + nb * sizeof(double) + 16;
     return b;
 }
@@ -865,7 +876,7 @@ int num_sms_of(int dev) {
 template <int MODE, int NB>
 cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     auto kern = gemv_kernel<MODE, NB>;
-    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.chunk_rows, p.norm != nullptr);
+    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.n_stages * p.stage_bytes, p.norm != nullptr);
     static std::mutex mu;
     static bool done[64] = {};
     int dev = 0;
@@ -906,18 +917,52 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-// Ring plan: CTAs of rows_per_cta contiguous rows (one per SM; 32 for q/k/v,
-// a quarter head each), stages of as many whole rows as fit kStageBytes.
+// Shared memory of a CTA that must fit twice on one SM (228 KB, less 1 KB
+// the hardware keeps per CTA).
+constexpr size_t kPairSmem = (228 - 2) * 1024 / 2;
+
+// Ring of a CTA whose rpc rows (unit bytes each, all matrices) are all in
+// flight: the fewest rows per stage that need no more than kMaxStages stages.
+void ring_all_in_flight(int rpc, int unit, GemvParams &p) {
+    p.chunk_rows = (rpc + kMaxStages - 1) / kMaxStages;
+    p.n_stages = (rpc + p.chunk_rows - 1) / p.chunk_rows;
+    p.stage_bytes = p.chunk_rows * unit;
+}
+
+// Ring plan.  CTAs take rows_per_cta contiguous rows: one CTA per SM (32 rows
+// for q/k/v, a quarter head, for the per-head norm).  A single vector whose
+// per-SM rows do not fit in one ring (the FFN's gate and up) is split over
+// two CTAs per SM when both rings then hold all their rows and two such
+// CTAs fit on an SM: every weight byte is then requested before the kernel
+// waits for its predecessor, instead of half of them in bursts after the
+// first rows are done.  A ring that cannot hold its CTA's rows streams them
+// through stages of about kStreamStageBytes.
 void plan_rows(GemvParams &p, int mode, int dev) {
     const int mats = mode == kSwiglu ? 2 : 1;
-    const int row_bytes = p.cols / kQK * kQ4Bytes;
+    const int unit = p.cols / kQK * kQ4Bytes * mats;
+    const bool has_norm = p.norm != nullptr;
     if (mode == kQkv) {
         p.rows_per_cta = kQkvRows;
     } else {
         const int sms = num_sms_of(dev);
         p.rows_per_cta = std::max(1, (p.rows + sms - 1) / sms);
+        if (p.n == 1 && static_cast<int64_t>(p.rows_per_cta) * unit > kRingCap) {
+            const int rpc2 = std::max(1, (p.rows + 2 * sms - 1) / (2 * sms));
+            GemvParams q = p;
+            ring_all_in_flight(rpc2, unit, q);
+            if (static_cast<int64_t>(rpc2) * unit <= kRingCap &&
+                gemv_smem(mode, 1, 1, p.cols, q.n_stages * q.stage_bytes, has_norm) <= kPairSmem) {
+                p.rows_per_cta = rpc2;
+            }
+        }
     }
-    p.chunk_rows = std::max(1, std::min(p.rows_per_cta, kStageBytes / (row_bytes * mats)));
+    if (static_cast<int64_t>(p.rows_per_cta) * unit <= kRingCap) {
+        ring_all_in_flight(p.rows_per_cta, unit, p);
+    } else {
+        p.chunk_rows = std::max(1, std::min(p.rows_per_cta, kStreamStageBytes / unit));
+        p.n_stages = std::max(2, std::min(kMaxStages, kRingCap / (p.chunk_rows * unit)));
+        p.stage_bytes = p.chunk_rows * unit;
+    }
 }
 
 template <int MODE>
@@ -929,8 +974,9 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
     // vectors per launch: at most kMaxVec, and as many as shared memory holds
     int vmax = kMaxVec;
     const size_t cap = static_cast<size_t>(smem_cap_of(dev));
-    while (vmax > 1 && gemv_smem(MODE, kMaxVec, vmax, p.cols, p.chunk_rows, p.norm != nullptr) > cap) --vmax;
-    if (gemv_smem(MODE, 1, 1, p.cols, p.chunk_rows, p.norm != nullptr) > cap) return cudaErrorInvalidValue;
+    const int ring_bytes = p.n_stages * p.stage_bytes;
+    while (vmax > 1 && gemv_smem(MODE, kMaxVec, vmax, p.cols, ring_bytes, p.norm != nullptr) > cap) --vmax;
+    if (gemv_smem(MODE, 1, 1, p.cols, ring_bytes, p.norm != nullptr) > cap) return cudaErrorInvalidValue;
     const int n_total = p.n;
     for (int e0 = 0; e0 < n_total; e0 += vmax) {
         GemvParams q = p;
