@@ -285,6 +285,71 @@ __device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View
     if (lane == 0) a.d[e * nsb + b] = d;
 }
 
+// The same quantisation for the blocks a warp holds in registers, one per
+// slab (block sl * kWarps + warp of slab sl), the slabs' chains interleaved.
+// The block maximum: the largest |x| bit pattern by one warp reduction
+// (non-negative floats order as unsigned integers), then the lowest lane
+// holding it (ballot), whose own first maximum is the block's first one --
+// lane l holds elements 8l .. 8l + 7, so lower lanes hold lower indices.
+template <int S>
+__device__ __forceinline__ void quantize_blocks(const float (&v)[S][8], int n_slabs, const Q8View &a, int cols,
+                                                int nsb, int e, int warp, int lane) {
+    float mx[S];
+    uint32_t am[S];
+#pragma unroll
+    for (int sl = 0; sl < S; ++sl) {
+        float best = 0.0f, val = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float ax = fabsf(v[sl][i]);
+            if (ax > best) {
+                best = ax;
+                val = v[sl][i];
+            }
+        }
+        am[sl] = __float_as_uint(best);
+        mx[sl] = val;
+    }
+#pragma unroll
+    for (int sl = 0; sl < S; ++sl) {
+        const uint32_t top = __reduce_max_sync(0xffffffffu, am[sl]);
+        const uint32_t holders = __ballot_sync(0xffffffffu, am[sl] == top);
+        mx[sl] = __shfl_sync(0xffffffffu, mx[sl], __ffs(static_cast<int>(holders)) - 1);
+        am[sl] = top;
+    }
+#pragma unroll
+    for (int sl = 0; sl < S; ++sl) {
+        const int b = sl * kWarps + warp;
+        if (sl >= n_slabs || b >= nsb) continue;
+        int q[8];
+        float d = 0.0f;
+        if (am[sl] == 0u) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = 0;
+        } else {
+            const float iscale = -127.0f / mx[sl];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, v[sl][i])));
+            d = 1.0f / iscale;
+        }
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            lo |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
+            hi |= (static_cast<uint32_t>(q[i + 4]) & 0xFFu) << (8 * i);
+        }
+        *reinterpret_cast<uint2 *>(a.q + static_cast<size_t>(e) * cols + q8_offset(b * 4 + (lane >> 3), (lane & 7) >> 1) +
+                                   (lane & 1) * 8) = make_uint2(lo, hi);
+        int qs = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qs += q[i];
+        qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+        qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+        if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
+        if (lane == 0) a.d[e * nsb + b] = d;
+    }
+}
+
 constexpr int kSlabMax = 5;  // 2048-element slabs held in registers (cols <= 10240)
 
 // Q8_K image of the n activation vectors, optionally of rms_norm(x) * norm
@@ -347,10 +412,24 @@ __device__ bool quantize_activations(const GemvParams &p, const float *x0, int n
                     }
                 }
             }
+            // slabs past the row hold zeros (their blocks are skipped)
 #pragma unroll
             for (int sl = 0; sl < kSlabMax; ++sl) {
                 const int b = sl * kWarps + warp;
-                if (sl < n_slabs && b < nsb) quantize_block(v[sl], a, p.cols, nsb, e, b, lane);
+                if (!(sl < n_slabs && b < nsb)) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[sl][i] = 0.0f;
+                }
+            }
+            if (n_slabs <= 2) {
+                float w2[2][8];
+#pragma unroll
+                for (int sl = 0; sl < 2; ++sl)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) w2[sl][i] = v[sl][i];
+                quantize_blocks<2>(w2, n_slabs, a, p.cols, nsb, e, warp, lane);
+            } else {
+                quantize_blocks<kSlabMax>(v, n_slabs, a, p.cols, nsb, e, warp, lane);
             }
             consumer_sync();  // red[] is reused by the next vector
         } else {
