@@ -478,8 +478,7 @@ def bench_ours(args):
         tfile = REPO / "profiles" / "attention_traffic.json"
         if tfile.exists():
             t = json.loads(tfile.read_text())
-            if t.get("workload") == args.workload:
-                traffic = t.get("dram_bytes_per_launch")
+            traffic = t.get("dram_bytes_per_launch", {}).get(args.workload)
         line = {
             "metric": METRIC,
             "value": value,
