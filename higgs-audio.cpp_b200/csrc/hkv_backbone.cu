@@ -728,28 +728,31 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
 
     if (MODE == kQkv) {
         // q / k / v rows; the 4 CTAs of a cluster hold the 128 rows of one
-        // head.  Every thread of every CTA takes the barriers, even after a
-        // timeout.
+        // head.  Each CTA stores its sums of squares into slot (its rank) of
+        // every CTA of the cluster, so after the one cluster barrier each CTA
+        // reads only its own shared memory and may leave at once.  Every
+        // thread of every CTA takes the barriers, even after a timeout.
         bad = __syncthreads_or(bad) != 0;
-        double *part_ss = reinterpret_cast<double *>(res + NB * kQkvRows);  // [NB]
+        double *part_ss = reinterpret_cast<double *>(res + NB * kQkvRows);  // [kClusterCtas][NB]
         cg::cluster_group cl = cg::this_cluster();
         const bool normed = m < 2;  // the same for every CTA of the cluster
+        const int rank = static_cast<int>(cl.block_rank());
         if (normed && warp == 0) {
             for (int e = 0; e < p.n; ++e) {
                 const float v = bad ? 0.0f : res[e * kQkvRows + lane];
                 const double ss = warp_sum_double(static_cast<double>(__fmul_rn(v, v)));
-                if (lane == 0) part_ss[e] = ss;
+                if (lane < kClusterCtas) *cl.map_shared_rank(part_ss + rank * NB + e, lane) = ss;
             }
         }
         cl.sync();
         __shared__ float scale_s[NB];
         if (normed && tid < p.n) {
             double total = 0.0;
-            for (int r = 0; r < kClusterCtas; ++r) total += *cl.map_shared_rank(part_ss + tid, r);
+            for (int r = 0; r < kClusterCtas; ++r) total += part_ss[r * NB + tid];
             const float mean = static_cast<float>(total / static_cast<double>(kHeadDim));
             scale_s[tid] = 1.0f / sqrtf(mean + p.eps);
         }
-        cl.sync();  // every CTA has read its peers' sums before any of them exits
+        __syncthreads();
         if (!bad) {
             const int dim0 = static_cast<int>(cl.block_rank()) * kQkvRows;
             for (int i = tid; i < p.n * kQkvRows; i += kThreads + 32) {
@@ -918,7 +921,7 @@ __global__ void argmax_kernel(const float *logits, int32_t n_books, int32_t size
 size_t gemv_smem(int mode, int nb, int n, int cols, int ring_bytes, bool has_norm) {
     size_t b = static_cast<size_t>(ring_bytes) + kBarBytes + q8_smem_bytes(n, cols) +
                (has_norm ? static_cast<size_t>(cols) * 4 : 0);
-    if (mode == kQkv) b += static_cast<size_t>(nb) * kQkvRows * sizeof(float) + nb * sizeof(double) + 16;
+    if (mode == kQkv) b += static_cast<size_t>(nb) * kQkvRows * sizeof(float) + kClusterCtas * nb * sizeof(double) + 16;
     return b;
 }
 
