@@ -77,6 +77,7 @@ struct GemvParams {
     int32_t chunk_rows;       // rows per ring stage
     int32_t n_stages;         // ring stages (<= kMaxStages)
     int32_t stage_bytes;      // chunk_rows * row bytes * matrices
+    int32_t lanes_per_row;    // 8 or 16 consumer lanes share a row's dot product
     DeviceError *err;         // bounded-wait timeouts are recorded here
 };
 
@@ -533,7 +534,7 @@ __device__ __forceinline__ float dot_act(const unsigned char *blk, int part, con
 // the rest as stages are released.  Dependents are released at once, so
 // consecutive projections overlap their weight streams with each other's
 // activation prologue and tail.  Each of the kWarps consumer warps owns whole
-// rows, four at a time, 8 lanes per row; a lane's items are independent
+// rows, 32 / p.lanes_per_row at a time; a lane's items are independent
 // dot products kept in four accumulators (the latency of one Q4_K x Q8_K
 // item is the limit at batch 1, not bandwidth); the row sum is a fixed-order
 // shuffle reduction (deterministic), and the row's stage slot is released by
@@ -643,13 +644,16 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             }
             bad = true;
         }
-        // 8 lanes per row: lane group q = lane / 8 of warp w takes CTA rows
-        // 4w + q, 4w + q + 32, ...; within a row, lane l8 = lane % 8 takes
-        // items l8, l8 + 8, ... with four independent accumulators.
+        // L = p.lanes_per_row lanes per row: lane group q = lane / L of warp
+        // w takes CTA rows (32 / L) w + q, then the same plus 32 kWarps / L,
+        // ...; within a row, lane l = lane % L takes items l, l + L, ...
+        // with four independent accumulators.
         const int items = nsb * 4;
-        const int qg = lane >> 3, l8 = lane & 7;
-        for (int base = 0; base < nrows && !bad; base += 4 * kWarps) {
-            const int r = base + 4 * warp + qg;
+        const int lpr = p.lanes_per_row;
+        const int rows_per_warp = 32 / lpr;
+        const int qg = lane / lpr, l8 = lane % lpr;
+        for (int base = 0; base < nrows && !bad; base += rows_per_warp * kWarps) {
+            const int r = base + rows_per_warp * warp + qg;
             const bool has_row = r < nrows;
             const int c = has_row ? r / R : 0, rs = has_row ? r % R : 0;
             const uint32_t full = full0 + 8 * (c % n_stages);
@@ -672,10 +676,10 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) acc[k][e][u] = 0.0f;
             if (has_row) {
-                for (int j0 = l8; j0 < items; j0 += 32) {
+                for (int j0 = l8; j0 < items; j0 += 4 * lpr) {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int j = j0 + 8 * u;
+                        const int j = j0 + lpr * u;
                         if (j < items) {
                             const int sb = j >> 2, part = j & 3;
 #pragma unroll
@@ -703,7 +707,9 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
                 for (int e = 0; e < NB; ++e) {
                     float v = (acc[k][e][0] + acc[k][e][1]) + (acc[k][e][2] + acc[k][e][3]);
 #pragma unroll
-                    for (int off = 4; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                    for (int off = 8; off > 0; off >>= 1) {
+                        if (off < lpr) v += __shfl_xor_sync(0xffffffffu, v, off);
+                    }
                     t[k][e] = v;
                 }
             if (has_row && l8 == 0) {
@@ -1011,32 +1017,59 @@ void ring_all_in_flight(int rpc, int unit, GemvParams &p) {
     p.stage_bytes = p.chunk_rows * unit;
 }
 
-// Ring plan.  CTAs take rows_per_cta contiguous rows: one CTA per SM (32 rows
-// for q/k/v, a quarter head, for the per-head norm).  A single vector whose
-// per-SM rows do not fit in one ring (the FFN's gate and up) is split over
-// two CTAs per SM when both rings then hold all their rows and two such
-// CTAs fit on an SM: every weight byte is then requested before the kernel
-// waits for its predecessor, instead of half of them in bursts after the
-// first rows are done.  A ring that cannot hold its CTA's rows streams them
-// through stages of about kStreamStageBytes.
+// Dependent item iterations of a CTA's dot products (passes over its rows
+// times item rounds per pass) with lpr lanes per row.
+int dot_rounds(int rpc, int items, int lpr) {
+    const int slots = kWarps * (32 / lpr);
+    return ((rpc + slots - 1) / slots) * ((items + 4 * lpr - 1) / (4 * lpr));
+}
+
+// Lanes per row: 16 when a CTA's rows then all fit in one pass (two rows per
+// consumer warp), else 8.  Fewer lanes per row only moved the work onto
+// fewer warps (gate/up: 4 lanes per row was 3% slower than 8).
+int plan_lanes(int rpc) { return rpc <= kWarps * 2 ? 16 : 8; }
+
+// Rows per CTA of a single-vector launch: one CTA per SM (32 rows for
+// q/k/v, a quarter head, for the per-head norm), or two CTAs per SM when
+// that needs fewer dependent dot-product rounds (half the rows each, more
+// lanes per row) and both rings then hold all their rows in shared memory
+// that two CTAs can share -- which is always the case for the FFN's gate and
+// up, whose rows per SM do not fit one ring: every weight byte is then
+// requested before the kernel waits for its predecessor, instead of half of
+// them in bursts after the first rows are done.
+int single_vector_rows(const GemvParams &p, int mode, int dev) {
+    if (mode == kQkv) return kQkvRows;
+    const int mats = mode == kSwiglu ? 2 : 1;
+    const int unit = p.cols / kQK * kQ4Bytes * mats;
+    const int items = p.cols / kQK * 4;
+    const int sms = num_sms_of(dev);
+    const int rpc1 = std::max(1, (p.rows + sms - 1) / sms);
+    const int rpc2 = std::max(1, (p.rows + 2 * sms - 1) / (2 * sms));
+    GemvParams q = p;
+    ring_all_in_flight(rpc2, unit, q);
+    const bool pair_fits = static_cast<int64_t>(rpc2) * unit <= kRingCap &&
+                           gemv_smem(mode, 1, 1, p.cols, q.n_stages * q.stage_bytes, p.norm != nullptr) <= kPairSmem;
+    const bool one_fits = static_cast<int64_t>(rpc1) * unit <= kRingCap;
+    const int r1 = dot_rounds(rpc1, items, plan_lanes(rpc1));
+    const int r2 = dot_rounds(rpc2, items, plan_lanes(rpc2));
+    return pair_fits && (!one_fits || r2 < r1) ? rpc2 : rpc1;
+}
+
+// Ring plan.  A single vector takes single_vector_rows; several vectors one
+// CTA per SM.  The lanes per row -- and with them the order in which a row's
+// products are summed -- come from the single-vector plan of the shape, so a
+// vector's results do not depend on how many others share the launch.  A
+// ring that cannot hold its CTA's rows streams them through stages of about
+// kStreamStageBytes.
 void plan_rows(GemvParams &p, int mode, int dev) {
     const int mats = mode == kSwiglu ? 2 : 1;
     const int unit = p.cols / kQK * kQ4Bytes * mats;
-    const bool has_norm = p.norm != nullptr;
-    if (mode == kQkv) {
-        p.rows_per_cta = kQkvRows;
+    const int rpc_single = single_vector_rows(p, mode, dev);
+    if (mode == kQkv || p.n == 1) {
+        p.rows_per_cta = rpc_single;
     } else {
         const int sms = num_sms_of(dev);
         p.rows_per_cta = std::max(1, (p.rows + sms - 1) / sms);
-        if (p.n == 1 && static_cast<int64_t>(p.rows_per_cta) * unit > kRingCap) {
-            const int rpc2 = std::max(1, (p.rows + 2 * sms - 1) / (2 * sms));
-            GemvParams q = p;
-            ring_all_in_flight(rpc2, unit, q);
-            if (static_cast<int64_t>(rpc2) * unit <= kRingCap &&
-                gemv_smem(mode, 1, 1, p.cols, q.n_stages * q.stage_bytes, has_norm) <= kPairSmem) {
-                p.rows_per_cta = rpc2;
-            }
-        }
     }
     if (static_cast<int64_t>(p.rows_per_cta) * unit <= kRingCap) {
         ring_all_in_flight(p.rows_per_cta, unit, p);
@@ -1045,6 +1078,7 @@ void plan_rows(GemvParams &p, int mode, int dev) {
         p.n_stages = std::max(2, std::min(kMaxStages, kRingCap / (p.chunk_rows * unit)));
         p.stage_bytes = p.chunk_rows * unit;
     }
+    p.lanes_per_row = plan_lanes(rpc_single);
 }
 
 template <int MODE>
