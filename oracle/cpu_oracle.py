@@ -1,7 +1,7 @@
 """ctypes view of the CPU oracle (oracle/hkv_oracle.c, oracle/hkv_oracle_graph.c).
 
 TEST AND MEASUREMENT INFRASTRUCTURE.  Imported only by tests/, by
-__graft_entry__.smoke() as the checker, and by bench.py's CPU-baseline leg and
+__graft_entry__.smoke() as the reference result, and by bench.py's CPU-baseline leg and
 `--impl reference` arm.  The engine never imports it.
 
 Pinning (see the C file header): append and layout are pinned by the

@@ -3,8 +3,8 @@
  *
  * TEST INFRASTRUCTURE ONLY.  Nothing in the product (libhkv.so, the package's
  * host code) links, loads or calls this file.  It is used by tests/ as the
- * parity checker, by __graft_entry__.smoke() as the checker of one tiny GPU
- * run, and by bench.py as the timed CPU baseline / reference arm.
+ * parity reference, by __graft_entry__.smoke() to check one tiny GPU run,
+ * and by bench.py as the timed CPU baseline / reference arm.
  *
  * Reference: bluryar/higgs-audio.cpp, src/higgs_pipeline.cpp.  The reference's
  * arithmetic lives in the ggml submodule (ggml-org/ggml, README.md:32 pins

@@ -1,6 +1,6 @@
 """The oracle against the reference's known answers and golden fixtures (CPU).
 
-Before the oracle is trusted as the GPU path's checker it is pinned here:
+Before the oracle is trusted as the reference for the GPU path it is pinned here:
   * its BF16 RoPE table against the reference's own table code (fixture made
     by compiling make_bf16_rope_table from the reference source);
   * its F16 conversion against numpy's float16 (round to nearest even);
