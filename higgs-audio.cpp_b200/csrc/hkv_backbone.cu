@@ -43,12 +43,15 @@
 #include <vector>
 
 #include "../../include/hkv.h"
+#include "hkv_device.cuh"
 #include "hkv_internal.h"
 
 namespace cg = cooperative_groups;
 
 namespace hkv {
 namespace bb {
+
+using namespace dev;
 
 constexpr int kQK = 256;        // weights per Q4_K / Q8_K block
 constexpr int kQ4Bytes = 144;   // bytes per Q4_K block
@@ -90,67 +93,11 @@ constexpr int kMaxStages = 12;
 constexpr int kRingCap = 100 * 1024;
 constexpr int kStreamStageBytes = 24 * 1024;
 constexpr int kBarBytes = 208;              // kMaxStages full + kMaxStages empty + 1 norm mbarrier
-constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int kQkvRows = 32;                // rows per CTA in the q/k/v launch (4 per head)
 static_assert(2 * kMaxStages * 8 + 8 <= kBarBytes && kBarBytes % 16 == 0, "mbarrier area too small");
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 __device__ __forceinline__ int4 ld_stream(const uint8_t *p) {
     return __ldcs(reinterpret_cast<const int4 *>(p));
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-// True when the phase with `parity` completed within the budget.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (clock64() - t0 < kWaitBudgetCycles) {
-        if (mbar_try_wait(bar, parity)) return true;
-    }
-    return false;
-}
-// 1-D bulk copy global -> this CTA's shared memory (no tensor map, no
-// multicast); completion counted in transaction bytes on `bar`.  Weights
-// are read once per step: evict-first in L2.
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
-                                          uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
-        : "memory");
-}
-__device__ __forceinline__ uint64_t evict_first_policy() {
-    uint64_t policy;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    return policy;
 }
 
 __device__ __forceinline__ float half_bits(uint32_t bits16) {

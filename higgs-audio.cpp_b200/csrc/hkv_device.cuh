@@ -1,0 +1,94 @@
+// hkv_device.cuh -- device helpers shared by the attention kernels
+// (hkv_kernels.cu) and the projection kernels (hkv_backbone.cu): mbarriers
+// with bounded waits, 1-D bulk copies into shared memory with an L2 cache
+// hint, and the controls of programmatic dependent launch.
+//
+// Every wait is bounded by kWaitBudgetCycles of the SM clock; a caller that
+// sees a wait give up records an error code and leaves instead of spinning.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hkv {
+namespace dev {
+
+constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ mbarrier
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// True when the phase with `parity` completed within the budget.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) {
+        return true;
+    }
+    const long long t0 = clock64();
+    while (clock64() - t0 < kWaitBudgetCycles) {
+        if (mbar_try_wait(bar, parity)) {
+            return true;
+        }
+    }
+    return false;
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (bulk copy) accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// --------------------------------------------------------------- bulk copy
+// 1-D bulk copy global -> this CTA's shared memory (no tensor map, no
+// multicast); completion is counted in transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+// L2 policy for data read once per step (the KV stream, the weights).
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+// ---------------------------------------------- programmatic dependent launch
+// Waits until the kernels this one depends on have finished and their
+// writes are visible (no-op when launched without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream start its prologue.
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace dev
+}  // namespace hkv

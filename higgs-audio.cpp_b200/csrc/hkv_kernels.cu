@@ -30,10 +30,13 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "hkv_device.cuh"
 #include "hkv_internal.h"
 
 namespace hkv {
 namespace {
+
+using namespace dev;
 
 constexpr int kStageBytes = 2 * kHeadBlockBytes;  // K block + V block
 constexpr int kQcStride = 136;                     // halves per staged-query row (272 B)
@@ -46,7 +49,6 @@ constexpr int kWarpSmem = kAttnStages * kStageBytes + kQcBytes + kPBufBytes + kB
 constexpr int kCtaPartFloats = kGqa * kHeadDim + 2 * kGqa;
 constexpr int kCtaPartBytes = kCtaPartFloats * 4;
 constexpr int kCtaSmem = kAttnWarps * 2 * kCtaPartBytes + 32;
-constexpr long long kWaitBudgetCycles = 4000000000LL;  // about 2 s at 2 GHz
 constexpr int kWhereAppend = 0;
 constexpr int kWhereAttn = 1;
 constexpr int kWhereGather = 3;
@@ -64,65 +66,6 @@ __device__ __forceinline__ void record_error(DeviceError *err, int code, int whe
         err->a = a;
         err->b = b;
     }
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-// ------------------------------------------------------------ mbarrier/TMA
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait: true when the phase with `parity` completed.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) {
-        return true;
-    }
-    const long long t0 = clock64();
-    while (clock64() - t0 < kWaitBudgetCycles) {
-        if (mbar_try_wait(bar, parity)) {
-            return true;
-        }
-    }
-    return false;
-}
-__device__ __forceinline__ void fence_barrier_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-// 1-D bulk copy global -> shared (no tensor map, no multicast), completion
-// reported as transaction bytes on `bar`.  The KV stream is read once per
-// step, so it is marked evict-first in L2.
-__device__ __forceinline__ void tma_load_1d(uint32_t dst, const void *src, uint32_t bytes,
-                                            uint32_t bar, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
-        : "memory");
-}
-__device__ __forceinline__ uint64_t l2_evict_first_policy() {
-    uint64_t policy;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    return policy;
 }
 
 // ------------------------------------------------------- ldmatrix / mma
@@ -302,8 +245,8 @@ __device__ __forceinline__ void issue_unit(const PoolView &pool, int layer, int6
         head_block_index(page, layer, 0, h, pool.n_pages, pool.n_head_kv) * kHeadBlockBytes;
     const uint8_t *vb = kb + static_cast<int64_t>(pool.n_head_kv) * kHeadBlockBytes;
     mbar_arrive_expect_tx(bar, kStageBytes);
-    tma_load_1d(stage, kb, kHeadBlockBytes, bar, policy);
-    tma_load_1d(stage + kHeadBlockBytes, vb, kHeadBlockBytes, bar, policy);
+    bulk_load(stage, kb, kHeadBlockBytes, bar, policy);
+    bulk_load(stage + kHeadBlockBytes, vb, kHeadBlockBytes, bar, policy);
 }
 
 // The new K/V row of one (slot, KV head): lanes 0-15 rope and convert the
@@ -648,7 +591,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     const uint32_t qc = stage0 + kAttnStages * kStageBytes;
     const uint32_t pbuf = qc + kQcBytes;
     const uint32_t bar0 = pbuf + kPBufBytes;
-    const uint64_t policy = l2_evict_first_policy();
+    const uint64_t policy = evict_first_policy();
 
     if (lane == 0) {
 #pragma unroll

@@ -22,7 +22,8 @@ LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libhkv.so"
 SOURCES = [CSRC / "hkv_kernels.cu", CSRC / "hkv_engine.cpp", CSRC / "hkv_noalloc.cu",
            CSRC / "hkv_backbone.cu"]
-HEADERS = [CSRC / "hkv_internal.h", CSRC / "hkv_plan.h", REPO / "include" / "hkv.h"]
+HEADERS = [CSRC / "hkv_internal.h", CSRC / "hkv_plan.h", CSRC / "hkv_device.cuh",
+           REPO / "include" / "hkv.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
