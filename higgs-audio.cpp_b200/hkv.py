@@ -166,6 +166,7 @@ SIGNATURES = {
     "hkv_rope_tables": ([_P, _P, _P], ctypes.c_int),
     "hkv_decode_attn_noalloc": ([ctypes.POINTER(PagedView), _I32, _I32, _I32P, _I32P, _I32P,
                                  _P, _P, _P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
+    "hkv_decode_attn_noalloc_sync_check": ([_P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
     "hkv_split_export": ([_P, _I32, _I32, _P], ctypes.c_int),
     "hkv_split_connect": ([_P, _P], ctypes.c_int),
     "hkv_split_step": ([_P, _I32, _I32, _I32P, _P, _P, _P, _P], ctypes.c_int),
@@ -467,6 +468,14 @@ def decode_attn_noalloc(view: PagedView, layer: int, pos: Sequence[int],
     if st != HKV_OK:
         cls = HkvRangeError if st == HKV_ERR_RANGE else HkvError
         raise cls(st, msg.value.decode())
+
+
+def decode_attn_noalloc_sync_check(stream=None, lib: Optional[ctypes.CDLL] = None) -> None:
+    """hkv_decode_attn_noalloc_sync_check: synchronise `stream` and raise if a
+    no-allocation call recorded a device-side error since the last check."""
+    lib = lib or load_library()
+    msg = ctypes.create_string_buffer(512)
+    _raise_msg(lib.hkv_decode_attn_noalloc_sync_check(_stream(stream), msg, len(msg)), msg)
 
 
 class DeviceArray:

@@ -299,11 +299,24 @@ typedef struct hkv_paged_view {
  * needs more is rejected with HKV_ERR_RANGE and a message in err_msg (which
  * may be NULL).  The first call on a device looks the array's address up
  * (cudaGetSymbolAddress); make that first call before any stream capture.
- * All calls share the array: calls that overlap on the GPU race. */
+ * All calls share the array: calls that overlap on the GPU race.  A kernel
+ * that gives up on a bounded wait or meets a bad page id records it in the
+ * array's error word and returns; the word keeps its first record until
+ * hkv_decode_attn_noalloc_sync_check reads it, so check after the calls whose
+ * outputs you use. */
 int hkv_decode_attn_noalloc(const hkv_paged_view *view, int32_t layer, int32_t n,
                             const int32_t *pos, const int32_t *page_off, const int32_t *pages,
                             const float *q_prerope, float *out, hkv_stream stream,
                             char *err_msg, size_t err_len);
+
+/* The error check of hkv_decode_attn_noalloc (also no counterpart in the
+ * reference, and it allocates nothing either): synchronises `stream`, reads
+ * the static array's error word on the current device and clears it.
+ * HKV_OK if no call since the last check recorded an error; HKV_ERR_TIMEOUT
+ * (a bounded wait gave up) or HKV_ERR_DEVICE (a bad page id reached a kernel)
+ * otherwise, with a message in err_msg (which may be NULL): the output of the
+ * call that recorded it is invalid. */
+int hkv_decode_attn_noalloc_sync_check(hkv_stream stream, char *err_msg, size_t err_len);
 
 /* ------------------------------------------- Q4_K backbone projections -- */
 /* The projections around the KV path in the reference's decode graph

@@ -36,6 +36,33 @@ def build(force: bool = False) -> Path:
     return LIB_PATH
 
 
+def reference_checkout():
+    """Location of a checkout of the reference (bluryar/higgs-audio.cpp), or
+    None: the HKV_REFERENCE environment variable, else a directory named
+    `reference` beside this repository.  Only the RoPE-table pin
+    (oracle/ref_rope_table.sh) reads it."""
+    import os
+    env = os.environ.get("HKV_REFERENCE")
+    cands = [Path(env)] if env else [HERE.parents[1] / "reference"]
+    for c in cands:
+        if (c / "src" / "higgs_pipeline.cpp").is_file():
+            return c
+    return None
+
+
+def build_reference_table_code() -> bool:
+    """Compiles the reference's own RoPE-table code into oracle/_ref/ when a
+    checkout is available; returns False (with a message) when it is not."""
+    ref = reference_checkout()
+    if ref is None:
+        print("oracle/_ref not built: no reference checkout (set HKV_REFERENCE); the RoPE "
+              "table stays pinned by tests/golden/rope_table_ref.npz")
+        return False
+    subprocess.run([str(HERE / "ref_rope_table.sh"), str(ref)], check=True,
+                   stdout=subprocess.DEVNULL)
+    return True
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:

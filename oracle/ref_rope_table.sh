@@ -10,8 +10,12 @@
 # committed), next to a shim for the two ggml bf16 conversions they call
 # (upstream ggml's published round-to-nearest-even conversion) and the
 # reference's own include/higgs_audio.h for TextConfig.
+#
+# Usage: oracle/ref_rope_table.sh <reference checkout>   (or HKV_REFERENCE=<checkout>)
+# There is no default location: without one the script says so and exits 2.
 set -euo pipefail
-REF=${HKV_REFERENCE:-/root/reference}
+REF=${1:-${HKV_REFERENCE:-}}
+[ -n "$REF" ] || { echo "no reference checkout given (argument or HKV_REFERENCE)" >&2; exit 2; }
 HERE="$(cd "$(dirname "$0")" && pwd)"
 OUT="$HERE/_ref"
 SRC="$REF/src/higgs_pipeline.cpp"

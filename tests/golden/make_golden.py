@@ -31,7 +31,6 @@ from __future__ import annotations
 
 import ctypes
 import hashlib
-import subprocess
 import sys
 from pathlib import Path
 
@@ -49,8 +48,8 @@ ROWS = np.array([0, 1, 2, 3, 15, 16, 17, 100, 511, 512, 513, 1000, 2047, 4095, 4
 
 def reference_rope_table():
     so = REPO / "oracle" / "_ref" / "libref_rope.so"
-    subprocess.run([str(REPO / "oracle" / "ref_rope_table.sh")], check=True,
-                   stdout=subprocess.DEVNULL)
+    if not cpu_oracle.build_reference_table_code():
+        raise SystemExit("rope_table_ref.npz needs a reference checkout (HKV_REFERENCE)")
     lib = ctypes.CDLL(str(so))
     lib.ref_rope_table.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                    ctypes.c_void_p, ctypes.c_void_p]

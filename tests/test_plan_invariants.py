@@ -152,6 +152,9 @@ def walk(plan_dump, npages, G=8, w_full=148 * 6):
     assert got["part2"] == [sum(n_groups[:i]) for i in range(n_seg + 1)]
     assert got["n_parts"] <= W + n_seg  # the engine's partial capacity
     assert sum(n_groups) <= (W + n_seg) // 8 + n_seg
+    # the tighter bound the no-allocation entry point sizes its scratch by
+    parts_bound = W + n_seg
+    assert sum(n_groups) <= parts_bound // 8 + parts_bound // 17 + 1
     # the cost bound: no share costs more than B, and B is not loose
     span = WPC if ref["cta_merge"] else 1
     starts, segs = ref["starts"], ref["segs"]

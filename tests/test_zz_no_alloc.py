@@ -7,10 +7,13 @@ memory they already own: a page pool in the engine's documented layout, the
 RoPE tables, q and out; its own working memory is a fixed static array.
 
 Here the engine fills its cache as usual, the same rows (read back through
-hkv_gather) are laid into a caller-owned pool on different physical pages,
-and two calls in a row of the new entry point must match the engine's
-hkv_decode_attn within the parity tolerance.  This file is collected last on
-purpose (a failure here comes after every other test has run).
+hkv_gather, and checked bit for bit against the oracle's own append) are laid
+into a caller-owned pool on different physical pages, and two calls in a row
+of the new entry point must match both the engine's hkv_decode_attn and the
+oracle (exact and ggml_f16 modes) within the parity tolerance, with
+hkv_decode_attn_noalloc_sync_check reporting no device-side error after each.
+This file is collected last on purpose (a failure here comes after every other
+test has run).
 """
 from __future__ import annotations
 
@@ -55,34 +58,44 @@ def caller_pool(rows_by_slot, layer, n_layers):
     return torch.from_numpy(pool.view(np.int16)).to(DEV), page_lists
 
 
-def test_noalloc_matches_engine_on_two_calls(hkv_lib):
+def test_noalloc_matches_engine_and_oracle_on_two_calls(hkv_lib, oracle, rope_tables):
     import hkv
     import synth
 
+    cos_t, sin_t = rope_tables
     eng = hkv.Engine(n_layers=L, n_pages=256, max_slots=4, device=0, shuffle_seed=99,
                      lib=hkv_lib)
     stream = torch.cuda.current_stream().cuda_stream
     lens = [37, 300, 1000]
     slots = [eng.acquire(n + 1) for n in lens]
-    for i, (s, n) in enumerate(zip(slots, lens)):
-        for layer in range(L):
-            k = torch.from_numpy(synth.normal(50 + 10 * i + layer, (n, G, D))).to(DEV)
-            v = torch.from_numpy(synth.normal(80 + 10 * i + layer, (n, G, D))).to(DEV)
-            eng.rope_append_range(layer, s, n, k, v, stream)
-        eng.advance([s], n)
     layer = 1
-    k_new = torch.from_numpy(synth.normal(7, (3, G, D))).to(DEV)
-    v_new = torch.from_numpy(synth.normal(8, (3, G, D))).to(DEV)
-    eng.rope_append(layer, slots, k_new, v_new, stream)
+    expect = []  # the oracle's rows of `layer`, [0, n] of each slot
+    k_new = synth.normal(7, (3, G, D))
+    v_new = synth.normal(8, (3, G, D))
+    for i, (s, n) in enumerate(zip(slots, lens)):
+        for lay in range(L):
+            k = synth.normal(50 + 10 * i + lay, (n, G, D))
+            v = synth.normal(80 + 10 * i + lay, (n, G, D))
+            eng.rope_append_range(lay, s, n, torch.from_numpy(k).to(DEV),
+                                  torch.from_numpy(v).to(DEV), stream)
+            if lay == layer:
+                k16, v16 = oracle.append_rows(k, v, np.arange(n), cos_t, sin_t)
+                kn, vn = oracle.append_rows(k_new[i:i + 1], v_new[i:i + 1], np.array([n]),
+                                            cos_t, sin_t)
+                expect.append((np.concatenate([k16, kn]), np.concatenate([v16, vn])))
+        eng.advance([s], n)
+    eng.rope_append(layer, slots, torch.from_numpy(k_new).to(DEV),
+                    torch.from_numpy(v_new).to(DEV), stream)
 
-    # the rows the engine now holds, [0, used] of each slot
+    # the rows the engine now holds, [0, used] of each slot: bit-exact
     rows = []
-    for s, n in zip(slots, lens):
+    for s, n, (ek, ev) in zip(slots, lens, expect):
         kb = torch.empty((n + 1, G, D), dtype=torch.int16, device=DEV)
         vb = torch.empty_like(kb)
         eng.gather(s, layer, 0, n + 1, kb, vb, stream)
         torch.cuda.synchronize()
         rows.append((kb.cpu().numpy().view(np.uint16), vb.cpu().numpy().view(np.uint16)))
+        assert np.array_equal(rows[-1][0], ek) and np.array_equal(rows[-1][1], ev)
     pool, page_lists = caller_pool(rows, layer, L)
     cos, sin = eng.rope_tables()
     cos_d = torch.from_numpy(cos).to(DEV)
@@ -92,16 +105,24 @@ def test_noalloc_matches_engine_on_two_calls(hkv_lib):
 
     calls = [([0, 1, 2], 11), ([2, 0], 12)]  # two calls in a row, different batches
     for order, seed in calls:
-        q = torch.from_numpy(synth.normal(seed, (len(order), H, D))).to(DEV)
+        qh = synth.normal(seed, (len(order), H, D))
+        q = torch.from_numpy(qh).to(DEV)
         ref = torch.empty((len(order), H * D), device=DEV)
         got = torch.full((len(order), H * D), float("nan"), device=DEV)
         eng.decode_attn(layer, [slots[i] for i in order], q, ref, stream)
         hkv.decode_attn_noalloc(view, layer, [lens[i] for i in order],
                                 [page_lists[i] for i in order], q, got, stream, lib=hkv_lib)
-        torch.cuda.synchronize()
-        err = rel_err(got.cpu().numpy(), ref.cpu().numpy())
-        assert np.all(np.isfinite(got.cpu().numpy()))
-        assert err <= TOL, (order, err)
+        hkv.decode_attn_noalloc_sync_check(stream, lib=hkv_lib)
+        g = got.cpu().numpy()
+        assert np.all(np.isfinite(g))
+        assert rel_err(g, ref.cpu().numpy()) <= TOL, order
+        qr = np.stack([oracle.rope_neox(qh[j], cos_t[lens[i]], sin_t[lens[i]])
+                       for j, i in enumerate(order)])
+        ks = [expect[i][0] for i in order]
+        vs = [expect[i][1] for i in order]
+        for mode in (oracle.EXACT, oracle.GGML_F16):
+            err = rel_err(g, oracle.decode_attn(qr, ks, vs, mode))
+            assert err <= TOL, (order, mode, err)
     eng.sync_check(stream)
     eng.close()
 
