@@ -58,13 +58,29 @@ def measured_peaks():
     return HBM_FALLBACK_GBS, "fallback"
 
 
-def workload(name: str, rank: int):
+SCALEOUT_REQUESTS, SCALEOUT_GPUS = 256, 8
+
+
+def scaleout_population():
+    """The scale-out config's 256 requests: contexts uniform in [2048, 16384]
+    (seed 1000), placed on 8 GPUs in balanced shards of 32 (equal request
+    counts, nearly equal total context)."""
+    import synth
+    from hkv_dist import balanced_shards
+    pop = [int(x) for x in synth.uniform_int(1000, SCALEOUT_REQUESTS, 2048, 16384)]
+    return pop, balanced_shards(pop, SCALEOUT_GPUS)
+
+
+def workload(name: str, rank: int, prefix: int = 768):
     import synth
     if name == "scaleout":
-        n = 32
-        lens = synth.uniform_int(1000 + rank, n, 2048, 16384)
-        desc = ("scale-out shard: 32 slots per GPU, contexts U[2048,16384], 36 layers, "
-                "F16 KV in 16-token pages (permuted), GQA 32/8, head_dim 128")
+        if rank >= SCALEOUT_GPUS:
+            raise SystemExit(f"the scale-out workload has {SCALEOUT_GPUS} shards")
+        pop, shards = scaleout_population()
+        lens = [pop[i] for i in shards[rank]]
+        desc = ("scale-out shard: 32 slots per GPU (shard %d of the 256-request population, "
+                "contexts U[2048,16384], balanced placement), 36 layers, F16 KV in 16-token "
+                "pages (permuted), GQA 32/8, head_dim 128" % rank)
     elif name == "headsplit":
         n = 1
         lens = [32768 - 16]
@@ -72,9 +88,10 @@ def workload(name: str, rank: int):
                 "F16 KV in 16-token pages")
     elif name == "churn":
         n = 64
-        lens = synth.uniform_int(3000 + rank, n, 769, 8192)
-        desc = ("slot churn with prefix sharing: 64 slots in 8 groups sharing a 768-token "
-                "prefix, contexts U[769, 8192], 36 layers")
+        lens = synth.uniform_int(3000 + rank, n, prefix + 1, 8192)
+        desc = (f"slot churn with prefix sharing: 64 slots in 8 groups sharing a {prefix}-token "
+                "prefix (copy-on-write pages), contexts U[prefix+1, 8192], each slot finishes "
+                "with p=0.01 per step and is replaced at once, 36 layers, F16 KV")
     elif name == "batched16":
         n = 16
         lens = synth.uniform_int(2000 + rank, n, 256, 4096)
@@ -159,40 +176,79 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------- CPU baseline
-def cpu_baseline(lens, budget_s: float = 12.0, max_sample_slots: int = 2):
-    """Times the reference's F32 decode graph (oracle restatement) on the host
-    cores for a bounded sample of the workload and scales it to the whole
-    workload's tokens/s (CPU cost is linear in the context length)."""
+def cpu_complete_steps(groups, budget_s: float, max_steps: int):
+    """Complete decode steps of a whole workload on the host cores: the
+    reference's F32 decode graph restated in C (oracle/hkv_oracle_graph.c:
+    F32 cache, materialised GQA repeat, QK, scale, softmax, permuted V, PV),
+    one graph per slot and layer as the reference runs requests, every slot
+    at its real context, all N_LAYERS layers per step, contexts growing by
+    one per step.  `groups` holds the slots' contexts in groups of at most 32
+    (one per GPU shard); the groups run one after another through one
+    group-sized F32 cache of one layer, which the layers and groups share
+    (host memory holds one group's contexts for one layer).  Every pass reads
+    it from DRAM -- gigabytes, far beyond any CPU cache -- so the traffic is
+    that of distinct caches.  Times at least one complete step and stops
+    before the next one would end past budget_s or max_steps."""
     sys.path.insert(0, str(REPO / "oracle"))
     import cpu_oracle
     cpu_oracle.build()
     cores = cpu_oracle.max_threads()
-    sample = sorted(range(len(lens)), key=lambda i: lens[i])[len(lens) // 2:][:max_sample_slots]
-    sl = [lens[i] for i in sample]
-    cap = max(sl) + 1
-    base = cpu_oracle.GraphBaseline(len(sl), cap)
+    width = max(len(g) for g in groups)
+    cap = max(max(g) for g in groups) + max_steps + 2
+    base = cpu_oracle.GraphBaseline(width, cap, fill_seed=7)
     rng = np.random.default_rng(0)
-    q = rng.standard_normal((len(sl), H, D), dtype=np.float32)
-    k = rng.standard_normal((len(sl), G, D), dtype=np.float32)
-    v = rng.standard_normal((len(sl), G, D), dtype=np.float32)
-    past = np.array(sl, np.int32)
-    base.decode_layer(q, k, v, past)  # warm-up (first touch of caches and scratch)
+    q = rng.standard_normal((N_LAYERS, width, H, D), dtype=np.float32)
+    k = rng.standard_normal((N_LAYERS, width, G, D), dtype=np.float32)
+    v = rng.standard_normal((N_LAYERS, width, G, D), dtype=np.float32)
+    past = [np.array(g, np.int32) for g in groups]
+    m0 = len(groups[0])
+    base.decode_layer(q[0, :m0], k[0, :m0], v[0, :m0], past[0])  # first touch of the scratch
     t0 = time.perf_counter()
-    calls = 0
-    while True:
-        base.decode_layer(q, k, v, past)
-        calls += 1
-        if time.perf_counter() - t0 >= budget_s or calls >= 200:
+    per_step = []
+    while len(per_step) < max_steps:
+        ts = time.perf_counter()
+        for p in past:
+            m = len(p)
+            for layer in range(N_LAYERS):
+                base.decode_layer(q[layer, :m], k[layer, :m], v[layer, :m], p)
+            p += 1
+        per_step.append(time.perf_counter() - ts)
+        if time.perf_counter() - t0 + per_step[-1] > budget_s:
             break
-    dt = time.perf_counter() - t0
-    per_token_row = dt / calls / sum(s + 1 for s in sl)  # seconds per attended row per layer
-    step_s = per_token_row * N_LAYERS * sum(L + 1 for L in lens)
+    total = float(sum(per_step))
+    n_slots = sum(len(g) for g in groups)
+    steps = len(per_step)
     return {
-        "value": len(lens) / step_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-        "sample": (f"{calls} single-layer decode graphs of {len(sl)} slots (contexts {sl}), "
-                   f"F32 cache, materialised GQA repeat, {dt:.1f} s; scaled by context "
-                   f"length to all {len(lens)} slots x {N_LAYERS} layers"),
-    }, step_s
+        "value": steps * n_slots / total, "unit": "tokens/s", "cores": cores, "kind": "port",
+        "steps_timed": steps, "step_s": total / steps,
+        "sample": (f"{steps} complete step(s) of the whole workload: {n_slots} slots at their "
+                   f"real contexts x {N_LAYERS} layers per step, {total:.1f} s on {cores} "
+                   f"threads (F32 cache, materialised GQA repeat, one graph per slot and layer)"),
+    }
+
+
+def run_config(name: str, world: int, lens_all, lens_rank0, desc: str, extra=None) -> dict:
+    """The `config` of a run's JSON line; both arms print the same one."""
+    gb = N_LAYERS * sum(4096 * L + 45056 for L in lens_rank0) / 1e9
+    cfg = {
+        "workload": desc,
+        "slots_per_gpu": len(lens_rank0),
+        "global_batch": len(lens_all),
+        "layers": N_LAYERS,
+        "mean_context": float(np.mean(lens_all)),
+        "seq_len": "per-slot contexts, see workload",
+        "parallelism": f"slot-sharded x{world} (no collective)",
+        "l2": "inputs larger than L2: %.1f GB of KV read per step per GPU" % gb,
+    }
+    if extra:
+        cfg.update(extra)
+    return cfg
+
+
+def workload_all(name: str, world: int, prefix: int = 768):
+    """Every rank's contexts (rank order) and rank 0's description."""
+    groups = [[int(x) for x in workload(name, r, prefix)[0]] for r in range(world)]
+    return groups, workload(name, 0, prefix)[1]
 
 
 # ------------------------------------------------------------------ ours
@@ -259,12 +315,9 @@ def bench_ours(args):
         # 64 slots in 8 groups; each group shares a published reference-prompt
         # prefix (copy-on-write pages); slots finish with probability 0.01 per
         # step and are replaced by fresh prefix-only slots of the same group.
-        import synth
         n, group, prefix = 64, 8, args.prefix
-        lens = [int(x) for x in synth.uniform_int(3000 + rank, n, prefix + 1, 8192)]
-        desc = (f"slot churn with prefix sharing: 64 slots in 8 groups sharing a {prefix}-token "
-                "prefix (copy-on-write pages), contexts U[prefix+1, 8192], each slot finishes "
-                "with p=0.01 per step and is replaced at once, 36 layers, F16 KV")
+        lens, desc = workload("churn", rank, prefix)
+        lens = [int(x) for x in lens]
         prefix_pages = (prefix + 15) // 16
         n_pages = (sum((L - prefix + total_steps + 15) // 16 + 2 for L in lens)
                    + (n // group) * prefix_pages + n * ((total_steps + 15) // 16 + 2) + 64)
@@ -467,13 +520,45 @@ def bench_ours(args):
                "host_enqueue_ms_per_step": 1e3 * host_s[0] / args.e2e_steps,
                "path": "pinned host q|k|v -> hkv_decode_step -> pinned host out "
                        "(one copy each way per 9 layers)"}
+        eng.sync_check(sh)
+        if churn is None:
+            # The host outputs of the last timed step, checked bit for bit
+            # against the same step run again from device-resident inputs:
+            # lengths rolled back by one, the same 36 decode launches (the
+            # same rows appended, the same plan), no copies or events between.
+            p_last = (args.e2e_steps - 1) % 2
+            for s_ in slots:
+                eng.set_length(s_, eng.length(s_) - 1)
+            redo = torch.empty((N_LAYERS, n, H * D), device=dev)
+            with torch.cuda.stream(stream):
+                for layer in range(N_LAYERS):
+                    x = din[p_last, layer]
+                    eng.decode_step(layer, slots, x[:n * H * D], x[n * H * D:n * (H + G) * D],
+                                    x[n * (H + G) * D:], redo[layer], sh)
+            eng.advance(slots, 1)
+            torch.cuda.synchronize()
+            eng.sync_check(sh)
+            same = bool(torch.equal(redo.cpu(), hout[p_last]))
+            e2e["check"] = {"bitwise_equal": same, "layers": N_LAYERS,
+                            "what": "last timed step's host outputs vs the same step from "
+                                    "device-resident inputs"}
+            if not same:
+                raise SystemExit("e2e outputs differ from the device-resident recompute")
     eng.sync_check(sh)
+    eng.close()
+
+    split = headsplit_run(args, dist, rank, world, local, steps=max(3, args.steps // 2),
+                          warmup=3) if not args.no_headsplit else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu, _ = cpu_baseline(lens)
+        groups_cpu, _ = workload_all(args.workload, 1, args.prefix)
+        cpu = cpu_complete_steps(groups_cpu, budget_s=30.0, max_steps=1)
+        if churn is not None:
+            cpu["sample"] += "; slots do not churn in this sample"
 
     if rank == 0:
+        groups_all, desc_all = workload_all(args.workload, world, args.prefix)
         traffic = None
         tfile = REPO / "profiles" / "attention_traffic.json"
         if tfile.exists():
@@ -492,17 +577,8 @@ def bench_ours(args):
             "vs_baseline": None,
             "dtype": "f16 KV, f32 accumulate",
             "data": "synthetic N(0,1) (torch generator on device), random physical page order",
-            "config": {
-                "workload": desc,
-                "slots_per_gpu": n,
-                "global_batch": int(tokens_total / args.steps),
-                "layers": N_LAYERS,
-                "mean_context": float(np.mean(lens)),
-                "seq_len": "per-slot contexts, see workload",
-                "parallelism": f"slot-sharded x{world} (no collective)",
-                "l2": "inputs larger than L2: %.1f GB of KV read per step per GPU" % (
-                    step_bytes_local / 1e9),
-            },
+            "config": run_config(args.workload, world, [x for g in groups_all for x in g],
+                                 groups_all[0], desc_all),
             "hbm": {"step_gbs_per_gpu": step_gbs_per_gpu, "peak_gbs": peak,
                     "frac": step_gbs_per_gpu / peak, "peak_kind": peak_kind},
             "roofline": {
@@ -522,41 +598,36 @@ def bench_ours(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,
+            "headsplit": split,
         }
         print(json.dumps(line), flush=True)
-    eng.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def bench_headsplit(args):
-    """One long request split by KV head across the ranks (HeadSplit): rank g
-    holds KV heads [8g/N, 8(g+1)/N) of every layer and attends its 32/N query
-    heads.  The head-major output of each layer is assembled on every rank
-    either inside the decode kernel (--xchg p2p: peer stores over NVLink +
-    a bounded arrival wait, hkv_split_step / hkv_split_wait) or by an NCCL
-    all-gather after it (--xchg nccl)."""
-    import datetime
+def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, warmup: int):
+    """One request near the 32768-position context split by KV head across
+    the ranks (HeadSplit): rank g holds KV heads [8g/N, 8(g+1)/N) of every
+    layer and attends its 32/N query heads.  The head-major output of each
+    layer reaches every rank either inside the decode kernel (--xchg p2p:
+    peer stores over NVLink + a bounded arrival wait, hkv_split_step /
+    hkv_split_wait) or by an NCCL all-gather after it (--xchg nccl).
 
+    Timed twice with CUDA events, max over ranks: the split decode alone
+    (each rank's hkv_decode_step, no exchange) and with the exchange; their
+    difference per layer is the exchange's cost.  Then the last step's output
+    of the last layer, as assembled on rank 0, is checked against the oracle
+    over the caches every rank holds (gathered with hkv_gather).  Returns a
+    dict on rank 0 (None elsewhere)."""
     import torch
     import hkv
     from hkv_dist import HeadSplit
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as tdist
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                 device_id=torch.device("cuda", local))
-        dist = tdist
     split = HeadSplit(world=world, rank=rank)
     Gl, Hl = split.local_kv_heads, split.local_q_heads
-    total_steps = args.warmup + args.steps + 2
-    L0 = 32768 - total_steps - 1  # the last step's new row sits at position 32766
+    total_steps = 2 * (warmup + steps) + 2
+    L0 = 32768 - total_steps - 1  # the last step's new row sits at position <= 32766
     dev = f"cuda:{local}"
     eng = hkv.Engine(n_layers=N_LAYERS, n_pages=(L0 + total_steps) // 16 + 2, max_slots=1,
                      device=local, shuffle_seed=0xBEEF + rank, **split.engine_shape())
@@ -589,64 +660,106 @@ def bench_headsplit(args):
         eng.split_connect(handles)
         dist.barrier()
 
-    def step():
+    def step(exchange: bool):
         for layer in range(N_LAYERS):
-            if p2p:
+            if exchange and p2p:
                 eng.split_step(layer, [slot], q[layer], k[layer], v[layer], sh)
                 eng.split_wait(layer, sh)
             else:
                 eng.decode_step(layer, [slot], q[layer], k[layer], v[layer], out_local[layer], sh)
-                if dist is not None:
+                if exchange and dist is not None:
                     dist.all_gather_into_tensor(out_full[layer], out_local[layer])
         eng.advance([slot], 1)
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step()
+    def timed(exchange: bool):
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                step(exchange)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        ctx0 = eng.length(slot) + 1
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(steps):
+                step(exchange)
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if dist is not None:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        eng.sync_check(sh)
+        return ms, ctx0
+
+    ms_alone, _ = timed(False)
+    ms, ctx0 = timed(True)
+
+    # ---- parity of the assembled output (last step, last layer) on rank 0
+    layer = N_LAYERS - 1
+    rows = eng.length(slot)
+    kb = torch.empty((rows, Gl, D), dtype=torch.int16, device=dev)
+    vb = torch.empty_like(kb)
+    eng.gather(slot, layer, 0, rows, kb, vb, sh)
     torch.cuda.synchronize()
+    if p2p:
+        ptr, width = eng.split_output(layer)
+        full = torch.as_tensor(hkv.DeviceArray(ptr, (1, width)), device=dev).clone()
+    elif dist is not None:
+        full = out_full[layer].reshape(1, -1).clone()
+    else:
+        full = out_local[layer].reshape(1, -1).clone()
     if dist is not None:
-        dist.barrier()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ctx0 = eng.length(slot) + 1
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if dist is not None:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    eng.sync_check(sh)
-    # full-output check of the assembly on the last layer: rank order == head order
-    if dist is not None and not p2p:
-        full = split.gather_output(out_local[N_LAYERS - 1])
-        assert torch.equal(full.view(world, Hl * D), out_full[N_LAYERS - 1])
-    rows = sum(ctx0 + s for s in range(args.steps))
-    bytes_per_rank = N_LAYERS * 512 * Gl * (rows + 11 * args.steps)
-    peak, peak_kind = measured_peaks()
-    gbs = bytes_per_rank / (ms / 1e3) / 1e9
+        parts = {}
+        for name, t in (("k", kb), ("v", vb), ("q", q[layer].reshape(Hl, D))):
+            lst = [torch.empty_like(t) for _ in range(world)]
+            src = t.view(torch.float16) if t.dtype == torch.int16 else t
+            lst16 = [x.view(torch.float16) if x.dtype == torch.int16 else x for x in lst]
+            dist.all_gather(lst16, src.contiguous())
+            parts[name] = lst
+        k_all = torch.cat(parts["k"], dim=1)
+        v_all = torch.cat(parts["v"], dim=1)
+        q_all = torch.cat(parts["q"], dim=0)
+    else:
+        k_all, v_all, q_all = kb, vb, q[layer].reshape(Hl, D)
+    out = None
     if rank == 0:
-        print(json.dumps({
-            "metric": METRIC, "value": args.steps / (ms / 1e3), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16 KV, f32 accumulate",
-            "data": "synthetic N(0,1) (torch generator on device)",
-            "config": {"workload": (f"one {ctx0}-position request split by KV head over "
-                                    f"{world} GPU(s), {Gl} KV heads each, 36 layers; per-head "
-                                    "outputs assembled every layer by "
-                                    + ("in-kernel peer stores (NVLink)" if p2p else
-                                       ("NCCL all-gather" if dist is not None else "-"))),
-                       "global_batch": 1, "layers": N_LAYERS,
-                       "parallelism": f"KV-head split x{world}"},
-            "hbm": {"step_gbs_per_gpu": gbs, "peak_gbs": peak, "frac": gbs / peak,
-                    "peak_kind": peak_kind},
-            "gpu_launches": N_LAYERS * args.steps, "e2e": None,
-        }), flush=True)
+        sys.path.insert(0, str(REPO / "oracle"))
+        import cpu_oracle
+        cpu_oracle.build()
+        cos, sin = cpu_oracle.rope_table()
+        pos = rows - 1
+        qr = cpu_oracle.rope_neox(q_all.cpu().numpy(), cos[pos], sin[pos])[None]
+        kh = k_all.cpu().numpy().view(np.uint16)
+        vh = v_all.cpu().numpy().view(np.uint16)
+        got = full.cpu().numpy().astype(np.float64).reshape(-1, D)
+        errs = []
+        for mode in (cpu_oracle.EXACT, cpu_oracle.GGML_F16):
+            ref = cpu_oracle.decode_attn(qr, [kh], [vh], mode).astype(np.float64).reshape(-1, D)
+            errs.append(float(np.max(np.abs(got - ref).max(1) / np.abs(ref).max(1))))
+        rows_attended = sum(ctx0 + s_ for s_ in range(steps))
+        bytes_per_rank = N_LAYERS * 512 * Gl * (rows_attended + 11 * steps)
+        peak, peak_kind = measured_peaks()
+        gbs = bytes_per_rank / (ms / 1e3) / 1e9
+        out = {
+            "tokens_s": steps / (ms / 1e3), "ms_per_step": ms / steps,
+            "decode_alone_tokens_s": steps / (ms_alone / 1e3),
+            "exchange_us_per_layer": 1e3 * (ms - ms_alone) / steps / N_LAYERS,
+            "max_rel_err": max(errs), "max_rel_err_modes": {"exact": errs[0], "ggml_f16": errs[1]},
+            "parity_case": f"layer {layer} of the last timed step, 32 query heads over {rows} "
+                           "positions, assembled output on rank 0 vs the oracle",
+            "context": ctx0, "steps": steps, "warmup": warmup, "gpus": world,
+            "kv_heads_per_gpu": Gl,
+            "exchange": ("in-kernel peer stores over NVLink + bounded arrival wait" if p2p else
+                         ("NCCL all-gather" if dist is not None else "none (one GPU)")),
+            "hbm_frac_per_gpu": gbs / peak, "peak_kind": peak_kind,
+            "scaling": "strong (one request, total work fixed)",
+        }
+        if max(errs) > 2e-3:
+            raise SystemExit(f"KV-head split output differs from the oracle: {max(errs):.3e}")
     if p2p:
         dist.barrier()
         eng.split_disconnect()
@@ -655,6 +768,44 @@ def bench_headsplit(args):
     eng.close()
     if dist is not None:
         dist.barrier()
+    return out
+
+
+def bench_headsplit(args):
+    """The KV-head split of one long request alone (see headsplit_run)."""
+    import datetime
+
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+    res = headsplit_run(args, dist, rank, world, local, args.steps, args.warmup)
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        print(json.dumps({
+            "metric": METRIC, "value": res["tokens_s"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 KV, f32 accumulate",
+            "data": "synthetic N(0,1) (torch generator on device)",
+            "config": {"workload": (f"one {res['context']}-position request split by KV head "
+                                    f"over {world} GPU(s), {res['kv_heads_per_gpu']} KV heads "
+                                    f"each, 36 layers; per-head outputs assembled every layer "
+                                    f"by {res['exchange']}"),
+                       "global_batch": 1, "layers": N_LAYERS,
+                       "parallelism": f"KV-head split x{world}"},
+            "hbm": {"frac_per_gpu": res["hbm_frac_per_gpu"], "peak_kind": peak_kind},
+            "headsplit": res, "gpu_launches": N_LAYERS * args.steps, "e2e": None,
+        }), flush=True)
+    if dist is not None:
         dist.destroy_process_group()
 
 
@@ -967,6 +1118,14 @@ def reference_backbone(args):
 
 
 def bench_reference(args):
+    """The reference arm: the reference's CPU decode graph (its GGML CPU path
+    restated in oracle/hkv_oracle_graph.c; ggml itself is absent) on the host
+    cores, on this run's exact workload -- every slot of every rank at its
+    real context, 36 layers -- timed over COMPLETE steps.  One step of the
+    full workload takes tens of seconds per 32 slots on the host, so the arm
+    times as many complete steps as fit a fixed budget (at least one) and
+    prints that count in `steps`; `steps_requested` keeps the driver's.
+    Under torchrun only rank 0 works."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
@@ -974,35 +1133,43 @@ def bench_reference(args):
     if args.workload == "backbone":
         reference_backbone(args)
         return
-    lens = []
-    for r in range(world):
-        lens += workload(args.workload, r)[0]
-    _, desc = workload(args.workload, 0)
+    if args.workload == "headsplit":
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "the reference has no multi-GPU path; see the scaleout workload"}))
+        return
+    groups, desc = workload_all(args.workload, world, args.prefix)
     t0 = time.perf_counter()
-    cpu, step_s = cpu_baseline(lens, budget_s=max(3.0, 2.0 * (args.steps + args.warmup)))
+    cpu = cpu_complete_steps(groups, budget_s=100.0, max_steps=max(1, args.steps))
     wall = time.perf_counter() - t0
+    flat = [x for g in groups for x in g]
     line = {
         "metric": METRIC,
         "value": cpu["value"],
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3,
+        "steps": cpu["steps_timed"],
+        "warmup": 0,
+        "ms_per_step": cpu["step_s"] * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32 (the reference's F32 cache and graph)",
         "data": "synthetic N(0,1)",
         "impl": "reference",
-        "config": {"workload": desc, "global_batch": len(lens), "layers": N_LAYERS,
-                   "parallelism": "host cores (the reference has no multi-GPU path)"},
-        "cpu_baseline": cpu,
+        "config": run_config(args.workload, world, flat, groups[0], desc),
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": ("the reference's GGML CPU graph cannot be built here (ggml submodule "
+        "steps_requested": args.steps,
+        "warmup_requested": args.warmup,
+        "note": ("the reference's GGML CPU graph cannot be built here (its ggml submodule is "
                  "absent); this times its restatement in oracle/hkv_oracle_graph.c on "
-                 f"{cpu['cores']} threads; wall {wall:.1f} s"),
+                 f"{cpu['cores']} host threads over {cpu['steps_timed']} complete step(s) of the "
+                 f"whole workload ({len(flat)} slots x {N_LAYERS} layers, {cpu['step_s']:.1f} s "
+                 f"per step; {args.steps} requested steps would take "
+                 f"{args.steps * cpu['step_s']:.0f} s); warm-up: one single-layer graph, not a "
+                 f"step; wall {wall:.1f} s"
+                 + ("; slots do not churn in this arm" if args.workload == "churn" else "")),
     }
     print(json.dumps(line), flush=True)
 
@@ -1016,6 +1183,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="scaleout")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-headsplit", action="store_true",
+                    help="skip the KV-head split leg that follows the slot-sharded measurement")
     ap.add_argument("--prefix", type=int, default=768,
                     help="churn: shared prefix length (770 puts the first append of every "
                          "replacement slot into a shared partial page: copy-on-write)")

@@ -263,7 +263,10 @@ struct hkv_engine {
     int64_t part_cap = 0;
     int num_sms = 0;
     float scale_log2 = 0.f;
-    hkv::Staging batch_stage, range_stage, gather_stage;
+    hkv::Staging batch_stage, range_stage, gather_stage, cow_stage;
+    // Copy-on-write copies decided on the host and not yet enqueued:
+    // {source page, destination page} pairs, flushed as one kernel launch.
+    std::vector<int32_t> cow_pending;
     hkv::BatchCache batch;
 
     // Launch overlap bookkeeping: a decode launch may start while the previous
@@ -392,6 +395,16 @@ int64_t pages_beyond_reservation(const Slot &s, int64_t need) {
     return std::max<int64_t>(0, need - s.reserved);
 }
 
+// References held on copy-on-write sources until their copies are enqueued
+// (a page another slot of the same call left can be owned outright).
+int32_t pending_cow_sources(const hkv_engine *eng, int32_t page) {
+    int32_t n = 0;
+    for (size_t i = 0; i < eng->cow_pending.size(); i += 2) {
+        n += eng->cow_pending[i] == page ? 1 : 0;
+    }
+    return n;
+}
+
 // Makes `slot` the only owner of every page touched by rows [begin, end),
 // appending fresh pages and copying shared ones (copy-on-write) on `stream`.
 // Availability has been checked by the caller.
@@ -406,18 +419,16 @@ int own_rows(hkv_engine *eng, Slot &s, int64_t begin, int64_t end, cudaStream_t 
         if (p >= static_cast<int64_t>(s.pages.size())) {
             s.pages.push_back(take_page(eng, s));
             changed = true;
-        } else if (eng->refcnt[s.pages[p]] > 1) {
+        } else if (eng->refcnt[s.pages[p]] - pending_cow_sources(eng, s.pages[p]) > 1) {
             const int32_t old = s.pages[p];
             const int32_t fresh = take_page(eng, s);
             if (eng->device_mode) {
-                ++eng->enqueue_seq;
-                // The page lives in every layer's slab: one copy per layer.
-                for (int32_t layer = 0; layer < eng->cfg.n_layers; ++layer) {
-                    HKV_CUDA_TRY(eng, cudaMemcpyAsync(page_ptr(eng, layer, fresh),
-                                                      page_ptr(eng, layer, old),
-                                                      static_cast<size_t>(layer_page_bytes(eng)),
-                                                      cudaMemcpyDeviceToDevice, stream));
-                }
+                // The page lives in every layer's slab; flush_cow copies all
+                // layers of all pending pages in one launch.  Until then the
+                // old page keeps a reference, so it cannot be reused.
+                incref(eng, old);
+                eng->cow_pending.push_back(old);
+                eng->cow_pending.push_back(fresh);
             }
             decref(eng, old);
             s.pages[p] = fresh;
@@ -429,6 +440,43 @@ int own_rows(hkv_engine *eng, Slot &s, int64_t begin, int64_t end, cudaStream_t 
         ++eng->epoch;
     }
     return HKV_OK;
+}
+
+PoolView pool_view(const hkv_engine *eng);
+
+// Enqueues the pending copy-on-write copies (one kernel launch for all pages
+// and layers) and drops the references that kept their source pages alive.
+int flush_cow(hkv_engine *eng, cudaStream_t stream) {
+    if (eng->cow_pending.empty()) {
+        return HKV_OK;
+    }
+    const int32_t n_pairs = static_cast<int32_t>(eng->cow_pending.size() / 2);
+    const size_t bytes = eng->cow_pending.size() * sizeof(int32_t);
+    void *host = nullptr;
+    int st = HKV_OK;
+    cudaError_t e = eng->cow_stage.begin(bytes, &host);
+    void *dev = nullptr;
+    if (e == cudaSuccess) {
+        std::memcpy(host, eng->cow_pending.data(), bytes);
+        ++eng->enqueue_seq;
+        e = eng->cow_stage.commit(bytes, stream, &dev);
+    }
+    if (e == cudaSuccess) {
+        launch_cow_copy(pool_view(eng), static_cast<const int32_t *>(dev), n_pairs, eng->d_err,
+                        stream);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) {
+            e = eng->cow_stage.mark_used(stream);
+        }
+    }
+    if (e != cudaSuccess) {
+        st = cuda_fail(eng, e, "copy-on-write launch");
+    }
+    for (size_t i = 0; i < eng->cow_pending.size(); i += 2) {
+        decref(eng, eng->cow_pending[i]);
+    }
+    eng->cow_pending.clear();
+    return st;
 }
 
 PoolView pool_view(const hkv_engine *eng) {
@@ -541,6 +589,12 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
     for (int32_t e = 0; e < n; ++e) {
         Slot &sl = eng->slots[slots[e]];
         const int st = own_rows(eng, sl, sl.used, sl.used + 1, stream);
+        if (st != HKV_OK) {
+            return st;
+        }
+    }
+    {
+        const int st = flush_cow(eng, stream);
         if (st != HKV_OK) {
             return st;
         }
@@ -662,6 +716,7 @@ void free_device(hkv_engine *eng) {
     eng->batch_stage.release();
     eng->range_stage.release();
     eng->gather_stage.release();
+    eng->cow_stage.release();
     for (auto &list : eng->prof) {
         for (auto &r : list) {
             cudaEventDestroy(r.start);
@@ -1148,6 +1203,8 @@ int hkv_rope_append_range(hkv_engine *eng, int32_t layer, int32_t slot, int64_t 
                     static_cast<long long>(extra), static_cast<long long>(unreserved_free(eng)));
     }
     st = own_rows(eng, s, begin, end, stream);
+    if (st != HKV_OK) return st;
+    st = flush_cow(eng, stream);
     if (st != HKV_OK) return st;
     const int64_t p0 = begin / kPageTokens;
     const int64_t p1 = (end - 1) / kPageTokens + 1;

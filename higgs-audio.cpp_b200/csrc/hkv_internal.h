@@ -154,6 +154,10 @@ void launch_attention(const PoolView &pool, const RopeView &rope, const BatchVie
 // (wrap-around safe); records kErrTimeout and returns if it never does.
 void launch_split_wait(const uint32_t *flag, uint32_t target, DeviceError *err,
                        cudaStream_t stream);
+// Copy-on-write of whole pages: pairs[2 i] -> pairs[2 i + 1] (device array of
+// n_pairs {source, destination} page ids), every layer, one launch.
+void launch_cow_copy(const PoolView &pool, const int32_t *pairs, int32_t n_pairs, DeviceError *err,
+                     cudaStream_t stream);
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
                    int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
                    cudaStream_t stream);

@@ -52,6 +52,7 @@ constexpr int kCtaSmem = kAttnWarps * 2 * kCtaPartBytes + 32;
 constexpr int kWhereAppend = 0;
 constexpr int kWhereAttn = 1;
 constexpr int kWhereGather = 3;
+constexpr int kWhereCow = 4;
 constexpr int kWhereSplitWait = 5;
 
 static_assert(kWarpSmem % 16 == 0, "per-warp shared region must keep 16-byte alignment");
@@ -1056,6 +1057,37 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     flush(true);
 }
 
+// ================================================================ copy-on-write
+// One block per (page pair, layer): copies the source page's K and V head
+// blocks of that layer (2 * n_head_kv * 4 KiB, contiguous in the layer's slab)
+// onto the destination page with 16-byte loads and stores.  All pending
+// copies of a call go out in this one launch.
+__global__ void __launch_bounds__(256) cow_copy_kernel(PoolView pool, const int2 *__restrict__ pairs,
+                                                       int32_t n_pairs, DeviceError *err) {
+    const int64_t item = blockIdx.x;
+    const int64_t pair = item / pool.n_layers;
+    const int layer = static_cast<int>(item - pair * pool.n_layers);
+    if (pair >= n_pairs) {
+        return;
+    }
+    const int2 pr = pairs[pair];
+    if (pr.x < 0 || pr.x >= pool.n_pages || pr.y < 0 || pr.y >= pool.n_pages) {
+        if (threadIdx.x == 0) {
+            record_error(err, kErrBadIndex, kWhereCow, pr.x, pr.y);
+        }
+        return;
+    }
+    const int G = pool.n_head_kv;
+    const uint4 *src = reinterpret_cast<const uint4 *>(
+        pool.base + head_block_index(pr.x, layer, 0, 0, pool.n_pages, G) * kHeadBlockBytes);
+    uint4 *dst = reinterpret_cast<uint4 *>(
+        pool.base + head_block_index(pr.y, layer, 0, 0, pool.n_pages, G) * kHeadBlockBytes);
+    const int n16 = 2 * G * kHeadBlockBytes / 16;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+        dst[i] = __ldcs(src + i);
+    }
+}
+
 // ===================================================================== gather
 __global__ void gather_kernel(PoolView pool, const int32_t *__restrict__ slot_pages, int64_t pos0,
                               int64_t n, int layer, uint16_t *__restrict__ k_out,
@@ -1215,6 +1247,16 @@ void launch_split_wait(const uint32_t *flag, uint32_t target, DeviceError *err,
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, split_wait_kernel, flag, target, err);
+}
+
+void launch_cow_copy(const PoolView &pool, const int32_t *pairs, int32_t n_pairs, DeviceError *err,
+                     cudaStream_t stream) {
+    const int64_t blocks = static_cast<int64_t>(n_pairs) * pool.n_layers;
+    if (blocks <= 0) {
+        return;
+    }
+    cow_copy_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        pool, reinterpret_cast<const int2 *>(pairs), n_pairs, err);
 }
 
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,

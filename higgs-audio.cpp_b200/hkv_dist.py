@@ -3,9 +3,12 @@
 Two placements, neither of which exists in the reference (it runs every
 request on CUDA device 0, src/higgs_pipeline.cpp:126):
 
-* Slot sharding (independent requests).  Request r lives on rank
-  r % world for its whole life; every rank runs its own engine on its own
-  slots and no data crosses GPUs.  ``shard_requests`` is the placement.
+* Slot sharding (independent requests).  A request lives on one rank for its
+  whole life; every rank runs its own engine on its own slots and no data
+  crosses GPUs.  ``shard_requests`` places request r on rank r % world;
+  ``balanced_shards`` gives every rank the same number of requests with
+  nearly the same total context (the step time of a rank is set by the K/V
+  bytes it reads, so the slowest rank sets the job's).
 
 * KV-head split (one long request).  Rank g of N holds KV heads
   [g*G/N, (g+1)*G/N) for all layers in its own engine (configured with
@@ -29,6 +32,27 @@ def shard_requests(request_ids: Sequence[int], world: int, rank: int) -> List[in
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world of {world}")
     return [r for r in request_ids if r % world == rank]
+
+
+def balanced_shards(costs: Sequence[int], world: int) -> List[List[int]]:
+    """Request indices grouped into `world` shards of equal size with nearly
+    equal total cost (for decode attention the cost of a request is its
+    context length: that many K/V rows are read per layer and step).  Longest
+    first, each request to the lightest shard that still has room; ties go
+    to the lower rank.  Deterministic, so every rank computes the same
+    placement from the same list."""
+    n = len(costs)
+    if world <= 0 or n % world != 0:
+        raise ValueError(f"{n} requests do not split into {world} equal shards")
+    per = n // world
+    order = sorted(range(n), key=lambda i: (-int(costs[i]), i))
+    shards: List[List[int]] = [[] for _ in range(world)]
+    total = [0] * world
+    for i in order:
+        r = min((r for r in range(world) if len(shards[r]) < per), key=lambda r: (total[r], r))
+        shards[r].append(i)
+        total[r] += int(costs[i])
+    return [sorted(s) for s in shards]
 
 
 def _contiguous(x):

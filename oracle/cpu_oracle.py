@@ -180,15 +180,48 @@ def decode_attn(q_roped: np.ndarray, k_caches, v_caches, mode: int = EXACT) -> n
     return out
 
 
+def decode_attn_rows(q_roped: np.ndarray, k_all: np.ndarray, v_all: np.ndarray,
+                     row_off: np.ndarray, lens: np.ndarray, mode: int = EXACT) -> np.ndarray:
+    """decode_attn over caches kept in one array: slot e's rows are
+    k_all[row_off[e] : row_off[e] + lens[e]] (uint16 [rows][n_head_kv][head_dim]),
+    so large caches are not copied per call."""
+    q = np.ascontiguousarray(q_roped, np.float32)
+    n, H, D = q.shape
+    G = k_all.shape[1]
+    assert k_all.flags.c_contiguous and v_all.flags.c_contiguous
+    assert k_all.dtype == np.uint16 and v_all.dtype == np.uint16
+    row_off = np.ascontiguousarray(row_off, np.int64)
+    lens = np.ascontiguousarray(lens, np.int32)
+    assert row_off.shape == (n,) and lens.shape == (n,)
+    assert np.all(row_off >= 0) and np.all(row_off + lens <= k_all.shape[0])
+    out = np.empty((n, H * D), np.float32)
+    lib().hkvo_decode_attn(mode, n, H, G, D, _p(q), _p(k_all), _p(v_all), _p(row_off), _p(lens),
+                           scale(D), _p(out))
+    return out
+
+
 class GraphBaseline:
     """The reference's F32 decode graph for one layer over contiguous per-slot
     caches (hkv_oracle_graph.c): the timed CPU baseline."""
 
     def __init__(self, n_slots: int, capacity: int, n_head: int = 32, n_head_kv: int = 8,
-                 head_dim: int = 128, cos=None, sin=None):
+                 head_dim: int = 128, cos=None, sin=None, fill_seed=None):
         self.n, self.cap, self.H, self.G, self.D = n_slots, capacity, n_head, n_head_kv, head_dim
-        self.k_cache = np.zeros((n_slots * capacity, n_head_kv, head_dim), np.float32)
-        self.v_cache = np.zeros_like(self.k_cache)
+        if fill_seed is None:
+            self.k_cache = np.zeros((n_slots * capacity, n_head_kv, head_dim), np.float32)
+            self.v_cache = np.zeros_like(self.k_cache)
+        else:
+            # N(0,1) rows: a seeded block tiled over the whole cache (fast to
+            # fill; the graph's cost does not depend on the values)
+            block = np.random.default_rng(fill_seed).standard_normal(
+                (4096, n_head_kv, head_dim), dtype=np.float32)
+            rows = n_slots * capacity
+            self.k_cache = np.empty((rows, n_head_kv, head_dim), np.float32)
+            self.v_cache = np.empty_like(self.k_cache)
+            for a in range(0, rows, 4096):
+                b = min(rows, a + 4096)
+                self.k_cache[a:b] = block[:b - a]
+                self.v_cache[a:b] = block[::-1][:b - a]
         self.row_off = (np.arange(n_slots, dtype=np.int64) * capacity)
         work = lib().hkvo_graph_work_floats(capacity, n_head, n_head_kv, head_dim)
         self.work = np.zeros(int(work), np.float32)
@@ -198,12 +231,15 @@ class GraphBaseline:
         self.out = np.zeros((n_slots, n_head * head_dim), np.float32)
 
     def decode_layer(self, q_pre, k_pre, v_new, past) -> np.ndarray:
+        """One layer for the first len(past) slots."""
         past = np.ascontiguousarray(past, np.int32)
-        assert past.max() < self.cap
+        n = past.shape[0]
+        assert 0 < n <= self.n and past.max() < self.cap
         q_pre = np.ascontiguousarray(q_pre, np.float32)
         k_pre = np.ascontiguousarray(k_pre, np.float32)
         v_new = np.ascontiguousarray(v_new, np.float32)
-        lib().hkvo_graph_decode_layer(self.n, self.H, self.G, self.D, _p(q_pre), _p(k_pre),
+        assert q_pre.shape[0] == n and k_pre.shape[0] == n and v_new.shape[0] == n
+        lib().hkvo_graph_decode_layer(n, self.H, self.G, self.D, _p(q_pre), _p(k_pre),
                                       _p(v_new), _p(self.k_cache), _p(self.v_cache),
                                       _p(self.row_off), _p(past), _p(self.cos), _p(self.sin),
                                       scale(self.D), _p(self.work), _p(self.out))
