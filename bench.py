@@ -452,6 +452,14 @@ def bench_ours(args):
         dout = torch.empty((2, N_LAYERS, n, H * D), device=dev)
         h2d = torch.cuda.Stream(device=local)
         d2h = torch.cuda.Stream(device=local)
+        # Per-call arguments prepared once, as a caller of the C ABI keeps
+        # them: device pointers of q, k, v and out per (buffer, layer), the
+        # slot array per step (rebuilt only when the batch changes).
+        fsz = 4
+        ptrs = [[(din[p_, layer].data_ptr(), din[p_, layer].data_ptr() + n * H * D * fsz,
+                  din[p_, layer].data_ptr() + n * (H + G) * D * fsz, dout[p_, layer].data_ptr())
+                 for layer in range(N_LAYERS)] for p_ in range(2)]
+        slot_arg = [eng.slots_array(slots)]
         ev_in = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
         ev_done = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
         ev_back = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
@@ -478,10 +486,10 @@ def bench_ours(args):
                 stream.wait_event(ev_in[p][c])
                 if used[p][c]:
                     stream.wait_event(ev_back[p][c])  # dout[p] chunk is on the host
+                n_, arr = slot_arg[0]
                 for layer in range(lo, hi):
-                    x = din[p, layer]
-                    eng.decode_step(layer, slots, x[:n * H * D], x[n * H * D:n * (H + G) * D],
-                                    x[n * (H + G) * D:], dout[p, layer], sh)
+                    qp, kp, vp, op = ptrs[p][layer]
+                    eng.decode_step_ptrs(layer, n_, arr, qp, kp, vp, op, sh)
                 ev_done[p][c].record(stream)
                 used[p][c] = True
                 with torch.cuda.stream(d2h):
@@ -493,6 +501,7 @@ def bench_ours(args):
                 cur_len[i] += 1
             if churn is not None:
                 churn()
+                slot_arg[0] = eng.slots_array(slots)
             host_s[0] += time.perf_counter() - t0
 
         e2e_step(0, True, True)
@@ -505,10 +514,12 @@ def bench_ours(args):
         h2d.wait_stream(stream)
         d2h.wait_stream(stream)
         host_s[0] = 0.0
+        eng.host_stats(reset=True)
         for i in range(args.e2e_steps):
             e2e_step(i, i == 0, i == args.e2e_steps - 1)
         stream.wait_stream(d2h)  # the last outputs are on the host
         e1.record(stream)
+        eng_calls, eng_us = eng.host_stats(reset=True)
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
         e2e_tokens = sum_over_ranks(n * args.e2e_steps)
@@ -518,6 +529,8 @@ def bench_ours(args):
                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
                "host_enqueue_ms_per_step": 1e3 * host_s[0] / args.e2e_steps,
+               "engine_host_us_per_call": eng_us / max(eng_calls, 1),
+               "engine_host_ms_per_step": 1e-3 * eng_us / args.e2e_steps,
                "path": "pinned host q|k|v -> hkv_decode_step -> pinned host out "
                        "(one copy each way per 9 layers)"}
         eng.sync_check(sh)

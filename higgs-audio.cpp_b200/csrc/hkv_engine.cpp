@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -291,6 +292,11 @@ struct hkv_engine {
     std::vector<uint32_t> split_target;      // expected arrivals per layer
     bool split_connected = false;
 
+    // host time spent inside the compute entry points (hkv_host_stats)
+    mutable std::mutex host_mu;
+    int64_t host_calls = 0;
+    int64_t host_ns = 0;
+
     // profiling
     bool profiling = false;
     std::vector<hkv::ProfileRecord> prof[HKV_KERNEL_COUNT];
@@ -533,6 +539,23 @@ class ProfileScope {
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Adds the host time of one compute call (entry to return, lock included)
+// to the engine's counters.
+class HostTimer {
+  public:
+    explicit HostTimer(hkv_engine *eng) : eng_(eng), t0_(std::chrono::steady_clock::now()) {}
+    ~HostTimer() {
+        const auto dt = std::chrono::steady_clock::now() - t0_;
+        std::lock_guard<std::mutex> lock(eng_->host_mu);
+        ++eng_->host_calls;
+        eng_->host_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(dt).count();
+    }
+
+  private:
+    hkv_engine *eng_;
+    std::chrono::steady_clock::time_point t0_;
+};
 
 int check_compute(hkv_engine *eng, int32_t layer) {
     if (!eng->device_mode) {
@@ -1227,6 +1250,7 @@ int hkv_rope_append_range(hkv_engine *eng, int32_t layer, int32_t slot, int64_t 
 int hkv_decode_attn(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots,
                     const float *q_prerope, float *out, hkv_stream stream_h) {
     if (eng == nullptr) return HKV_ERR_INVALID;
+    HostTimer host_timer(eng);
     std::lock_guard<std::mutex> lock(eng->mu);
     DeviceGuard guard(eng->cfg.device);
     cudaStream_t stream = static_cast<cudaStream_t>(stream_h);
@@ -1244,6 +1268,7 @@ int hkv_decode_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *sl
                     const float *q_prerope, const float *k_prerope, const float *v, float *out,
                     hkv_stream stream_h) {
     if (eng == nullptr) return HKV_ERR_INVALID;
+    HostTimer host_timer(eng);
     std::lock_guard<std::mutex> lock(eng->mu);
     DeviceGuard guard(eng->cfg.device);
     cudaStream_t stream = static_cast<cudaStream_t>(stream_h);
@@ -1439,8 +1464,13 @@ int hkv_split_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slo
     x.layer_floats = static_cast<int64_t>(eng->cfg.max_slots) * eng->xchg_row_floats;
     st = do_attention(eng, layer, q_prerope, k_prerope, v, nullptr, stream, x);
     if (st != HKV_OK) return st;
-    // every rank's kernel signals once per (entry, KV head)
-    eng->split_target[layer] += static_cast<uint32_t>(n) * eng->cfg.n_head_kv * eng->split_world;
+    // every rank signals once per (entry, KV head) its attention launch
+    // finishes, and -- when split partials go through the combine launch --
+    // once per query head of every segment that launch finishes
+    const uint32_t whole = static_cast<uint32_t>(n) * eng->cfg.n_head_kv - eng->batch.view.split_segments;
+    const uint32_t per_split = HKV_COMBINE ? kGqa : 1;
+    eng->split_target[layer] +=
+        (whole + per_split * static_cast<uint32_t>(eng->batch.view.split_segments)) * eng->split_world;
     return HKV_OK;
 }
 
@@ -1501,6 +1531,20 @@ int hkv_profile_reset(hkv_engine *eng) {
             eng->event_pool.push_back(r.stop);
         }
         list.clear();
+    }
+    return HKV_OK;
+}
+
+int hkv_host_stats(hkv_engine *eng, int64_t *calls, double *host_us, int reset) {
+    if (eng == nullptr || calls == nullptr || host_us == nullptr) {
+        return HKV_ERR_INVALID;
+    }
+    std::lock_guard<std::mutex> lock(eng->host_mu);
+    *calls = eng->host_calls;
+    *host_us = static_cast<double>(eng->host_ns) * 1e-3;
+    if (reset) {
+        eng->host_calls = 0;
+        eng->host_ns = 0;
     }
     return HKV_OK;
 }

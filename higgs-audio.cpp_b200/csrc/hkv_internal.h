@@ -66,6 +66,7 @@ struct BatchView {
     int32_t n_parts;
     int32_t cta_merge;        // 1: the warps of a CTA pre-merge in shared memory (one
                               // partial per CTA); 0: one partial per warp
+    int32_t split_segments;   // segments with more than one partial
 };
 
 // Partials of one (entry, KV head) are merged by one warp when there are at
@@ -126,6 +127,9 @@ struct RopeView {
 #endif
 #ifndef HKV_ATTN_STAGES
 #define HKV_ATTN_STAGES 2
+#endif
+#ifndef HKV_COMBINE
+#define HKV_COMBINE 0
 #endif
 constexpr int kAttnWarps = HKV_ATTN_WARPS;    // consumer warps per CTA, one CTA per SM
 constexpr int kAttnStages = HKV_ATTN_STAGES;  // TMA ring depth per warp (K+V block per stage)

@@ -755,6 +755,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 }
             }
         }
+#if HKV_COMBINE
+        // The combine kernel that follows merges the stored partials once
+        // this grid has completed: no fence or ticket here.
+        return;
+#endif
         // Publish the partial; the last of a group of partials merges the
         // group, and the last group (or the only one) produces the output.
         __threadfence();
@@ -1057,6 +1062,128 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     flush(true);
 }
 
+#if HKV_COMBINE
+// ==================================================================== combine
+// One CTA per (segment, query head of its group) for the segments whose
+// partials the attention launch before it stored (segments held by one warp
+// or one CTA were written there).  Up to kCombineWarps warps each merge a
+// contiguous chunk of ceil(p / warps) partials -- eight loads in flight
+// before their sums -- leave (o, m, l) in shared memory, and warp 0 merges
+// those in warp order: a fixed summation order, so results do not depend on
+// timing.  It waits for the attention grid (griddepcontrol.wait) and lets the
+// next launch in the stream be scheduled at once.  One head's 128 dims (a
+// float4 per lane) keep it small enough to share an SM with an attention CTA.
+// In a KV-head split every CTA signals one arrival after its stores.
+constexpr int kCombineWarps = 8;
+constexpr int kCombineBatch = 8;
+
+__global__ void __launch_bounds__(kCombineWarps * 32)
+    combine_kernel(BatchView batch, int layer, const float *__restrict__ part_o,
+                   const float *__restrict__ part_ml, float *__restrict__ out, Exchange xchg) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    __shared__ float4 s_o[kCombineWarps][32];
+    __shared__ float2 s_ml[kCombineWarps];
+    const int seg = static_cast<int>(blockIdx.x) / kGqa;
+    const int j = static_cast<int>(blockIdx.x) - seg * kGqa;  // query head within the group
+    const int G = static_cast<int>(gridDim.x) / (kGqa * batch.n);
+    // the plan was uploaded before the attention launch this kernel follows
+    const int4 sg = batch.seg[seg];
+    const int nparts = sg.y;
+    if (nparts <= 1) {
+        return;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int lane = threadIdx.x & 31;
+    const int wid = threadIdx.x >> 5;
+    const int want = (nparts + kCombineBatch - 1) / kCombineBatch;
+    const int active = want < kCombineWarps ? want : kCombineWarps;
+    const int chunk = (nparts + active - 1) / active;
+    const int used = (nparts + chunk - 1) / chunk;  // warps with a non-empty chunk
+    if (wid < used) {
+        const int p0 = sg.x + wid * chunk;
+        const int cnt = min(chunk, nparts - wid * chunk);
+        const float2 *mlp = reinterpret_cast<const float2 *>(part_ml) + j;  // (m, l) of head j
+        float mx = -INFINITY;
+        for (int b = lane; b < cnt; b += 32) {
+            mx = fmaxf(mx, __ldcg(mlp + static_cast<int64_t>(p0 + b) * kGqa).x);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float den = 0.f;
+        for (int b = 0; b < cnt; b += 32) {
+            float w = 0.f;
+            if (b + lane < cnt) {
+                const float2 ml = __ldcg(mlp + static_cast<int64_t>(p0 + b + lane) * kGqa);
+                w = exp2f(ml.x - mx);
+                den += w * ml.y;
+            }
+            const int cb = min(32, cnt - b);
+            for (int t0 = 0; t0 < cb; t0 += kCombineBatch) {
+                float4 ov[kCombineBatch];
+#pragma unroll
+                for (int t = 0; t < kCombineBatch; ++t) {
+                    if (t0 + t < cb) {
+                        ov[t] = __ldcg(reinterpret_cast<const float4 *>(
+                                           part_o + static_cast<int64_t>(p0 + b + t0 + t) * (kGqa * kHeadDim) +
+                                           j * kHeadDim) + lane);
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < kCombineBatch; ++t) {
+                    if (t0 + t < cb) {
+                        const float wt = __shfl_sync(0xffffffffu, w, t0 + t);
+                        acc.x += wt * ov[t].x;
+                        acc.y += wt * ov[t].y;
+                        acc.z += wt * ov[t].z;
+                        acc.w += wt * ov[t].w;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            den += __shfl_xor_sync(0xffffffffu, den, off);
+        }
+        s_o[wid][lane] = acc;
+        if (lane == 0) {
+            s_ml[wid] = make_float2(mx, den);
+        }
+    }
+    __syncthreads();
+    if (wid != 0) {
+        return;
+    }
+    float mx = -INFINITY;
+    for (int w = 0; w < used; ++w) {
+        mx = fmaxf(mx, s_ml[w].x);
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float den = 0.f;
+    for (int w = 0; w < used; ++w) {
+        const float wt = exp2f(s_ml[w].x - mx);
+        den += wt * s_ml[w].y;
+        const float4 ov = s_o[w][lane];
+        acc.x += wt * ov.x;
+        acc.y += wt * ov.y;
+        acc.z += wt * ov.z;
+        acc.w += wt * ov.w;
+    }
+    const float inv = 1.f / den;
+    const float4 res = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    const int e = seg / G;
+    const int h = seg - e * G;
+    const int n_dst = xchg.n_ranks == 0 ? 1 : xchg.n_ranks;
+    for (int r = 0; r < n_dst; ++r) {
+        float4 *ob = reinterpret_cast<float4 *>(out_slice(out, xchg, r, layer, e, h, G) + j * kHeadDim);
+        ob[lane] = res;
+    }
+    signal_arrival(xchg, layer, lane);
+}
+#endif
+
 // ================================================================ copy-on-write
 // One block per (page pair, layer): copies the source page's K and V head
 // blocks of that layer (2 * n_head_kv * 4 KiB, contiguous in the layer's slab)
@@ -1185,6 +1312,19 @@ void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchV
     cfg.numAttrs = overlap_previous ? 1 : 0;
     cudaLaunchKernelEx(&cfg, attention_kernel<kAppend, kCtaMerge>, pool, rope, batch, layer, q, k_new,
                        v_new, part_o, part_ml, counters, out, xchg, scale_log2, err);
+#if HKV_COMBINE
+    if (batch.split_segments > 0) {
+        cudaLaunchConfig_t cc = {};
+        cc.gridDim = dim3(static_cast<unsigned>(batch.n * pool.n_head_kv * kGqa));
+        cc.blockDim = dim3(kCombineWarps * 32);
+        cc.stream = stream;
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cc.attrs = attr;
+        cc.numAttrs = 1;
+        cudaLaunchKernelEx(&cc, combine_kernel, batch, layer, part_o, part_ml, out, xchg);
+    }
+#endif
 }
 
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,

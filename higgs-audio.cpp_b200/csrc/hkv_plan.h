@@ -121,6 +121,7 @@ struct PlanSummary {
     int32_t n_parts = 0;   // level-1 partials
     int32_t n_groups = 0;  // group partials (and group counters)
     int32_t shares = 0;    // non-empty shares (<= W)
+    int32_t split_segments = 0;  // segments with more than one partial
     int64_t budget = 0;    // the cost bound B of every share
     bool cta_merge = false;
 };
@@ -199,6 +200,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         rec[2] = k;
         rec[3] = last;
         parts += np_parts;
+        s.split_segments += np_parts > 1 ? 1 : 0;
         part2_off[sg + 1] = part2_off[sg] + merge_groups(np_parts);
     }
 
@@ -267,6 +269,7 @@ inline BatchView bind_plan(const int32_t *d, int32_t n, int32_t G, const PlanSum
     b.n_warps = W;
     b.n_parts = s.n_parts;
     b.cta_merge = s.cta_merge ? 1 : 0;
+    b.split_segments = s.split_segments;
     return b;
 }
 

@@ -192,6 +192,7 @@ SIGNATURES = {
     "hkv_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
     "hkv_profile_reset": ([_P], ctypes.c_int),
     "hkv_profile_read": ([_P, ctypes.c_int, _I64P, ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+    "hkv_host_stats": ([_P, _I64P, ctypes.POINTER(ctypes.c_double), ctypes.c_int], ctypes.c_int),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -397,6 +398,27 @@ class Engine:
 
     def sync_check(self, stream=None) -> None:
         self._check(self.lib.hkv_sync_check(self.handle, _stream(stream)))
+
+    def slots_array(self, slots: Sequence[int]):
+        """(n, ctypes int32 array) of a slot list, for decode_step_ptrs."""
+        return _slots_arg(slots)
+
+    def decode_step_ptrs(self, layer: int, n: int, slots_arr, q: int, k: int, v: int, out: int,
+                         stream: int) -> None:
+        """hkv_decode_step with every argument prepared (device pointers and the
+        stream as ints, the slots as a ctypes array): the least a caller does
+        per call."""
+        st = self.lib.hkv_decode_step(self.handle, layer, n, slots_arr, q, k, v, out, stream)
+        if st != HKV_OK:
+            self._check(st)
+
+    def host_stats(self, reset: bool = False):
+        """(calls, host microseconds) spent inside hkv_decode_step / hkv_decode_attn."""
+        c = ctypes.c_int64()
+        us = ctypes.c_double()
+        self._check(self.lib.hkv_host_stats(self.handle, ctypes.byref(c), ctypes.byref(us),
+                                            1 if reset else 0))
+        return c.value, us.value
 
     def rope_tables(self):
         half = self.cfg.head_dim // 2
