@@ -128,6 +128,12 @@ struct RopeView {
 #ifndef HKV_ATTN_STAGES
 #define HKV_ATTN_STAGES 2
 #endif
+// HKV_CUDA_CORES=1 builds the attention's QK and PV on the CUDA cores (exact
+// F16 -> F32 conversions, F32 products) instead of the tensor cores: the
+// comparison variant, never the default.
+#ifndef HKV_CUDA_CORES
+#define HKV_CUDA_CORES 0
+#endif
 #ifndef HKV_COMBINE
 #define HKV_COMBINE 0
 #endif

@@ -113,6 +113,46 @@ __device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
 __device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
     asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_f32x2(uint32_t addr, float a, float b) {
+    asm volatile("st.shared.v2.f32 [%0], {%1,%2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void st_shared_f32x4(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_shared_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint4 ld_shared_u32x4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 ld_shared_u32x2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t u) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&u));
+}
 __device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(addr), "r"(0) : "memory");
 }
@@ -647,11 +687,39 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 
     float o[8][4];
     uint32_t qb[8][2];
+#if HKV_CUDA_CORES
+    // CUDA-core variant: this lane's 4 dims (4 lane .. 4 lane + 3) of each of
+    // the 4 query heads, over all tokens of the segment so far
+    float4 acc[kGqa];
+#endif
     float m_a = kNegInf, m_b = kNegInf, l_a = 0.f, l_b = 0.f;
     int seg_e = 0, seg_h = 0, seg_pos = 0, part = 0, p_first = 0, nparts = 1, ntok = 0;
     int run_w0 = wid, run_m = 1;  // this CTA's warps of the current segment: w0 .. w0 + m - 1
 
     auto flush = [&](bool after_loop) {
+#if HKV_CUDA_CORES
+        // Lay the CUDA-core accumulators out as the tensor-core fragments the
+        // rest of the flush reads (the staged q is no longer needed: its area
+        // holds them; lanes of the F16-residual columns get zeros).
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < kGqa; ++j) {
+            st_shared_f32x4(qc + (j * kHeadDim + 4 * lane) * 4, acc[j]);
+        }
+        __syncwarp();
+        {
+            const int ha = (lane & 1) * 2;
+            const int g = lane >> 2;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                o[mt][0] = lo_side ? 0.f : ld_shared_f32(qc + (ha * kHeadDim + 16 * mt + g) * 4);
+                o[mt][1] = lo_side ? 0.f : ld_shared_f32(qc + ((ha + 1) * kHeadDim + 16 * mt + g) * 4);
+                o[mt][2] = lo_side ? 0.f : ld_shared_f32(qc + (ha * kHeadDim + 16 * mt + g + 8) * 4);
+                o[mt][3] = lo_side ? 0.f : ld_shared_f32(qc + ((ha + 1) * kHeadDim + 16 * mt + g + 8) * 4);
+            }
+        }
+        __syncwarp();
+#endif
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
 #pragma unroll
@@ -898,6 +966,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                     const float x1 = __ldg(qe + j * kHeadDim + i + kHeadDim / 2);
                     const float y0 = rope_lo(x0, x1, c, sn);
                     const float y1 = rope_hi(x0, x1, c, sn);
+#if HKV_CUDA_CORES
+                    st_shared_f32(qc + (j * kHeadDim + i) * 4, y0);
+                    st_shared_f32(qc + (j * kHeadDim + i + 64) * 4, y1);
+                    continue;
+#endif
                     const __half h0 = __float2half_rn(y0);
                     const __half h1 = __float2half_rn(y1);
                     const __half l0 = __float2half_rn(__fsub_rn(y0, __half2float(h0)));
@@ -909,11 +982,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 }
             }
             __syncwarp();
+#if HKV_CUDA_CORES
+#pragma unroll
+            for (int j = 0; j < kGqa; ++j) {
+                acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#else
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
                 ldsm_x4(qc + (r7 * kQcStride + jj * 32 + mi * 8) * 2, qb[2 * jj][0],
                         qb[2 * jj][1], qb[2 * jj + 1][0], qb[2 * jj + 1][1]);
             }
+#endif
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) {
 #pragma unroll
@@ -976,6 +1056,44 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             __syncwarp();
         }
 
+#if HKV_CUDA_CORES
+        // ---- CUDA cores: this lane's partial scores of tokens g and g + 8 for
+        // heads ha, ha + 1 over its half of the dims (the lanes of the other
+        // half hold the rest; the shuffle below adds them), F16 K converted
+        // exactly, F32 products.  Lanes of the upper half walk their chunks
+        // rotated by four so a load phase hits eight bank groups.
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        float sd[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+            const int hsel = (lane >> 1) & 1;
+            const int ha = (lane & 1) * 2;
+            const int g = lane >> 2;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c = hsel * 8 + ((i + 4 * hsel) & 7);
+                const uint4 k0 = ld_shared_u32x4(kt + g * kRowBytes + ((c ^ g) << 4));
+                const uint4 k1 = ld_shared_u32x4(kt + (g + 8) * kRowBytes + ((c ^ g) << 4));
+                const float4 qa0 = ld_shared_f32x4(qc + (ha * kHeadDim + c * 8) * 4);
+                const float4 qa1 = ld_shared_f32x4(qc + (ha * kHeadDim + c * 8 + 4) * 4);
+                const float4 qb0 = ld_shared_f32x4(qc + ((ha + 1) * kHeadDim + c * 8) * 4);
+                const float4 qb1 = ld_shared_f32x4(qc + ((ha + 1) * kHeadDim + c * 8 + 4) * 4);
+                const float qa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
+                const float qbv[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
+                const uint32_t kw0[4] = {k0.x, k0.y, k0.z, k0.w};
+                const uint32_t kw1[4] = {k1.x, k1.y, k1.z, k1.w};
+                float *acc_s = (i & 1) ? sd : sc;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f0 = half2_bits_to_float2(kw0[e]);
+                    const float2 f1 = half2_bits_to_float2(kw1[e]);
+                    acc_s[0] = fmaf(f0.x, qa[2 * e], fmaf(f0.y, qa[2 * e + 1], acc_s[0]));
+                    acc_s[1] = fmaf(f0.x, qbv[2 * e], fmaf(f0.y, qbv[2 * e + 1], acc_s[1]));
+                    acc_s[2] = fmaf(f1.x, qa[2 * e], fmaf(f1.y, qa[2 * e + 1], acc_s[2]));
+                    acc_s[3] = fmaf(f1.x, qbv[2 * e], fmaf(f1.y, qbv[2 * e + 1], acc_s[3]));
+                }
+            }
+        }
+#else
         // ---- S^T[token][col] = K[token][:] . Qc[col][:]   (col 0-3 hi, 4-7 lo)
         // Two accumulators (even / odd k-steps) halve the dependent mma chain.
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -988,6 +1106,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             mma_16816(sc, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
             mma_16816(sd, b0, b1, b2, b3, qb[ks + 1][0], qb[ks + 1][1]);
         }
+#endif
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             sc[j] += sd[j];
@@ -1017,6 +1136,47 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         l_b = l_b * alpha_b + (p1 + p3);
         m_a = mn_a;
         m_b = mn_b;
+#if HKV_CUDA_CORES
+        // ---- CUDA cores: p (F32) to shared memory as [token][head], then each
+        // lane accumulates its 4 dims of every head over the 16 tokens.
+        {
+            const int ha = (lane & 1) * 2;
+            const int g = lane >> 2;
+            if (!lo_side) {
+                st_shared_f32x2(pbuf + (g * kGqa + ha) * 4, p0, p1);
+                st_shared_f32x2(pbuf + ((g + 8) * kGqa + ha) * 4, p2, p3);
+            }
+            // the rescale of every head: lane ^ 1 holds the other head pair
+            const float alpha_c = __shfl_xor_sync(0xffffffffu, alpha_a, 1);
+            const float alpha_d = __shfl_xor_sync(0xffffffffu, alpha_b, 1);
+            const float al[kGqa] = {ha == 0 ? alpha_a : alpha_c, ha == 0 ? alpha_b : alpha_d,
+                                    ha == 0 ? alpha_c : alpha_a, ha == 0 ? alpha_d : alpha_b};
+#pragma unroll
+            for (int j = 0; j < kGqa; ++j) {
+                acc[j].x *= al[j];
+                acc[j].y *= al[j];
+                acc[j].z *= al[j];
+                acc[j].w *= al[j];
+            }
+            __syncwarp();
+#pragma unroll 4
+            for (int t = 0; t < kPageTokens; ++t) {
+                const float4 pv = ld_shared_f32x4(pbuf + t * kGqa * 4);
+                const uint2 vv = ld_shared_u32x2(vt + t * kRowBytes + (((lane >> 1) ^ (t & 7)) << 4) +
+                                                 (lane & 1) * 8);
+                const float2 v01 = half2_bits_to_float2(vv.x);
+                const float2 v23 = half2_bits_to_float2(vv.y);
+                const float pj[kGqa] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+                for (int j = 0; j < kGqa; ++j) {
+                    acc[j].x = fmaf(pj[j], v01.x, acc[j].x);
+                    acc[j].y = fmaf(pj[j], v01.y, acc[j].y);
+                    acc[j].z = fmaf(pj[j], v23.x, acc[j].z);
+                    acc[j].w = fmaf(pj[j], v23.y, acc[j].w);
+                }
+            }
+        }
+#else
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
             o[mt][0] *= alpha_a;
@@ -1044,6 +1204,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             ldsm_x4_trans(vt + v_row_off + ((chunk ^ r7) << 4), a0, a1, a2, a3);
             mma_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
         }
+#endif
         __syncwarp();
         if (lane == 0 && u + kAttnStages < u_end) {
             fence_proxy_async_smem();
