@@ -637,7 +637,10 @@ def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, war
     import hkv
     from hkv_dist import HeadSplit
 
-    split = HeadSplit(world=world, rank=rank)
+    # --split-shape N on one GPU: rank 0's engine shape of an N-way split, no
+    # exchange (tunes the per-rank launch without N GPUs)
+    shape_world = args.split_shape if (dist is None and args.split_shape > 1) else world
+    split = HeadSplit(world=shape_world, rank=rank)
     Gl, Hl = split.local_kv_heads, split.local_q_heads
     total_steps = 2 * (warmup + steps) + 2
     L0 = 32768 - total_steps - 1  # the last step's new row sits at position <= 32766
@@ -738,6 +741,7 @@ def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, war
         q_all = torch.cat(parts["q"], dim=0)
     else:
         k_all, v_all, q_all = kb, vb, q[layer].reshape(Hl, D)
+        full = full[:, :Hl * D]
     out = None
     if rank == 0:
         sys.path.insert(0, str(REPO / "oracle"))
@@ -765,6 +769,7 @@ def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, war
             "parity_case": f"layer {layer} of the last timed step, 32 query heads over {rows} "
                            "positions, assembled output on rank 0 vs the oracle",
             "context": ctx0, "steps": steps, "warmup": warmup, "gpus": world,
+            "shape_of_split": shape_world,
             "kv_heads_per_gpu": Gl,
             "exchange": ("in-kernel peer stores over NVLink + bounded arrival wait" if p2p else
                          ("NCCL all-gather" if dist is not None else "none (one GPU)")),
@@ -1201,6 +1206,9 @@ def main():
     ap.add_argument("--prefix", type=int, default=768,
                     help="churn: shared prefix length (770 puts the first append of every "
                          "replacement slot into a shared partial page: copy-on-write)")
+    ap.add_argument("--split-shape", type=int, default=1,
+                    help="headsplit on one GPU: run rank 0's shape of an N-way KV-head split "
+                         "(8/N KV heads) without the exchange")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
                     help="headsplit: how the per-head outputs reach every rank")
     ap.add_argument("--prompt-len", type=int, default=1024,

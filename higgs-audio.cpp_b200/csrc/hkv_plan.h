@@ -46,9 +46,17 @@
 
 namespace hkv {
 
-// Warps to share U units among (at most one per unit).
+// Warps to share U units among: at most one per kMinUnitsPerWarp units
+// (short shares split every segment over many warps and make its merge the
+// longest part of a small launch), at most a full grid, at least one.
+#ifndef HKV_MIN_UNITS_PER_WARP
+#define HKV_MIN_UNITS_PER_WARP 1
+#endif
+constexpr int64_t kMinUnitsPerWarp = HKV_MIN_UNITS_PER_WARP;
 inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
-    return static_cast<int32_t>(total_units < max_warps ? total_units : max_warps);
+    int64_t w = (total_units + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
+    w = w < max_warps ? w : max_warps;
+    return static_cast<int32_t>(w > 0 ? w : 1);
 }
 
 // CTA-level pre-merge pays when a segment spans many warps (a few long
