@@ -1468,7 +1468,7 @@ int hkv_split_step(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slo
     // finishes, and -- when split partials go through the combine launch --
     // once per query head of every segment that launch finishes
     const uint32_t whole = static_cast<uint32_t>(n) * eng->cfg.n_head_kv - eng->batch.view.split_segments;
-    const uint32_t per_split = HKV_COMBINE ? kGqa : 1;
+    const uint32_t per_split = eng->batch.view.combine ? kGqa : 1;
     eng->split_target[layer] +=
         (whole + per_split * static_cast<uint32_t>(eng->batch.view.split_segments)) * eng->split_world;
     return HKV_OK;

@@ -67,6 +67,8 @@ struct BatchView {
     int32_t cta_merge;        // 1: the warps of a CTA pre-merge in shared memory (one
                               // partial per CTA); 0: one partial per warp
     int32_t split_segments;   // segments with more than one partial
+    int32_t combine;          // 1: split partials are only stored; the combine launch
+                              // that follows merges them (plan_combine)
 };
 
 // Partials of one (entry, KV head) are merged by one warp when there are at
@@ -131,11 +133,11 @@ struct RopeView {
 // HKV_CUDA_CORES=1 builds the attention's QK and PV on the CUDA cores (exact
 // F16 -> F32 conversions, F32 products) instead of the tensor cores: the
 // comparison variant, never the default.
+#ifndef HKV_Q_PREFETCH
+#define HKV_Q_PREFETCH 0
+#endif
 #ifndef HKV_CUDA_CORES
 #define HKV_CUDA_CORES 0
-#endif
-#ifndef HKV_COMBINE
-#define HKV_COMBINE 0
 #endif
 constexpr int kAttnWarps = HKV_ATTN_WARPS;    // consumer warps per CTA, one CTA per SM
 constexpr int kAttnStages = HKV_ATTN_STAGES;  // TMA ring depth per warp (K+V block per stage)

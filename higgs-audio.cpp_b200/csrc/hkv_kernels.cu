@@ -669,6 +669,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
     }
 
+#if HKV_Q_PREFETCH
+    // The first segment's query rows and RoPE table rows into L2 before the
+    // dependency wait (a prefetch reads nothing into registers, so a q still
+    // being written by the kernel before is not consumed early).
+    if (lane == 1) {
+        const float *qe = q + (static_cast<int64_t>(cons.e) * (kGqa * G) + kGqa * cons.h) * kHeadDim;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(qe), "r"(kGqa * kHeadDim * 4) : "memory");
+        const int64_t pos0 = batch.pos[cons.e];
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rope.cos_tab + pos0 * (kHeadDim / 2)),
+                     "r"(kHeadDim * 2) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rope.sin_tab + pos0 * (kHeadDim / 2)),
+                     "r"(kHeadDim * 2) : "memory");
+    }
+#endif
     // Programmatic dependent launch: everything above only reads this launch's
     // plan and this layer's pages; q / k / v may come from the kernel before,
     // and the partials, counters and outputs may still be in use by it, so
@@ -823,11 +837,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 }
             }
         }
-#if HKV_COMBINE
-        // The combine kernel that follows merges the stored partials once
-        // this grid has completed: no fence or ticket here.
-        return;
-#endif
+        if (batch.combine) {
+            // The combine launch that follows merges the stored partials once
+            // this grid has completed: no fence or ticket here.
+            return;
+        }
         // Publish the partial; the last of a group of partials merges the
         // group, and the last group (or the only one) produces the output.
         __threadfence();
@@ -1223,7 +1237,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     flush(true);
 }
 
-#if HKV_COMBINE
 // ==================================================================== combine
 // One CTA per (segment, query head of its group) for the segments whose
 // partials the attention launch before it stored (segments held by one warp
@@ -1343,7 +1356,6 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
     }
     signal_arrival(xchg, layer, lane);
 }
-#endif
 
 // ================================================================ copy-on-write
 // One block per (page pair, layer): copies the source page's K and V head
@@ -1473,8 +1485,7 @@ void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchV
     cfg.numAttrs = overlap_previous ? 1 : 0;
     cudaLaunchKernelEx(&cfg, attention_kernel<kAppend, kCtaMerge>, pool, rope, batch, layer, q, k_new,
                        v_new, part_o, part_ml, counters, out, xchg, scale_log2, err);
-#if HKV_COMBINE
-    if (batch.split_segments > 0) {
+    if (batch.combine && batch.split_segments > 0) {
         cudaLaunchConfig_t cc = {};
         cc.gridDim = dim3(static_cast<unsigned>(batch.n * pool.n_head_kv * kGqa));
         cc.blockDim = dim3(kCombineWarps * 32);
@@ -1485,7 +1496,6 @@ void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchV
         cc.numAttrs = 1;
         cudaLaunchKernelEx(&cc, combine_kernel, batch, layer, part_o, part_ml, out, xchg);
     }
-#endif
 }
 
 void launch_attention(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,

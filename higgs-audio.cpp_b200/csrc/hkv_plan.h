@@ -46,23 +46,30 @@
 
 namespace hkv {
 
-// Warps to share U units among: at most one per kMinUnitsPerWarp units
-// (short shares split every segment over many warps and make its merge the
-// longest part of a small launch), at most a full grid, at least one.
-#ifndef HKV_MIN_UNITS_PER_WARP
-#define HKV_MIN_UNITS_PER_WARP 1
-#endif
-constexpr int64_t kMinUnitsPerWarp = HKV_MIN_UNITS_PER_WARP;
+// Warps to share U units among (at most one per unit).
 inline int32_t plan_warps(int64_t total_units, int64_t max_warps) {
-    int64_t w = (total_units + kMinUnitsPerWarp - 1) / kMinUnitsPerWarp;
-    w = w < max_warps ? w : max_warps;
-    return static_cast<int32_t>(w > 0 ? w : 1);
+    return static_cast<int32_t>(total_units < max_warps ? total_units : max_warps);
 }
 
 // CTA-level pre-merge pays when a segment spans many warps (a few long
 // requests); with many short segments it only adds shared-memory traffic
 // and footprint.
 inline bool plan_cta_merge(int64_t n_segments, int64_t W) { return W >= 2 * kAttnWarps * n_segments; }
+
+// Where the split partials are merged.  Inside the attention launch, by the
+// last warp (or CTA) of each segment to finish, behind a fence and an atomic
+// ticket -- best when segments are short (many segments, a few warp partials
+// each: the merges of early segments overlap the other warps' work), and for
+// one segment over the whole grid (its groups merge as they complete).  Or
+// by a combine launch after the attention grid, one CTA per (segment, query
+// head) -- best for CTA-merged segments of at most kCombineMaxParts partials
+// (a few long requests: one request near 32k positions +11%, the batch-1
+// backbone step +7%, measured against the in-launch merge), whose in-launch
+// merge would sit in the tail behind fences, tickets and a second level.
+constexpr int32_t kCombineMaxParts = 32;
+inline bool plan_combine(bool cta_merge, int32_t max_parts) {
+    return cta_merge && max_parts > 1 && max_parts <= kCombineMaxParts;
+}
 
 // Share costs in sixteenths of a unit, from per-warp timestamps of the
 // attention kernel on B200 (16 slots of 256-4096 positions): a unit takes
@@ -130,6 +137,8 @@ struct PlanSummary {
     int32_t n_groups = 0;  // group partials (and group counters)
     int32_t shares = 0;    // non-empty shares (<= W)
     int32_t split_segments = 0;  // segments with more than one partial
+    int32_t max_parts = 0;       // most partials of one segment
+    bool combine = false;        // split partials merged by the combine launch (plan_combine)
     int64_t budget = 0;    // the cost bound B of every share
     bool cta_merge = false;
 };
@@ -209,6 +218,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         rec[3] = last;
         parts += np_parts;
         s.split_segments += np_parts > 1 ? 1 : 0;
+        s.max_parts = std::max(s.max_parts, np_parts);
         part2_off[sg + 1] = part2_off[sg] + merge_groups(np_parts);
     }
 
@@ -256,6 +266,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
     }
     s.n_parts = parts;
     s.n_groups = part2_off[S];
+    s.combine = plan_combine(s.cta_merge, s.max_parts);
     return s;
 }
 
@@ -278,6 +289,7 @@ inline BatchView bind_plan(const int32_t *d, int32_t n, int32_t G, const PlanSum
     b.n_parts = s.n_parts;
     b.cta_merge = s.cta_merge ? 1 : 0;
     b.split_segments = s.split_segments;
+    b.combine = s.combine ? 1 : 0;
     return b;
 }
 

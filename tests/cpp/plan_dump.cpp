@@ -3,7 +3,7 @@
 //
 // Input, one batch per line:  G W pos_0 pos_1 ... pos_{n-1}
 // Output, per batch:
-//   plan <shares> <budget> <cta_merge> <n_parts> <n_groups>
+//   plan <shares> <budget> <cta_merge> <n_parts> <n_groups> <combine>
 //   starts <u_begin of warp 0 .. W-1> <U>
 //   seg <first partial> <partials> <first warp> <last warp>   (one line per segment)
 //   part2 <part2_off[0 .. n*G]>
@@ -43,8 +43,8 @@ int main() {
         }
         std::vector<int32_t> w(hkv::plan_words(n, G, total_pages, W));
         const hkv::PlanSummary s = hkv::build_plan(w.data(), n, G, pos.data(), ptrs.data(), total_pages, W);
-        std::printf("plan %d %lld %d %d %d\n", s.shares, static_cast<long long>(s.budget),
-                    s.cta_merge ? 1 : 0, s.n_parts, s.n_groups);
+        std::printf("plan %d %lld %d %d %d %d\n", s.shares, static_cast<long long>(s.budget),
+                    s.cta_merge ? 1 : 0, s.n_parts, s.n_groups, s.combine ? 1 : 0);
         std::printf("starts");
         for (int32_t k = 0; k < W; ++k) {
             std::printf(" %d", w[hkv::kWarpStartWords * k + 8]);

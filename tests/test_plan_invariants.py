@@ -10,6 +10,10 @@ prints its descriptor) and checked against a restatement here:
 - segments: each (slot, KV head) segment records its first and last warp
   and its partial count (warps, or CTAs of WPC warps with the CTA merge).
 
+The plan also chooses where the split partials are merged: by a combine
+launch after the attention grid for CTA-merged segments of at most 32
+partials, else inside the launch.
+
 Then every warp is walked the way attention_kernel does, with the two-level
 merge (a segment with more than 16 partials is merged in groups of
 max(8, ceil(sqrt(n))) by the last warp of each group, and the last group
@@ -55,14 +59,15 @@ def plan_dump(tmp_path_factory):
         for G, W, pos in batches:
             hdr = out[i].split()
             assert hdr[0] == "plan"
-            shares, budget, cta, n_parts, n_groups = map(int, hdr[1:])
+            shares, budget, cta, n_parts, n_groups, combine = map(int, hdr[1:])
             starts = list(map(int, out[i + 1].split()[1:]))
             n_seg = len(pos) * G
             segs = [tuple(map(int, out[i + 2 + j].split()[1:])) for j in range(n_seg)]
             part2 = list(map(int, out[i + 2 + n_seg].split()[1:]))
             warps = list(map(int, out[i + 3 + n_seg].split()[1:]))
             i += 4 + n_seg
-            plans.append(dict(shares=shares, budget=budget, cta_merge=bool(cta), n_parts=n_parts,
+            plans.append(dict(shares=shares, budget=budget, cta_merge=bool(cta), combine=bool(combine),
+                              n_parts=n_parts,
                               n_groups=n_groups, starts=starts, segs=segs, part2=part2,
                               warps=[tuple(warps[k:k + 3]) for k in range(0, len(warps), 3)]))
         return plans
@@ -147,6 +152,9 @@ def walk(plan_dump, npages, G=8, w_full=148 * 6):
     assert got["starts"] == ref["starts"]
     assert got["segs"] == ref["segs"] and got["cta_merge"] == ref["cta_merge"]
     assert got["n_parts"] == sum(n for _, n, _, _ in ref["segs"])
+    # merged by the combine launch: CTA-merged segments of at most 32 partials
+    max_parts = max(n for _, n, _, _ in ref["segs"])
+    assert got["combine"] == (ref["cta_merge"] and 1 < max_parts <= 32)
     n_seg = len(npages) * G
     n_groups = [n_groups_of(sg[1]) for sg in ref["segs"]]
     assert got["part2"] == [sum(n_groups[:i]) for i in range(n_seg + 1)]
