@@ -133,9 +133,6 @@ struct RopeView {
 // HKV_CUDA_CORES=1 builds the attention's QK and PV on the CUDA cores (exact
 // F16 -> F32 conversions, F32 products) instead of the tensor cores: the
 // comparison variant, never the default.
-#ifndef HKV_Q_PREFETCH
-#define HKV_Q_PREFETCH 0
-#endif
 #ifndef HKV_CUDA_CORES
 #define HKV_CUDA_CORES 0
 #endif

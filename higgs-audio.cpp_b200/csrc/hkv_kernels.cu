@@ -669,20 +669,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
     }
 
-#if HKV_Q_PREFETCH
-    // The first segment's query rows and RoPE table rows into L2 before the
-    // dependency wait (a prefetch reads nothing into registers, so a q still
-    // being written by the kernel before is not consumed early).
-    if (lane == 1) {
-        const float *qe = q + (static_cast<int64_t>(cons.e) * (kGqa * G) + kGqa * cons.h) * kHeadDim;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(qe), "r"(kGqa * kHeadDim * 4) : "memory");
-        const int64_t pos0 = batch.pos[cons.e];
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rope.cos_tab + pos0 * (kHeadDim / 2)),
-                     "r"(kHeadDim * 2) : "memory");
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rope.sin_tab + pos0 * (kHeadDim / 2)),
-                     "r"(kHeadDim * 2) : "memory");
-    }
-#endif
     // Programmatic dependent launch: everything above only reads this launch's
     // plan and this layer's pages; q / k / v may come from the kernel before,
     // and the partials, counters and outputs may still be in use by it, so
