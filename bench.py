@@ -519,7 +519,7 @@ def bench_ours(args):
             e2e_step(i, i == 0, i == args.e2e_steps - 1)
         stream.wait_stream(d2h)  # the last outputs are on the host
         e1.record(stream)
-        eng_calls, eng_us = eng.host_stats(reset=True)
+        eng_calls, eng_us, eng_launch_us = eng.host_stats(reset=True)
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
         e2e_tokens = sum_over_ranks(n * args.e2e_steps)
@@ -529,8 +529,10 @@ def bench_ours(args):
                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
                "host_enqueue_ms_per_step": 1e3 * host_s[0] / args.e2e_steps,
-               "engine_host_us_per_call": eng_us / max(eng_calls, 1),
-               "engine_host_ms_per_step": 1e-3 * eng_us / args.e2e_steps,
+               "engine_cpu_us_per_call": (eng_us - eng_launch_us) / max(eng_calls, 1),
+               "launch_api_us_per_call": eng_launch_us / max(eng_calls, 1),
+               "launch_api_note": "time inside the CUDA launch calls: it includes blocking "
+                                  "when the host is ahead of the GPU by a full launch queue",
                "path": "pinned host q|k|v -> hkv_decode_step -> pinned host out "
                        "(one copy each way per 9 layers)"}
         eng.sync_check(sh)

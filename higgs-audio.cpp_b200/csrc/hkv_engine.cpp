@@ -296,6 +296,7 @@ struct hkv_engine {
     mutable std::mutex host_mu;
     int64_t host_calls = 0;
     int64_t host_ns = 0;
+    int64_t launch_ns = 0;  // of host_ns: inside the kernel launch calls
 
     // profiling
     bool profiling = false;
@@ -704,9 +705,13 @@ int do_attention(hkv_engine *eng, int32_t layer, const float *q, const float *k_
                          eng->last_decode_stream == stream && eng->last_decode_layer != layer;
     {
         ProfileScope ps(eng, k_new != nullptr ? HKV_KERNEL_STEP : HKV_KERNEL_ATTN, stream);
+        const auto t0 = std::chrono::steady_clock::now();
         launch_attention(pool_view(eng), rope_view(eng), eng->batch.view, layer, q, k_new, v_new,
                          eng->part_o, eng->part_ml, eng->counters, out, xchg,
                          eng->scale_log2, eng->d_err, overlap, stream);
+        const auto dt = std::chrono::steady_clock::now() - t0;
+        std::lock_guard<std::mutex> lock(eng->host_mu);
+        eng->launch_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(dt).count();
     }
     eng->last_decode_seq = eng->enqueue_seq;
     eng->last_decode_layer = layer;
@@ -1535,16 +1540,19 @@ int hkv_profile_reset(hkv_engine *eng) {
     return HKV_OK;
 }
 
-int hkv_host_stats(hkv_engine *eng, int64_t *calls, double *host_us, int reset) {
-    if (eng == nullptr || calls == nullptr || host_us == nullptr) {
+int hkv_host_stats(hkv_engine *eng, int64_t *calls, double *host_us, double *launch_us,
+                   int reset) {
+    if (eng == nullptr || calls == nullptr || host_us == nullptr || launch_us == nullptr) {
         return HKV_ERR_INVALID;
     }
     std::lock_guard<std::mutex> lock(eng->host_mu);
     *calls = eng->host_calls;
     *host_us = static_cast<double>(eng->host_ns) * 1e-3;
+    *launch_us = static_cast<double>(eng->launch_ns) * 1e-3;
     if (reset) {
         eng->host_calls = 0;
         eng->host_ns = 0;
+        eng->launch_ns = 0;
     }
     return HKV_OK;
 }

@@ -192,7 +192,8 @@ SIGNATURES = {
     "hkv_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
     "hkv_profile_reset": ([_P], ctypes.c_int),
     "hkv_profile_read": ([_P, ctypes.c_int, _I64P, ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
-    "hkv_host_stats": ([_P, _I64P, ctypes.POINTER(ctypes.c_double), ctypes.c_int], ctypes.c_int),
+    "hkv_host_stats": ([_P, _I64P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                        ctypes.c_int], ctypes.c_int),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -413,12 +414,14 @@ class Engine:
             self._check(st)
 
     def host_stats(self, reset: bool = False):
-        """(calls, host microseconds) spent inside hkv_decode_step / hkv_decode_attn."""
+        """(calls, host microseconds, of which inside the launch calls) spent in
+        hkv_decode_step / hkv_decode_attn."""
         c = ctypes.c_int64()
         us = ctypes.c_double()
+        lus = ctypes.c_double()
         self._check(self.lib.hkv_host_stats(self.handle, ctypes.byref(c), ctypes.byref(us),
-                                            1 if reset else 0))
-        return c.value, us.value
+                                            ctypes.byref(lus), 1 if reset else 0))
+        return c.value, us.value, lus.value
 
     def rope_tables(self):
         half = self.cfg.head_dim // 2
