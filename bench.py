@@ -444,7 +444,7 @@ def bench_ours(args):
         # chunk computes, so the stream sees event waits only at chunk
         # boundaries and the launches inside a chunk still overlap.
         qkv_floats = n * (H + 2 * G) * D
-        chunk = 9
+        chunk = args.e2e_chunk
         chunks = [(c, min(c + chunk, N_LAYERS)) for c in range(0, N_LAYERS, chunk)]
         hin = torch.randn((N_LAYERS, qkv_floats)).pin_memory()
         hout = torch.empty((2, N_LAYERS, n, H * D)).pin_memory()
@@ -530,11 +530,12 @@ def bench_ours(args):
                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
                "host_enqueue_ms_per_step": 1e3 * host_s[0] / args.e2e_steps,
                "engine_cpu_us_per_call": (eng_us - eng_launch_us) / max(eng_calls, 1),
-               "launch_api_us_per_call": eng_launch_us / max(eng_calls, 1),
-               "launch_api_note": "time inside the CUDA launch calls: it includes blocking "
-                                  "when the host is ahead of the GPU by a full launch queue",
+               "engine_blocking_us_per_call": eng_launch_us / max(eng_calls, 1),
+               "engine_blocking_note": "inside the CUDA launch calls and waits to reuse a plan "
+                                       "upload buffer: blocks when the host is ahead of the GPU",
+               "chunk_layers": chunk,
                "path": "pinned host q|k|v -> hkv_decode_step -> pinned host out "
-                       "(one copy each way per 9 layers)"}
+                       f"(one copy each way per {chunk} layers)"}
         eng.sync_check(sh)
         if churn is None:
             # The host outputs of the last timed step, checked bit for bit
@@ -1203,6 +1204,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="scaleout")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-chunk", type=int, default=9,
+                    help="e2e: layers per host<->device copy (and per event wait)")
     ap.add_argument("--no-headsplit", action="store_true",
                     help="skip the KV-head split leg that follows the slot-sharded measurement")
     ap.add_argument("--prefix", type=int, default=768,

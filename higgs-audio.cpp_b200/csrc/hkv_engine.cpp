@@ -138,7 +138,11 @@ class Staging {
             if (e != cudaSuccess) return e;
         }
         if (b.copy_pending) {
+            const auto t0 = std::chrono::steady_clock::now();
             cudaError_t e = cudaEventSynchronize(b.copied);
+            wait_ns_ += std::chrono::duration_cast<std::chrono::nanoseconds>(
+                            std::chrono::steady_clock::now() - t0)
+                            .count();
             if (e != cudaSuccess) return e;
             b.copy_pending = false;
         }
@@ -180,6 +184,13 @@ class Staging {
         return cudaSuccess;
     }
 
+    // Host time spent waiting for an earlier upload from the buffer now reused.
+    int64_t take_wait_ns() {
+        const int64_t w = wait_ns_;
+        wait_ns_ = 0;
+        return w;
+    }
+
     // Marks the current buffer as read by work queued on `stream` so far.
     cudaError_t mark_used(cudaStream_t stream) {
         Buf &b = buf_[cur_];
@@ -199,6 +210,7 @@ class Staging {
     };
     Buf buf_[2];
     int cur_ = 1;
+    int64_t wait_ns_ = 0;
 };
 
 struct Slot {
@@ -297,6 +309,7 @@ struct hkv_engine {
     int64_t host_calls = 0;
     int64_t host_ns = 0;
     int64_t launch_ns = 0;  // of host_ns: inside the kernel launch calls
+    int64_t staging_wait_ns = 0;  // of host_ns: waiting to reuse a plan upload buffer
 
     // profiling
     bool profiling = false;
@@ -548,9 +561,11 @@ class HostTimer {
     explicit HostTimer(hkv_engine *eng) : eng_(eng), t0_(std::chrono::steady_clock::now()) {}
     ~HostTimer() {
         const auto dt = std::chrono::steady_clock::now() - t0_;
+        const int64_t waited = eng_->batch_stage.take_wait_ns();
         std::lock_guard<std::mutex> lock(eng_->host_mu);
         ++eng_->host_calls;
         eng_->host_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(dt).count();
+        eng_->staging_wait_ns += waited;
     }
 
   private:
@@ -1540,19 +1555,20 @@ int hkv_profile_reset(hkv_engine *eng) {
     return HKV_OK;
 }
 
-int hkv_host_stats(hkv_engine *eng, int64_t *calls, double *host_us, double *launch_us,
+int hkv_host_stats(hkv_engine *eng, int64_t *calls, double *host_us, double *blocked_us,
                    int reset) {
-    if (eng == nullptr || calls == nullptr || host_us == nullptr || launch_us == nullptr) {
+    if (eng == nullptr || calls == nullptr || host_us == nullptr || blocked_us == nullptr) {
         return HKV_ERR_INVALID;
     }
     std::lock_guard<std::mutex> lock(eng->host_mu);
     *calls = eng->host_calls;
     *host_us = static_cast<double>(eng->host_ns) * 1e-3;
-    *launch_us = static_cast<double>(eng->launch_ns) * 1e-3;
+    *blocked_us = static_cast<double>(eng->launch_ns + eng->staging_wait_ns) * 1e-3;
     if (reset) {
         eng->host_calls = 0;
         eng->host_ns = 0;
         eng->launch_ns = 0;
+        eng->staging_wait_ns = 0;
     }
     return HKV_OK;
 }

@@ -414,8 +414,8 @@ class Engine:
             self._check(st)
 
     def host_stats(self, reset: bool = False):
-        """(calls, host microseconds, of which inside the launch calls) spent in
-        hkv_decode_step / hkv_decode_attn."""
+        """(calls, host microseconds, of which launch calls and buffer waits that
+        can block on the GPU) spent in hkv_decode_step / hkv_decode_attn."""
         c = ctypes.c_int64()
         us = ctypes.c_double()
         lus = ctypes.c_double()

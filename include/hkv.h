@@ -437,13 +437,14 @@ int hkv_backbone_sync_check(hkv_backbone *bb, hkv_stream stream);
 
 /* Host time the engine spent inside hkv_decode_step and hkv_decode_attn
  * (entry to return, including the wait for the engine's lock): the calls
- * counted, their total in microseconds, and the part of it inside the CUDA
- * launch calls (which block when the host runs far enough ahead of the GPU
- * that the launch queue is full), since the last reset; reset != 0 clears
- * the counters after reading.  Instrumentation of this engine, no
- * counterpart in the reference: host_us - launch_us is the engine's own CPU
- * work per call (validation, batch plan), apart from its caller's. */
-int hkv_host_stats(hkv_engine *eng, int64_t *calls, double *host_us, double *launch_us,
+ * counted, their total in microseconds, and the part of it that can block on
+ * the GPU -- inside the CUDA launch calls (whose queue fills when the host
+ * runs far ahead) and waiting to reuse a plan upload buffer still being
+ * copied -- since the last reset; reset != 0 clears the counters after
+ * reading.  Instrumentation of this engine, no counterpart in the reference:
+ * host_us - blocked_us is the engine's own CPU work per call (validation,
+ * batch plan), apart from its caller's. */
+int hkv_host_stats(hkv_engine *eng, int64_t *calls, double *host_us, double *blocked_us,
                    int reset);
 
 /* When on, every kernel launch is bracketed by CUDA events on its stream;
