@@ -76,9 +76,11 @@ inline bool plan_combine(bool cta_merge, int32_t max_parts) {
 // about 0.95 us of a warp's time, leaving a segment held whole about 1 us
 // (output stores, next queries), leaving a shared one about 3.3 us (partial
 // stores, fence, ticket round trip, next queries).
+// Raised from 16 / 56 after a same-box sweep (16/40, 16/56, 16/80, 16/104, 32/80):
+// 32/80 was best on batched and churn by 0.2-0.4% and equal on the scale-out shard.
 constexpr int64_t kCostUnit = 16;
-constexpr int64_t kCostLeaveWhole = 16;
-constexpr int64_t kCostLeaveShared = 56;
+constexpr int64_t kCostLeaveWhole = 32;
+constexpr int64_t kCostLeaveShared = 80;
 
 // Greedy cut of the segments (segment s has npg[s / G] units) into shares of
 // cost at most B (B >= kCostUnit, so every share holds a unit).  Returns the

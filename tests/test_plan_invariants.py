@@ -3,8 +3,8 @@
 The plan builder itself is compiled from its header (tests/cpp/plan_dump.cpp
 prints its descriptor) and checked against a restatement here:
 - shares: the unit range [0, U) is cut greedily into consecutive shares of
-  cost at most B (a unit costs 16, leaving a segment inside a share costs 16
-  when the share held it from its first page, 56 otherwise; a share never
+  cost at most B (a unit costs 16, leaving a segment inside a share costs 32
+  when the share held it from its first page, 80 otherwise; a share never
   enters a segment it cannot take a unit of), and B is the smallest budget
   that needs at most W = min(U, grid warps) shares;
 - segments: each (slot, KV head) segment records its first and last warp
@@ -36,7 +36,7 @@ import pytest
 
 REPO = Path(__file__).resolve().parents[1]
 WPC = 6  # warps per CTA (kAttnWarps)
-UNIT, LEAVE_WHOLE, LEAVE_SHARED = 16, 16, 56
+UNIT, LEAVE_WHOLE, LEAVE_SHARED = 16, 32, 80
 
 
 @pytest.fixture(scope="module")
