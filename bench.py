@@ -607,7 +607,7 @@ def bench_ours(args):
                 "launch_ms_from": "timed region: step time / launches (includes launch gaps)",
                 "kernel_only_ms_profiled": kernel_only_ms,
             },
-            "gpu_launches": N_LAYERS * args.steps,
+            "gpu_launches": stats_after["kernel_launches"] - stats_before["kernel_launches"],
             "pool": {"cow_copies_timed": stats_after["cow_copies"] - stats_before["cow_copies"],
                      "shared_pages": stats_after["shared_pages"],
                      "replaced_slots": (churn_stats["replaced"] if churn is not None else 0)},
@@ -715,7 +715,9 @@ def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, war
         return ms, ctx0
 
     ms_alone, _ = timed(False)
+    launches0 = eng.stats()["kernel_launches"]
     ms, ctx0 = timed(True)
+    launches_per_step = (eng.stats()["kernel_launches"] - launches0) / (warmup + steps)
 
     # ---- parity of the assembled output (last step, last layer) on rank 0
     layer = N_LAYERS - 1
@@ -772,6 +774,7 @@ def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, war
             "parity_case": f"layer {layer} of the last timed step, 32 query heads over {rows} "
                            "positions, assembled output on rank 0 vs the oracle",
             "context": ctx0, "steps": steps, "warmup": warmup, "gpus": world,
+            "launches_per_step": launches_per_step,
             "shape_of_split": shape_world,
             "kv_heads_per_gpu": Gl,
             "exchange": ("in-kernel peer stores over NVLink + bounded arrival wait" if p2p else
@@ -824,7 +827,7 @@ def bench_headsplit(args):
                        "global_batch": 1, "layers": N_LAYERS,
                        "parallelism": f"KV-head split x{world}"},
             "hbm": {"frac_per_gpu": res["hbm_frac_per_gpu"], "peak_kind": peak_kind},
-            "headsplit": res, "gpu_launches": N_LAYERS * args.steps, "e2e": None,
+            "headsplit": res, "gpu_launches": res["launches_per_step"] * args.steps, "e2e": None,
         }), flush=True)
     if dist is not None:
         dist.destroy_process_group()
@@ -928,6 +931,7 @@ def bench_backbone(args):
     if dist is not None:
         dist.barrier()
     ctx0 = eng.length(slot)
+    launches0 = eng.stats()["kernel_launches"]
     clocks = ClockSampler(local)
     clocks.start()
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -945,6 +949,10 @@ def bench_backbone(args):
     clk = clocks.stop()
     ms_local = ev0.elapsed_time(ev1)
     bb.sync_check(sh)
+    # the engine counts its own launches (append + attention, and a combine
+    # launch where the plan merges split partials after the grid); the
+    # backbone adds embedding, 4 projections per layer, the head and argmax
+    engine_launches = eng.stats()["kernel_launches"] - launches0
 
     def max_ranks(x):
         if dist is None:
@@ -1021,7 +1029,7 @@ def bench_backbone(args):
                          "traffic": None, "algorithmic_bytes_per_step": step_bytes,
                          "peak_kind": peak_kind},
             "cpu_baseline": cpu, "clocks": clk, "e2e": e2e,
-            "gpu_launches": (3 + 5 * N_LAYERS) * args.steps,
+            "gpu_launches": (3 + 4 * N_LAYERS) * args.steps + engine_launches,
             "host_enqueue_ms_per_step": host_ms / args.steps,
         }), flush=True)
     bb.close()

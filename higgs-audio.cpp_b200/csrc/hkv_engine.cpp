@@ -258,6 +258,7 @@ struct hkv_engine {
     int64_t reserved_total = 0;
     int64_t shared_pages = 0;
     int64_t cow_copies = 0;
+    int64_t kernel_launches = 0;  // every kernel this engine enqueued
     std::vector<hkv::Slot> slots;
     std::vector<int32_t> free_slots;  // stack
     std::map<std::pair<uint64_t, int64_t>, hkv::Prefix> prefixes;
@@ -484,6 +485,7 @@ int flush_cow(hkv_engine *eng, cudaStream_t stream) {
     if (e == cudaSuccess) {
         launch_cow_copy(pool_view(eng), static_cast<const int32_t *>(dev), n_pairs, eng->d_err,
                         stream);
+        ++eng->kernel_launches;
         e = cudaGetLastError();
         if (e == cudaSuccess) {
             e = eng->cow_stage.mark_used(stream);
@@ -703,6 +705,7 @@ int do_append(hkv_engine *eng, int32_t layer, int32_t n, const int32_t *slots, c
         ProfileScope ps(eng, HKV_KERNEL_APPEND, stream);
         launch_append(pool_view(eng), rope_view(eng), eng->batch.view, layer, k, v, rope,
                       eng->d_err, stream);
+        ++eng->kernel_launches;
     }
     eng->batch.consumed = true;
     eng->batch.consumer_stream = stream;
@@ -724,6 +727,8 @@ int do_attention(hkv_engine *eng, int32_t layer, const float *q, const float *k_
         launch_attention(pool_view(eng), rope_view(eng), eng->batch.view, layer, q, k_new, v_new,
                          eng->part_o, eng->part_ml, eng->counters, out, xchg,
                          eng->scale_log2, eng->d_err, overlap, stream);
+        eng->kernel_launches +=
+            (eng->batch.view.combine && eng->batch.view.split_segments > 0) ? 2 : 1;
         const auto dt = std::chrono::steady_clock::now() - t0;
         std::lock_guard<std::mutex> lock(eng->host_mu);
         eng->launch_ns += std::chrono::duration_cast<std::chrono::nanoseconds>(dt).count();
@@ -1197,6 +1202,7 @@ int hkv_pool_stats_get(const hkv_engine *eng, hkv_pool_stats *out) {
     out->prefixes = static_cast<int32_t>(eng->prefixes.size());
     out->page_bytes = eng->page_bytes;
     out->cow_copies = eng->cow_copies;
+    out->kernel_launches = eng->kernel_launches;
     return HKV_OK;
 }
 
@@ -1262,6 +1268,7 @@ int hkv_rope_append_range(hkv_engine *eng, int32_t layer, int32_t slot, int64_t 
         ProfileScope ps(eng, HKV_KERNEL_APPEND, stream);
         launch_append_range(pool_view(eng), rope_view(eng), static_cast<const int32_t *>(dev),
                             begin, n_tokens, layer, k_prerope, v, true, eng->d_err, stream);
+        ++eng->kernel_launches;
     }
     HKV_CUDA_TRY(eng, eng->range_stage.mark_used(stream));
     return launch_status(eng, "range append kernel launch");
@@ -1337,6 +1344,7 @@ int hkv_gather(hkv_engine *eng, int32_t slot, int32_t layer, int64_t pos0, int64
         ProfileScope ps(eng, HKV_KERNEL_GATHER, stream);
         launch_gather(pool_view(eng), static_cast<const int32_t *>(dev), pos0, n, layer, k_out,
                       v_out, eng->d_err, stream);
+        ++eng->kernel_launches;
     }
     HKV_CUDA_TRY(eng, eng->gather_stage.mark_used(stream));
     return launch_status(eng, "gather kernel launch");
@@ -1507,6 +1515,7 @@ int hkv_split_wait(hkv_engine *eng, int32_t layer, hkv_stream stream_h) {
     // may still overlap it (enqueue_seq stays).
     launch_split_wait(reinterpret_cast<const uint32_t *>(eng->xchg) + layer,
                       eng->split_target[layer], eng->d_err, static_cast<cudaStream_t>(stream_h));
+    ++eng->kernel_launches;
     return launch_status(eng, "split wait launch");
 }
 

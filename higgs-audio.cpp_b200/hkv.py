@@ -83,6 +83,7 @@ class PoolStats(ctypes.Structure):
         ("prefixes", ctypes.c_int32),
         ("page_bytes", ctypes.c_int64),
         ("cow_copies", ctypes.c_int64),
+        ("kernel_launches", ctypes.c_int64),
     ]
 
 

@@ -45,7 +45,7 @@
 extern "C" {
 #endif
 
-#define HKV_ABI_VERSION 1
+#define HKV_ABI_VERSION 2  /* 2: hkv_pool_stats.kernel_launches */
 
 typedef enum hkv_status {
     HKV_OK = 0,
@@ -99,6 +99,7 @@ typedef struct hkv_pool_stats {
     int32_t prefixes;
     int64_t page_bytes;    /* bytes of one page (all layers, K and V)         */
     int64_t cow_copies;    /* pages copied on write since creation            */
+    int64_t kernel_launches; /* kernels this engine enqueued since creation   */
 } hkv_pool_stats;
 
 /* Kernel ids for the CUDA-event profiler. */
