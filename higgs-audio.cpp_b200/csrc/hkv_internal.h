@@ -133,12 +133,6 @@ struct RopeView {
 // HKV_CUDA_CORES=1 builds the attention's QK and PV on the CUDA cores (exact
 // F16 -> F32 conversions, F32 products) instead of the tensor cores: the
 // comparison variant, never the default.
-// HKV_CTA_FINAL=1: segments of CTA-merged plans are merged at the end of the
-// attention launch by the CTA that published their last partial (all its
-// warps), instead of by a combine launch or a two-level merge in the launch.
-#ifndef HKV_CTA_FINAL
-#define HKV_CTA_FINAL 0
-#endif
 #ifndef HKV_CUDA_CORES
 #define HKV_CUDA_CORES 0
 #endif

@@ -48,15 +48,10 @@ constexpr int kWarpSmem = kAttnStages * kStageBytes + kQcBytes + kPBufBytes + kB
 // the run it starts), each o[4][128] + (m, l)[4]; then one ticket per run.
 constexpr int kCtaPartFloats = kGqa * kHeadDim + 2 * kGqa;
 constexpr int kCtaPartBytes = kCtaPartFloats * 4;
-// After the slots: one run ticket per warp (32 B), then -- for the in-launch
-// final merge of CTA-merged segments -- two mbarriers, the count of pending
-// final merges and their segments (64 B).
-constexpr int kMaxPendingFinal = 12;
-constexpr int kCtaSmem = kAttnWarps * 2 * kCtaPartBytes + 32 + 64;
+constexpr int kCtaSmem = kAttnWarps * 2 * kCtaPartBytes + 32;
 constexpr int kWhereAppend = 0;
 constexpr int kWhereAttn = 1;
 constexpr int kWhereGather = 3;
-constexpr int kWhereFinal = 6;
 constexpr int kWhereCow = 4;
 constexpr int kWhereSplitWait = 5;
 
@@ -598,109 +593,6 @@ __device__ __forceinline__ void signal_arrival(const Exchange &x, int layer, int
     }
 }
 
-#if HKV_CTA_FINAL
-// End of an attention CTA of a CTA-merged plan.  Every warp arrives here once
-// (after its main loop, or at once when it has no share or gave up); then the
-// CTA merges the segments whose last CTA partial it published: each of its
-// warps merges a contiguous chunk of the segment's partials into its shared
-// memory slot (two slot banks alternate between segments), and warp 0 merges
-// the warps' results in warp order and writes the output.  Both waits are
-// bounded: a warp that never arrives ends them with kErrTimeout, not a hang.
-__device__ __forceinline__ void cta_final_merges(const BatchView &batch, int G, int layer,
-                                              const float *part_o, const float *part_ml,
-                                              int32_t *counters, float *out, const Exchange &xchg,
-                                              float *cta_slots, uint32_t end_bar, uint32_t merge_bar,
-                                              const volatile int *pending_n, const volatile int *pending,
-                                              int lane, int wid, DeviceError *err) {
-    __syncwarp();
-    if (lane == 0) {
-        mbar_arrive(end_bar);
-    }
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(end_bar, 0))) {
-        if (lane == 0) {
-            record_error(err, kErrTimeout, kWhereFinal, wid, blockIdx.x);
-        }
-        return;
-    }
-    const int np = min(*pending_n, kMaxPendingFinal);
-    for (int it = 0; it < np; ++it) {
-        const int eh = pending[it];
-        const int4 sg = batch.seg[eh];
-        const int nparts = sg.y;
-        const int chunk = (nparts + kAttnWarps - 1) / kAttnWarps;
-        const int used = (nparts + chunk - 1) / chunk;
-        float *bank = cta_slots + (it & 1) * kAttnWarps * kCtaPartFloats;
-        if (wid < used) {
-            const int a = wid * chunk;
-            Merged r;
-            merge_partials_wide(part_o, part_ml, sg.x + a, min(chunk, nparts - a), lane, r);
-            float *slot = bank + wid * kCtaPartFloats;
-#pragma unroll
-            for (int j = 0; j < kGqa; ++j) {
-                reinterpret_cast<float4 *>(slot + j * kHeadDim)[lane] = r.o[j];
-            }
-            if (lane == 0) {
-#pragma unroll
-                for (int j = 0; j < kGqa; ++j) {
-                    slot[kGqa * kHeadDim + 2 * j] = r.m[j];
-                    slot[kGqa * kHeadDim + 2 * j + 1] = r.l[j];
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(merge_bar);  // one phase per pending segment
-        }
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(merge_bar, static_cast<uint32_t>(it & 1)))) {
-            if (lane == 0) {
-                record_error(err, kErrTimeout, kWhereFinal, wid, blockIdx.x);
-            }
-            return;
-        }
-        if (wid != 0) {
-            continue;
-        }
-        Merged res;
-#pragma unroll
-        for (int j = 0; j < kGqa; ++j) {
-            float mx = -INFINITY;
-            for (int w = 0; w < used; ++w) {
-                mx = fmaxf(mx, bank[w * kCtaPartFloats + kGqa * kHeadDim + 2 * j]);
-            }
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            float den = 0.f;
-            for (int w = 0; w < used; ++w) {
-                const float *slot = bank + w * kCtaPartFloats;
-                const float wt = exp2f(slot[kGqa * kHeadDim + 2 * j] - mx);
-                den += wt * slot[kGqa * kHeadDim + 2 * j + 1];
-                const float4 ov = reinterpret_cast<const float4 *>(slot + j * kHeadDim)[lane];
-                acc.x += wt * ov.x;
-                acc.y += wt * ov.y;
-                acc.z += wt * ov.z;
-                acc.w += wt * ov.w;
-            }
-            res.o[j] = acc;
-            res.m[j] = mx;
-            res.l[j] = den;
-        }
-        const int e = eh / G;
-        const int h = eh - e * G;
-        const int n_dst = xchg.n_ranks == 0 ? 1 : xchg.n_ranks;
-        for (int r = 0; r < n_dst; ++r) {
-            float4 *ob = reinterpret_cast<float4 *>(out_slice(out, xchg, r, layer, e, h, G));
-#pragma unroll
-            for (int j = 0; j < kGqa; ++j) {
-                ob[j * (kHeadDim / 4) + lane] = normalised(res, j);
-            }
-        }
-        if (lane == 0) {
-            counters[eh] = 0;  // ready for the next launch
-        }
-        signal_arrival(xchg, layer, lane);
-    }
-}
-#endif
-
 template <bool kAppend, bool kCtaMerge>
 __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     attention_kernel(PoolView pool, RopeView rope, BatchView batch, int layer,
@@ -716,32 +608,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     const int W = batch.n_warps;
     float *cta_slots = reinterpret_cast<float *>(smem + kAttnWarps * kWarpSmem);
     int *run_ticket = reinterpret_cast<int *>(smem + kAttnWarps * kWarpSmem + kAttnWarps * 2 * kCtaPartBytes);
-    // in-launch final merge state (CTA-merged plans): end barrier, merge
-    // barrier, pending count, pending segments
-    uint8_t *final_area = smem + kAttnWarps * kWarpSmem + kAttnWarps * 2 * kCtaPartBytes + 32;
-    const uint32_t end_bar = smem_u32(final_area);
-    const uint32_t merge_bar = end_bar + 8;
-    int *pending_n = reinterpret_cast<int *>(final_area + 16);
-    int *pending = pending_n + 1;
     if (kCtaMerge) {
         if (threadIdx.x < kAttnWarps) {
             run_ticket[threadIdx.x] = 0;
         }
-        if (threadIdx.x == 0) {
-            mbar_init(end_bar, kAttnWarps);
-            mbar_init(merge_bar, kAttnWarps);
-            *pending_n = 0;
-            fence_barrier_init();
-        }
-        __syncthreads();  // the only unbounded CTA barrier: before any warp can leave
+        __syncthreads();  // the only CTA barrier: before any warp can leave
     }
     if (gw >= W) {
-#if HKV_CTA_FINAL
-        if (kCtaMerge) {
-            cta_final_merges(batch, G, layer, part_o, part_ml, counters, out, xchg, cta_slots, end_bar,
-                             merge_bar, pending_n, pending, lane, wid, err);
-        }
-#endif
         return;
     }
     // The plan hands each warp its share, its starting cursor and the
@@ -753,12 +626,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     const int u_begin = ws2.x;
     const int u_end = ws2.y;
     if (u_begin >= u_end) {
-#if HKV_CTA_FINAL
-        if (kCtaMerge) {
-            cta_final_merges(batch, G, layer, part_o, part_ml, counters, out, xchg, cta_slots, end_bar,
-                             merge_bar, pending_n, pending, lane, wid, err);
-        }
-#endif
         return;
     }
     const uint32_t stage0 = smem_u32(smem + wid * kWarpSmem);
@@ -981,34 +848,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             }
             signal_arrival(xchg, layer, lane);
         };
-#if HKV_CTA_FINAL
-        if (kCtaMerge) {
-            // One ticket per CTA partial; the CTA that publishes the last one
-            // merges the segment at its end with all of its warps.
-            int ticket = 0;
-            if (lane == 0) {
-                ticket = atomicAdd(counters + eh, 1);
-            }
-            ticket = __shfl_sync(0xffffffffu, ticket, 0);
-            if (ticket == nparts - 1) {
-                __threadfence();
-                int idx = 0;
-                if (lane == 0) {
-                    idx = atomicAdd(pending_n, 1);
-                    if (idx < kMaxPendingFinal) {
-                        pending[idx] = eh;
-                    }
-                }
-                idx = __shfl_sync(0xffffffffu, idx, 0);
-                if (idx >= kMaxPendingFinal) {  // list full: this warp merges it alone
-                    Merged res;
-                    merge_partials_wide(part_o, part_ml, p_first, nparts, lane, res);
-                    finish(res);
-                }
-            }
-            return;
-        }
-#endif
         if (n_groups == 0) {
             int ticket = 0;
             if (lane == 0) {
@@ -1179,12 +1018,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
                 mbar_wait_bounded(bar0 + 8 * (kk % kAttnStages),
                                   static_cast<uint32_t>(kk / kAttnStages) & 1u);
             }
-#if HKV_CTA_FINAL
-            if (kCtaMerge) {
-                cta_final_merges(batch, G, layer, part_o, part_ml, counters, out, xchg, cta_slots, end_bar,
-                             merge_bar, pending_n, pending, lane, wid, err);
-            }
-#endif
             return;
         }
         const uint32_t kt = stage0 + s * kStageBytes;
@@ -1388,12 +1221,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     // finishes its tail.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     flush(true);
-#if HKV_CTA_FINAL
-    if (kCtaMerge) {
-        cta_final_merges(batch, G, layer, part_o, part_ml, counters, out, xchg, cta_slots, end_bar,
-                             merge_bar, pending_n, pending, lane, wid, err);
-    }
-#endif
 }
 
 // ==================================================================== combine

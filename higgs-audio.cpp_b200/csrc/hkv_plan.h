@@ -68,13 +68,7 @@ inline bool plan_cta_merge(int64_t n_segments, int64_t W) { return W >= 2 * kAtt
 // merge would sit in the tail behind fences, tickets and a second level.
 constexpr int32_t kCombineMaxParts = 32;
 inline bool plan_combine(bool cta_merge, int32_t max_parts) {
-#if HKV_CTA_FINAL
-    (void)cta_merge;
-    (void)max_parts;
-    return false;  // CTA-merged segments are merged at the end of the launch
-#else
     return cta_merge && max_parts > 1 && max_parts <= kCombineMaxParts;
-#endif
 }
 
 // Share costs in sixteenths of a unit, from per-warp timestamps of the
