@@ -57,7 +57,8 @@ constexpr int kQK = 256;        // weights per Q4_K / Q8_K block
 constexpr int kQ4Bytes = 144;   // bytes per Q4_K block
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxVec = 8;      // activation vectors per launch
+constexpr int kMaxVec = 8;      // activation vectors per launch (one mma n-tile)
+constexpr int kTileRows = 16;   // weight rows of an mma tile
 constexpr int kClusterCtas = 4; // CTAs per head in the q/k/v launch (32 rows each)
 constexpr int kMaxCols = 16384;
 
@@ -77,10 +78,14 @@ struct GemvParams {
     int32_t y_rows[3];
     const float *head_norm[2];  // kQkv: q_norm, k_norm [128]
     int32_t rows_per_cta;     // contiguous weight rows of one CTA
-    int32_t chunk_rows;       // rows per ring stage
+    int32_t chunk_rows;       // rows per ring stage (kTileRows for several vectors)
     int32_t n_stages;         // ring stages (<= kMaxStages)
     int32_t stage_bytes;      // chunk_rows * row bytes * matrices
-    int32_t lanes_per_row;    // 8 or 16 consumer lanes share a row's dot product
+    int32_t ring_bytes;       // shared memory of the ring
+    int32_t empty_count;      // arrivals that free a stage
+    int32_t lanes_per_row;    // one vector: 8 or 16 consumer lanes share a row's dot product
+    int32_t ksplit;           // several vectors: warps sharing one tile's blocks
+    int32_t tensor;           // 1: the tensor-core kernel even for one vector
     DeviceError *err;         // bounded-wait timeouts are recorded here
 };
 
@@ -92,9 +97,17 @@ struct GemvParams {
 constexpr int kMaxStages = 12;
 constexpr int kRingCap = 100 * 1024;
 constexpr int kStreamStageBytes = 24 * 1024;
-constexpr int kBarBytes = 208;              // kMaxStages full + kMaxStages empty + 1 norm mbarrier
+// "full" mbarriers: one per stage, completed once per chunk loaded into it
+// (one vector: a warp takes its rows in stage order, so it always waits for
+// the phase after the one it saw last); one per tile, used once, for the
+// tensor-core kernel, whose warps take tiles out of stage order -- waiting on
+// a reused stage's second phase before its first completed would return at
+// once, as the first phase's parity differs.
+constexpr int kMaxTiles = 24;
+constexpr int kBarBytes = 304;              // kMaxTiles full + kMaxStages empty + 1 norm mbarrier
 constexpr int kQkvRows = 32;                // rows per CTA in the q/k/v launch (4 per head)
-static_assert(2 * kMaxStages * 8 + 8 <= kBarBytes && kBarBytes % 16 == 0, "mbarrier area too small");
+static_assert((kMaxTiles + kMaxStages + 1) * 8 <= kBarBytes && kBarBytes % 16 == 0, "mbarrier area too small");
+static_assert(kMaxTiles >= kMaxStages, "the one-vector kernel uses a full barrier per stage");
 
 __device__ __forceinline__ int4 ld_stream(const uint8_t *p) {
     return __ldcs(reinterpret_cast<const int4 *>(p));
@@ -137,28 +150,44 @@ __device__ __forceinline__ double warp_sum_double(double v) {
 // same chunk of 8 consecutive items, hit 8 different bank groups.
 __device__ __forceinline__ int q8_offset(int j, int c) { return j * 64 + ((c ^ ((j >> 1) & 3)) << 4); }
 
-// Shared-memory image of the Q8_K activations.
+// Shared-memory image of the Q8_K activations, in one of two layouts:
+//  * rows (frag == 0, the one-vector dot products): q [n][cols] with the
+//    chunks of each 64-byte item rotated (q8_offset), and s, the sums of q
+//    over each 32-element sub-block;
+//  * tensor-core fragments (frag == NB, the several-vector kernels): for item
+//    j (sub-blocks 2p, 2p+1 of block j / 4) and vector e, 64 bytes at
+//    (j * NB + e) * 64, where lane t (0..3) of an mma B fragment finds, at
+//    t * 16, elements 8t .. 8t+7 of sub-block 2p then of sub-block 2p+1 --
+//    one conflict-free 16-byte load per lane.  No sums: the mins go through
+//    the mma as well.
 struct Q8View {
-    int8_t *q;   // [n][cols]
+    int8_t *q;   // rows: [n][cols]; fragments: [cols / 64][NB][64]
     float *d;    // [n][nsb]
-    int32_t *s;  // [n][nsb * 8]: sum of q over each 32-element sub-block
+    int32_t *s;  // rows only: [n][nsb * 8]
     double *red; // [kWarps + 1] reduction scratch
+    int frag;    // 0, or NB of the fragment layout
 };
 
-__host__ __device__ inline size_t q8_smem_bytes(int n, int cols) {
+__host__ __device__ inline size_t q8_smem_bytes(int n, int cols, bool frag) {
     const int nsb = cols / kQK;
     size_t b = static_cast<size_t>(n) * cols;          // q
     b = (b + 15) & ~size_t(15);
     b += static_cast<size_t>(n) * nsb * 4;             // d
     b = (b + 15) & ~size_t(15);
-    b += static_cast<size_t>(n) * nsb * 8 * 4;         // s
+    if (!frag) b += static_cast<size_t>(n) * nsb * 8 * 4;  // s
     b = (b + 15) & ~size_t(15);
     b += (kWarps + 1) * sizeof(double);                // red
     b = (b + 15) & ~size_t(15);
     return b;
 }
 
-__device__ inline Q8View carve_q8(unsigned char *smem, int n, int cols) {
+// kQkv: the projected rows [nb][kQkvRows] and the cluster's sums of
+// squares [kClusterCtas][nb] after the activation image.
+__host__ __device__ constexpr int qkv_extra_bytes(int mode, int nb) {
+    return mode == kQkv ? nb * kQkvRows * 4 + kClusterCtas * nb * 8 + 16 : 0;
+}
+
+__device__ inline Q8View carve_q8(unsigned char *smem, int n, int cols, bool frag) {
     const int nsb = cols / kQK;
     Q8View v;
     size_t off = 0;
@@ -167,9 +196,21 @@ __device__ inline Q8View carve_q8(unsigned char *smem, int n, int cols) {
     v.d = reinterpret_cast<float *>(smem + off);
     off = (off + static_cast<size_t>(n) * nsb * 4 + 15) & ~size_t(15);
     v.s = reinterpret_cast<int32_t *>(smem + off);
-    off = (off + static_cast<size_t>(n) * nsb * 32 + 15) & ~size_t(15);
+    if (!frag) off = (off + static_cast<size_t>(n) * nsb * 32 + 15) & ~size_t(15);
     v.red = reinterpret_cast<double *>(smem + off);
+    v.frag = frag ? n : 0;
     return v;
+}
+
+// Where lane `lane` of a quantising warp stores its 8 values of block b of
+// vector e: elements 8 lane .. 8 lane + 7 of the block, i.e. quarter
+// (lane & 3) of sub-block lane / 4.
+__device__ __forceinline__ int8_t *q8_store_at(const Q8View &a, int cols, int e, int b, int lane) {
+    if (a.frag != 0) {
+        const int j = b * 4 + (lane >> 3);
+        return a.q + (static_cast<size_t>(j) * a.frag + e) * 64 + (lane & 3) * 16 + ((lane >> 2) & 1) * 8;
+    }
+    return a.q + static_cast<size_t>(e) * cols + q8_offset(b * 4 + (lane >> 3), (lane & 7) >> 1) + (lane & 1) * 8;
 }
 
 // Barrier of the kWarps consumer warps only (the producer warp never joins).
@@ -222,14 +263,15 @@ __device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View
         lo |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
         hi |= (static_cast<uint32_t>(q[i + 4]) & 0xFFu) << (8 * i);
     }
-    *reinterpret_cast<uint2 *>(a.q + static_cast<size_t>(e) * cols + q8_offset(b * 4 + (lane >> 3), (lane & 7) >> 1) +
-                               (lane & 1) * 8) = make_uint2(lo, hi);
-    int qs = 0;
+    *reinterpret_cast<uint2 *>(q8_store_at(a, cols, e, b, lane)) = make_uint2(lo, hi);
+    if (a.frag == 0) {
+        int qs = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) qs += q[i];
-    qs += __shfl_xor_sync(0xffffffffu, qs, 1);
-    qs += __shfl_xor_sync(0xffffffffu, qs, 2);
-    if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
+        for (int i = 0; i < 8; ++i) qs += q[i];
+        qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+        qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+        if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
+    }
     if (lane == 0) a.d[e * nsb + b] = d;
 }
 
@@ -286,14 +328,15 @@ __device__ __forceinline__ void quantize_blocks(const float (&v)[S][8], int n_sl
             lo |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
             hi |= (static_cast<uint32_t>(q[i + 4]) & 0xFFu) << (8 * i);
         }
-        *reinterpret_cast<uint2 *>(a.q + static_cast<size_t>(e) * cols + q8_offset(b * 4 + (lane >> 3), (lane & 7) >> 1) +
-                                   (lane & 1) * 8) = make_uint2(lo, hi);
-        int qs = 0;
+        *reinterpret_cast<uint2 *>(q8_store_at(a, cols, e, b, lane)) = make_uint2(lo, hi);
+        if (a.frag == 0) {
+            int qs = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) qs += q[i];
-        qs += __shfl_xor_sync(0xffffffffu, qs, 1);
-        qs += __shfl_xor_sync(0xffffffffu, qs, 2);
-        if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
+            for (int i = 0; i < 8; ++i) qs += q[i];
+            qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+            qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+            if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
+        }
         if (lane == 0) a.d[e * nsb + b] = d;
     }
 }
@@ -475,6 +518,65 @@ __device__ __forceinline__ float dot_act(const unsigned char *blk, int part, con
            __fmul_rn(half_bits(hdr.x >> 16), x.d) * static_cast<float>(msum);
 }
 
+// D = A B + C for a 16x32 tile A of unsigned bytes (Q4_K nibbles or
+// broadcast 6-bit mins) and a 32x8 tile B of signed bytes (Q8_K), s32
+// accumulators.  Fragments: lane l holds rows l/4 and l/4 + 8 of A and D,
+// column l/4 of B; a[0], a[2] (row l/4) and a[1], a[3] (row l/4 + 8) carry k
+// quads (l % 4) and (l % 4) + 4, b[0], b[1] the same quads of B, d columns
+// 2 (l % 4) and 2 (l % 4) + 1.  Which 32 elements a k slot stands for is
+// free as long as A and B agree: here slot quads (t, t + 4) of lane quarter
+// t are elements 8t .. 8t + 7 of a sub-block, 8 contiguous bytes on both
+// sides.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Packed 6-bit scales (sc) and mins (mn) of sub-blocks 0-3 (lo) and 4-7
+// (hi), one byte each, from bytes 4..15 of a Q4_K block.
+struct BlockScales {
+    uint32_t sc_lo, sc_hi, mn_lo, mn_hi;
+};
+
+__device__ __forceinline__ BlockScales block_scales(uint32_t s0, uint32_t s1, uint32_t s2) {
+    BlockScales r;
+    r.sc_lo = s0 & 0x3F3F3F3Fu;
+    r.mn_lo = s1 & 0x3F3F3F3Fu;
+    r.sc_hi = (s2 & 0x0F0F0F0Fu) | (((s0 >> 6) & 0x03030303u) << 4);
+    r.mn_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | (((s1 >> 6) & 0x03030303u) << 4);
+    return r;
+}
+
+// Scale of sub-block sb (0..7; a constant after unrolling), and its min
+// copied into all 4 bytes of a word.
+__device__ __forceinline__ int sub_scale(const BlockScales &s, int sb) {
+    return static_cast<int>(((sb < 4 ? s.sc_lo : s.sc_hi) >> (8 * (sb & 3))) & 0xFFu);
+}
+__device__ __forceinline__ uint32_t sub_min4(const BlockScales &s, int sb) {
+    const uint32_t b = static_cast<uint32_t>(sb & 3);
+    return __byte_perm(sb < 4 ? s.mn_lo : s.mn_hi, 0u, b | (b << 4) | (b << 8) | (b << 12));
+}
+
+// Output of row r (of the CTA) for vector e: t[0] (and t[1], the up
+// projection of kSwiglu).
+template <int MODE>
+__device__ __forceinline__ void store_row(const GemvParams &p, float *res, int row0, int r, int e, float t0,
+                                          float t1) {
+    const int grow = row0 + r;
+    if (MODE == kPlain) {
+        const size_t o = static_cast<size_t>(e) * p.rows + grow;
+        p.y[0][o] = p.residual != nullptr ? p.residual[o] + t0 : t0;
+    } else if (MODE == kSwiglu) {
+        const float sl = t0 / (1.0f + expf(-t0));
+        p.y[0][static_cast<size_t>(e) * p.rows + grow] = sl * t1;
+    } else {
+        res[e * kQkvRows + r] = t0;
+    }
+}
+
 // One CTA streams its p.rows_per_cta contiguous weight rows (of each matrix)
 // through a ring of p.n_stages bulk-copy stages in shared memory, issued by a
 // producer warp: the first stages before waiting for the previous kernel,
@@ -486,9 +588,12 @@ __device__ __forceinline__ float dot_act(const unsigned char *blk, int part, con
 // item is the limit at batch 1, not bandwidth); the row sum is a fixed-order
 // shuffle reduction (deterministic), and the row's stage slot is released by
 // one arrival on the stage's "empty" barrier -- no CTA-wide barrier in the
-// loop.  NB activation vectors (1 or kMaxVec).
+// loop.  NB activation vectors: 1, or kMaxVec with the products on the
+// tensor cores (mma m16n8k32, integer): stages of kTileRows rows, each tile
+// of 16 rows x 8 vectors taken by p.ksplit warps over disjoint block ranges,
+// whose partial sums are added in a fixed order after one consumer barrier.
 template <int MODE, int NB>
-__global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2) gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int kMats = MODE == kSwiglu ? 2 : 1;
     const int nsb = p.cols / kQK;
@@ -500,21 +605,24 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
     const int R = p.chunk_rows;
     const int n_stages = p.n_stages;
     const int stage_bytes = p.stage_bytes;
-    const int ring_bytes = n_stages * stage_bytes;
+    const int ring_bytes = p.ring_bytes;
     const int n_chunks = (nrows + R - 1) / R;
     unsigned char *ring = smem;
     const uint32_t full0 = smem_u32(smem + ring_bytes);
-    const uint32_t empty0 = full0 + 8 * kMaxStages;
+    const uint32_t empty0 = full0 + 8 * kMaxTiles;
     const uint32_t normbar = empty0 + 8 * kMaxStages;
+    // full barrier of chunk c and the parity of its completion
+    auto full_of = [&](int c) { return full0 + 8 * (NB > 1 ? c : c % n_stages); };
+    auto full_parity = [&](int c) { return NB > 1 ? 0u : static_cast<uint32_t>((c / n_stages) & 1); };
     int m = 0, mrow0 = row0;
     if (MODE == kQkv) {
         m = row0 < p.row_end[0] ? 0 : (row0 < p.row_end[1] ? 1 : 2);
         mrow0 = row0 - (m == 0 ? 0 : p.row_end[m - 1]);
     }
     if (tid == 0) {
+        for (int c = 0; c < (NB > 1 ? n_chunks : n_stages); ++c) mbar_init(full_of(c), 1);
         for (int st = 0; st < n_stages; ++st) {
-            mbar_init(full0 + 8 * st, 1);
-            mbar_init(empty0 + 8 * st, static_cast<uint32_t>(R));
+            mbar_init(empty0 + 8 * st, static_cast<uint32_t>(p.empty_count));
         }
         mbar_init(normbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -525,9 +633,11 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
     pdl_trigger();
 
     unsigned char *after_ring = smem + ring_bytes + kBarBytes;
-    const Q8View a = carve_q8(after_ring, p.n, p.cols);
-    float *normbuf = reinterpret_cast<float *>(after_ring + q8_smem_bytes(p.n, p.cols));  // [cols] if p.norm
+    const Q8View a = carve_q8(after_ring, NB > 1 ? NB : p.n, p.cols, NB > 1);
+    float *normbuf = reinterpret_cast<float *>(after_ring + q8_smem_bytes(NB > 1 ? NB : p.n, p.cols, NB > 1));
     float *res = normbuf + (p.norm != nullptr ? p.cols : 0);  // kQkv [NB][32]
+    // several vectors: partial sums [kWarps][kMats][32 lanes][4]
+    float *part = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(res) + qkv_extra_bytes(MODE, NB));
     bool bad = false;
 
     if (producer) {
@@ -564,7 +674,7 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
                 const int r0 = c * R;
                 const uint32_t bytes = static_cast<uint32_t>(min(R, nrows - r0) * row_bytes);
                 const uint32_t stage = smem_u32(ring + (c % n_stages) * stage_bytes);
-                const uint32_t bar = full0 + 8 * (c % n_stages);
+                const uint32_t bar = full_of(c);
                 mbar_arrive_expect_tx(bar, bytes * kMats);
 #pragma unroll
                 for (int k = 0; k < kMats; ++k) {
@@ -576,7 +686,7 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             // the CTA must not exit with copies in flight: wait (bounded) for
             // the last copy issued into each stage
             for (int c = max(0, issued - n_stages); c < issued; ++c) {
-                mbar_wait_bounded(full0 + 8 * (c % n_stages), static_cast<uint32_t>((c / n_stages) & 1));
+                mbar_wait_bounded(full_of(c), full_parity(c));
             }
             if (p.norm != nullptr) mbar_wait_bounded(normbar, 0);
         }
@@ -591,88 +701,210 @@ __global__ void __launch_bounds__(kThreads + 32, 2) gemv_kernel(GemvParams p) {
             }
             bad = true;
         }
-        // L = p.lanes_per_row lanes per row: lane group q = lane / L of warp
-        // w takes CTA rows (32 / L) w + q, then the same plus 32 kWarps / L,
-        // ...; within a row, lane l = lane % L takes items l, l + L, ...
-        // with four independent accumulators.
-        const int items = nsb * 4;
-        const int lpr = p.lanes_per_row;
-        const int rows_per_warp = 32 / lpr;
-        const int qg = lane / lpr, l8 = lane % lpr;
-        for (int base = 0; base < nrows && !bad; base += rows_per_warp * kWarps) {
-            const int r = base + rows_per_warp * warp + qg;
-            const bool has_row = r < nrows;
-            const int c = has_row ? r / R : 0, rs = has_row ? r % R : 0;
-            const uint32_t full = full0 + 8 * (c % n_stages);
-            const bool ok = !has_row || mbar_wait_bounded(full, static_cast<uint32_t>((c / n_stages) & 1));
-            if (!__all_sync(0xffffffffu, ok)) {
-                if (lane == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
-                    p.err->where = HKV_KERNEL_GEMV;
-                    p.err->a = blockIdx.x;
-                    p.err->b = c;
+        if constexpr (NB == 1) {
+            // L = p.lanes_per_row lanes per row: lane group q = lane / L of warp
+            // w takes CTA rows (32 / L) w + q, then the same plus 32 kWarps / L,
+            // ...; within a row, lane l = lane % L takes items l, l + L, ...
+            // with four independent accumulators.
+            const int items = nsb * 4;
+            const int lpr = p.lanes_per_row;
+            const int rows_per_warp = 32 / lpr;
+            const int qg = lane / lpr, l8 = lane % lpr;
+            for (int base = 0; base < nrows && !bad; base += rows_per_warp * kWarps) {
+                const int r = base + rows_per_warp * warp + qg;
+                const bool has_row = r < nrows;
+                const int c = has_row ? r / R : 0, rs = has_row ? r % R : 0;
+                const bool ok = !has_row || mbar_wait_bounded(full_of(c), full_parity(c));
+                if (!__all_sync(0xffffffffu, ok)) {
+                    if (lane == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
+                        p.err->where = HKV_KERNEL_GEMV;
+                        p.err->a = blockIdx.x;
+                        p.err->b = c;
+                    }
+                    bad = true;
+                    break;
                 }
-                bad = true;
-                break;
-            }
-            const unsigned char *stage = ring + (c % n_stages) * stage_bytes;
-            float acc[kMats][NB][4];
-#pragma unroll
-            for (int k = 0; k < kMats; ++k)
-#pragma unroll
-                for (int e = 0; e < NB; ++e)
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) acc[k][e][u] = 0.0f;
-            if (has_row) {
-                for (int j0 = l8; j0 < items; j0 += 4 * lpr) {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int j = j0 + lpr * u;
-                        if (j < items) {
-                            const int sb = j >> 2, part = j & 3;
-#pragma unroll
-                            for (int e = 0; e < NB; ++e) {
-                                if (e < p.n) {
-                                    ActPart ax;
-                                    load_act(ax, a, p.cols, nsb, sb, part, e);
-#pragma unroll
-                                    for (int k = 0; k < kMats; ++k) {
-                                        acc[k][e][u] += dot_act(stage + (k * R + rs) * row_bytes + sb * kQ4Bytes,
-                                                                part, ax);
+                const unsigned char *stage = ring + (c % n_stages) * stage_bytes;
+                float acc[kMats][NB][4];
+    #pragma unroll
+                for (int k = 0; k < kMats; ++k)
+    #pragma unroll
+                    for (int e = 0; e < NB; ++e)
+    #pragma unroll
+                        for (int u = 0; u < 4; ++u) acc[k][e][u] = 0.0f;
+                if (has_row) {
+                    for (int j0 = l8; j0 < items; j0 += 4 * lpr) {
+    #pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = j0 + lpr * u;
+                            if (j < items) {
+                                const int sb = j >> 2, part = j & 3;
+    #pragma unroll
+                                for (int e = 0; e < NB; ++e) {
+                                    if (e < p.n) {
+                                        ActPart ax;
+                                        load_act(ax, a, p.cols, nsb, sb, part, e);
+    #pragma unroll
+                                        for (int k = 0; k < kMats; ++k) {
+                                            acc[k][e][u] += dot_act(stage + (k * R + rs) * row_bytes + sb * kQ4Bytes,
+                                                                    part, ax);
+                                        }
                                     }
                                 }
                             }
                         }
                     }
                 }
-            }
-            __syncwarp();
-            if (has_row && l8 == 0) mbar_arrive(empty0 + 8 * (c % n_stages));  // the row's bytes are read
-            float t[kMats][NB];
-#pragma unroll
-            for (int k = 0; k < kMats; ++k)
-#pragma unroll
-                for (int e = 0; e < NB; ++e) {
-                    float v = (acc[k][e][0] + acc[k][e][1]) + (acc[k][e][2] + acc[k][e][3]);
-#pragma unroll
-                    for (int off = 8; off > 0; off >>= 1) {
-                        if (off < lpr) v += __shfl_xor_sync(0xffffffffu, v, off);
+                __syncwarp();
+                if (has_row && l8 == 0) mbar_arrive(empty0 + 8 * (c % n_stages));  // the row's bytes are read
+                float t[kMats][NB];
+    #pragma unroll
+                for (int k = 0; k < kMats; ++k)
+    #pragma unroll
+                    for (int e = 0; e < NB; ++e) {
+                        float v = (acc[k][e][0] + acc[k][e][1]) + (acc[k][e][2] + acc[k][e][3]);
+    #pragma unroll
+                        for (int off = 8; off > 0; off >>= 1) {
+                            if (off < lpr) v += __shfl_xor_sync(0xffffffffu, v, off);
+                        }
+                        t[k][e] = v;
                     }
-                    t[k][e] = v;
+                if (has_row && l8 == 0) {
+    #pragma unroll
+                    for (int e = 0; e < NB; ++e) {
+                        if (e < p.n) store_row<MODE>(p, res, row0, r, e, t[0][e], t[kMats - 1][e]);
+                    }
                 }
-            if (has_row && l8 == 0) {
-                const int grow = row0 + r;
+            }
+        } else {
+            // Tile i = CTA rows 16 i .. 16 i + 15, in stage i % n_stages;
+            // item it = tile it / ks, blocks [nsb s / ks, nsb (s + 1) / ks)
+            // of slice s = it % ks.  Per block and matrix, lane (g, t) keeps
+            // the s32 sums of rows g, g + 8 for vectors 2t, 2t + 1: the
+            // scaled nibble products sum_j sc_j (q4 . q8)_j and, through the
+            // same mma with the min broadcast as A, sum_j m_j bsum_j; then
+            // (d4 d8) isum - (dmin4 d8) msum joins the float accumulator.
+            constexpr uint32_t kLo = 0x0F0F0F0Fu;
+            const int ks = p.ksplit;
+            const int tiles = (nrows + kTileRows - 1) / kTileRows;
+            const int n_items = tiles * ks;
+            const int g = lane >> 2, tq = lane & 3;
+            float4 *part4 = reinterpret_cast<float4 *>(part);
+            for (int it = warp; it < n_items && !bad; it += kWarps) {
+                const int tile = it / ks, slice = it - tile * ks;
+                const bool ok = mbar_wait_bounded(full_of(tile), full_parity(tile));
+                if (!__all_sync(0xffffffffu, ok)) {
+                    if (lane == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
+                        p.err->where = HKV_KERNEL_GEMV;
+                        p.err->a = blockIdx.x;
+                        p.err->b = tile;
+                    }
+                    bad = true;
+                    break;
+                }
+                const unsigned char *stage = ring + (tile % n_stages) * stage_bytes;
+                const int r_lo = tile * kTileRows + g;  // CTA rows r_lo and r_lo + 8
+                const bool v_lo = r_lo < nrows, v_hi = r_lo + 8 < nrows;
+                const int sb0 = nsb * slice / ks, sb1 = nsb * (slice + 1) / ks;
+                float acc[kMats][4];
 #pragma unroll
-                for (int e = 0; e < NB; ++e) {
-                    if (e >= p.n) continue;
-                    if (MODE == kPlain) {
-                        const size_t o = static_cast<size_t>(e) * p.rows + grow;
-                        p.y[0][o] = p.residual != nullptr ? p.residual[o] + t[0][e] : t[0][e];
-                    } else if (MODE == kSwiglu) {
-                        const float g = t[0][e];
-                        const float sl = g / (1.0f + expf(-g));
-                        p.y[0][static_cast<size_t>(e) * p.rows + grow] = sl * t[kMats - 1][e];
-                    } else {
-                        res[e * kQkvRows + r] = t[0][e];
+                for (int k = 0; k < kMats; ++k)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[k][i] = 0.0f;
+                for (int sb = sb0; sb < sb1; ++sb) {
+                    const unsigned char *blk[kMats];
+                    BlockScales sl[kMats], sh[kMats];
+                    uint32_t dl[kMats], dh[kMats];  // f16 bits: d | dmin << 16
+                    int isum[kMats][4], ma[kMats][4], mb[kMats][4];
+#pragma unroll
+                    for (int k = 0; k < kMats; ++k) {
+                        blk[k] = stage + static_cast<size_t>(k * kTileRows + g) * row_bytes +
+                                 static_cast<size_t>(sb) * kQ4Bytes;
+                        const uint4 hl = v_lo ? *reinterpret_cast<const uint4 *>(blk[k]) : make_uint4(0, 0, 0, 0);
+                        const uint4 hh = v_hi ? *reinterpret_cast<const uint4 *>(blk[k] + 8 * row_bytes)
+                                              : make_uint4(0, 0, 0, 0);
+                        sl[k] = block_scales(hl.y, hl.z, hl.w);
+                        sh[k] = block_scales(hh.y, hh.z, hh.w);
+                        dl[k] = hl.x;
+                        dh[k] = hh.x;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) isum[k][i] = ma[k][i] = mb[k][i] = 0;
+                    }
+#pragma unroll
+                    for (int pp = 0; pp < 4; ++pp) {
+                        const uint4 bq = *reinterpret_cast<const uint4 *>(
+                            a.q + (static_cast<size_t>(sb * 4 + pp) * NB + g) * 64 + tq * 16);
+#pragma unroll
+                        for (int k = 0; k < kMats; ++k) {
+                            const unsigned char *q = blk[k] + 16 + 32 * pp + 8 * tq;
+                            const uint2 wl = v_lo ? *reinterpret_cast<const uint2 *>(q) : make_uint2(0, 0);
+                            const uint2 wh = v_hi ? *reinterpret_cast<const uint2 *>(q + 8 * row_bytes)
+                                                  : make_uint2(0, 0);
+                            int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+                            mma_u8s8(c0, wl.x & kLo, wh.x & kLo, wl.y & kLo, wh.y & kLo, bq.x, bq.y);
+                            mma_u8s8(c1, (wl.x >> 4) & kLo, (wh.x >> 4) & kLo, (wl.y >> 4) & kLo, (wh.y >> 4) & kLo,
+                                     bq.z, bq.w);
+                            const uint32_t m0l = sub_min4(sl[k], 2 * pp), m0h = sub_min4(sh[k], 2 * pp);
+                            const uint32_t m1l = sub_min4(sl[k], 2 * pp + 1), m1h = sub_min4(sh[k], 2 * pp + 1);
+                            mma_u8s8(ma[k], m0l, m0h, m0l, m0h, bq.x, bq.y);
+                            mma_u8s8(mb[k], m1l, m1h, m1l, m1h, bq.z, bq.w);
+                            const int s0l = sub_scale(sl[k], 2 * pp), s1l = sub_scale(sl[k], 2 * pp + 1);
+                            const int s0h = sub_scale(sh[k], 2 * pp), s1h = sub_scale(sh[k], 2 * pp + 1);
+                            isum[k][0] += s0l * c0[0] + s1l * c1[0];
+                            isum[k][1] += s0l * c0[1] + s1l * c1[1];
+                            isum[k][2] += s0h * c0[2] + s1h * c1[2];
+                            isum[k][3] += s0h * c0[3] + s1h * c1[3];
+                        }
+                    }
+                    const float d8[2] = {a.d[(2 * tq) * nsb + sb], a.d[(2 * tq + 1) * nsb + sb]};
+#pragma unroll
+                    for (int k = 0; k < kMats; ++k) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t dd = i < 2 ? dl[k] : dh[k];
+                            const float y8 = d8[i & 1];
+                            acc[k][i] += __fmul_rn(half_bits(dd), y8) * static_cast<float>(isum[k][i]) -
+                                         __fmul_rn(half_bits(dd >> 16), y8) * static_cast<float>(ma[k][i] + mb[k][i]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty0 + 8 * (tile % n_stages));  // this slice of the tile is read
+                if (ks == 1) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int r = r_lo + 8 * (i >> 1), e = 2 * tq + (i & 1);
+                        if (r < nrows && e < p.n) store_row<MODE>(p, res, row0, r, e, acc[0][i], acc[kMats - 1][i]);
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < kMats; ++k) {
+                        part4[(it * kMats + k) * 32 + lane] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+                    }
+                }
+            }
+            if (ks > 1) {
+                // tiles * ks <= kWarps: every item above was one warp's only one
+                consumer_sync();
+                for (int tile = warp; tile < tiles && !bad; tile += kWarps) {
+                    float t[kMats][4];
+#pragma unroll
+                    for (int k = 0; k < kMats; ++k) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) t[k][i] = 0.0f;
+                        for (int s2 = 0; s2 < ks; ++s2) {
+                            const float4 v = part4[((tile * ks + s2) * kMats + k) * 32 + lane];
+                            t[k][0] += v.x;
+                            t[k][1] += v.y;
+                            t[k][2] += v.z;
+                            t[k][3] += v.w;
+                        }
+                    }
+                    const int r_lo = tile * kTileRows + g;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int r = r_lo + 8 * (i >> 1), e = 2 * tq + (i & 1);
+                        if (r < nrows && e < p.n) store_row<MODE>(p, res, row0, r, e, t[0][i], t[kMats - 1][i]);
                     }
                 }
             }
@@ -872,9 +1104,10 @@ __global__ void argmax_kernel(const float *logits, int32_t n_books, int32_t size
 
 // ------------------------------------------------------------- launchers
 size_t gemv_smem(int mode, int nb, int n, int cols, int ring_bytes, bool has_norm) {
-    size_t b = static_cast<size_t>(ring_bytes) + kBarBytes + q8_smem_bytes(n, cols) +
-               (has_norm ? static_cast<size_t>(cols) * 4 : 0);
-    if (mode == kQkv) b += static_cast<size_t>(nb) * kQkvRows * sizeof(float) + kClusterCtas * nb * sizeof(double) + 16;
+    const bool frag = nb > 1;
+    size_t b = static_cast<size_t>(ring_bytes) + kBarBytes + q8_smem_bytes(frag ? nb : n, cols, frag) +
+               (has_norm ? static_cast<size_t>(cols) * 4 : 0) + qkv_extra_bytes(mode, nb);
+    if (frag) b += static_cast<size_t>(kWarps) * (mode == kSwiglu ? 2 : 1) * 32 * sizeof(float4);  // partials
     return b;
 }
 
@@ -911,7 +1144,7 @@ int num_sms_of(int dev) {
 template <int MODE, int NB>
 cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     auto kern = gemv_kernel<MODE, NB>;
-    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.n_stages * p.stage_bytes, p.norm != nullptr);
+    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.ring_bytes, p.norm != nullptr);
     static std::mutex mu;
     static bool done[64] = {};
     int dev = 0;
@@ -1025,31 +1258,90 @@ void plan_rows(GemvParams &p, int mode, int dev) {
         p.n_stages = std::max(2, std::min(kMaxStages, kRingCap / (p.chunk_rows * unit)));
         p.stage_bytes = p.chunk_rows * unit;
     }
+    p.ring_bytes = p.n_stages * p.stage_bytes;
+    p.empty_count = p.chunk_rows;
     p.lanes_per_row = plan_lanes(rpc_single);
+    p.ksplit = 1;
 }
 
+// Plan of a several-vector (tensor-core) launch: one CTA per SM with
+// ceil(rows / SMs) rows (32 for q/k/v, a quarter head), stages of kTileRows
+// rows; ksplit warps share a tile's blocks when the CTA has fewer tiles than
+// warps (each slice at least 2 blocks).  All rows in flight when they fit
+// beside the activation image, else as many 16-row stages as fit (>= 2).
+// The split depends on the shape only, so a vector's results do not depend
+// on how many others share the launch.  False when not even two stages fit.
+bool plan_tiles(GemvParams &p, int mode, int dev) {
+    const int mats = mode == kSwiglu ? 2 : 1;
+    const int nsb = p.cols / kQK;
+    const int unit = nsb * kQ4Bytes * mats;
+    const int sms = num_sms_of(dev);
+    p.rows_per_cta = mode == kQkv ? kQkvRows : std::max(1, (p.rows + sms - 1) / sms);
+    const int rpc = p.rows_per_cta;
+    const int tiles = (rpc + kTileRows - 1) / kTileRows;
+    if (tiles > kMaxTiles) return false;
+    p.chunk_rows = kTileRows;
+    p.stage_bytes = kTileRows * unit;
+    p.ksplit = std::max(1, std::min(kWarps / tiles, nsb / 2));
+    p.empty_count = p.ksplit;
+    p.lanes_per_row = 1;
+    const size_t fixed = gemv_smem(mode, kMaxVec, kMaxVec, p.cols, 0, p.norm != nullptr);
+    const size_t cap = static_cast<size_t>(smem_cap_of(dev));
+    if (fixed >= cap) return false;
+    const size_t budget = cap - fixed;
+    // the last stage holds rpc - 16 (tiles - 1) rows of each matrix, the
+    // second matrix of kSwiglu at a full stage's offset
+    const int rows_last = rpc - (tiles - 1) * kTileRows;
+    const size_t all = static_cast<size_t>(tiles - 1) * p.stage_bytes +
+                       (mats == 1 ? static_cast<size_t>(rows_last) * unit : static_cast<size_t>(p.stage_bytes));
+    if (tiles <= kMaxStages && all <= budget) {
+        p.n_stages = tiles;
+        p.ring_bytes = static_cast<int32_t>(all);
+        return true;
+    }
+    p.n_stages = static_cast<int32_t>(std::min<size_t>(kMaxStages, budget / p.stage_bytes));
+    p.ring_bytes = p.n_stages * p.stage_bytes;
+    return p.n_stages >= 2;
+}
+
+// Vectors e0 .. e0 + count - 1 of p.
+GemvParams vector_slice(const GemvParams &p, int mode, int e0, int count) {
+    GemvParams q = p;
+    q.n = count;
+    q.x = p.x + static_cast<size_t>(e0) * p.cols;
+    if (q.residual) q.residual += static_cast<size_t>(e0) * p.rows;
+    for (int k = 0; k < 3; ++k) {
+        if (q.y[k]) q.y[k] += static_cast<size_t>(e0) * (mode == kQkv ? p.y_rows[k] : p.rows);
+    }
+    return q;
+}
+
+// One vector: the dp4a kernel (plan_rows), unless p.tensor.  Several (or
+// p.tensor): the tensor-core kernel, kMaxVec vectors per launch (each launch
+// reads the weights once); if its plan does not fit shared memory, one dp4a
+// launch per vector.  The two kernels sum in different orders: a caller that
+// wants a vector's result not to depend on its batch-mates fixes p.tensor.
 template <int MODE>
 cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
     int dev = 0;
     cudaError_t st = cudaGetDevice(&dev);
     if (st != cudaSuccess) return st;
-    plan_rows(p, MODE, dev);
-    // vectors per launch: at most kMaxVec, and as many as shared memory holds
-    int vmax = kMaxVec;
-    const size_t cap = static_cast<size_t>(smem_cap_of(dev));
-    const int ring_bytes = p.n_stages * p.stage_bytes;
-    while (vmax > 1 && gemv_smem(MODE, kMaxVec, vmax, p.cols, ring_bytes, p.norm != nullptr) > cap) --vmax;
-    if (gemv_smem(MODE, 1, 1, p.cols, ring_bytes, p.norm != nullptr) > cap) return cudaErrorInvalidValue;
-    const int n_total = p.n;
-    for (int e0 = 0; e0 < n_total; e0 += vmax) {
-        GemvParams q = p;
-        q.n = std::min(vmax, n_total - e0);
-        q.x = p.x + static_cast<size_t>(e0) * p.cols;
-        if (q.residual) q.residual += static_cast<size_t>(e0) * p.rows;
-        for (int k = 0; k < 3; ++k) {
-            if (q.y[k]) q.y[k] += static_cast<size_t>(e0) * (MODE == kQkv ? p.y_rows[k] : p.rows);
+    if (p.n > 1 || p.tensor != 0) {
+        GemvParams t = p;
+        if (plan_tiles(t, MODE, dev)) {
+            for (int e0 = 0; e0 < p.n; e0 += kMaxVec) {
+                st = launch_one<MODE, kMaxVec>(vector_slice(t, MODE, e0, std::min(kMaxVec, p.n - e0)), stream);
+                if (st != cudaSuccess) return st;
+            }
+            return cudaSuccess;
         }
-        st = q.n == 1 ? launch_one<MODE, 1>(q, stream) : launch_one<MODE, kMaxVec>(q, stream);
+    }
+    plan_rows(p, MODE, dev);
+    if (gemv_smem(MODE, 1, 1, p.cols, p.ring_bytes, p.norm != nullptr) > static_cast<size_t>(smem_cap_of(dev))) {
+        return cudaErrorInvalidValue;
+    }
+    for (int e0 = 0; e0 < p.n; ++e0) {
+        st = launch_one<MODE, 1>(vector_slice(p, MODE, e0, 1), stream);
         if (st != cudaSuccess) return st;
     }
     return cudaSuccess;
@@ -1171,6 +1463,7 @@ extern "C" int hkv_q4k_gemv(const hkv_q4k_gemv_args *a, hkv_stream stream, char 
     p.w[0] = static_cast<const uint8_t *>(a->w);
     p.w[1] = static_cast<const uint8_t *>(a->w_up);
     p.rows = static_cast<int32_t>(a->rows);
+    p.tensor = a->tensor_cores != 0 ? 1 : 0;
     p.row_end[0] = p.row_end[1] = p.row_end[2] = p.rows;
     p.cols = static_cast<int32_t>(a->cols);
     p.n = a->n;
@@ -1231,6 +1524,7 @@ extern "C" int hkv_q4k_qkv(const hkv_q4k_qkv_args *a, hkv_stream stream, char *e
     p.y_rows[1] = p.y_rows[2] = static_cast<int32_t>(rk);
     p.head_norm[0] = a->q_norm;
     p.head_norm[1] = a->k_norm;
+    p.tensor = a->tensor_cores != 0 ? 1 : 0;
     p.err = q4k_err_word();
     return finish(launch_gemv<kQkv>(p, static_cast<cudaStream_t>(stream)), err_msg, err_len, who);
 }
@@ -1509,6 +1803,13 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const hkv_backbone_weights &w = bb->w;
     const float eps = w.rms_eps;
+    // one kernel family for every batch size of this backbone, so a
+    // request's results do not depend on how many share its step
+    const int32_t tc = bb->max_batch > 1 ? 1 : 0;
+    auto with_tc = [tc](GemvParams q) {
+        q.tensor = tc;
+        return q;
+    };
     for (int32_t l = 0; l < bb->cfg.n_layers; ++l) {
         const hkv_backbone_layer &L = bb->layers[static_cast<size_t>(l)];
         // q, k, v with the per-head norms (:5709-5733)
@@ -1533,6 +1834,7 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
         p.head_norm[0] = L.attn_q_norm;
         p.head_norm[1] = L.attn_k_norm;
         p.err = bb->err;
+        p.tensor = tc;
         int st = bb_cuda(bb, launch_gemv<kQkv>(p, s), "hkv_backbone_decode: q/k/v");
         if (st != HKV_OK) return st;
         // RoPE + append + attention (:5734-5786)
@@ -1541,19 +1843,22 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
             return bb_fail(bb, st, "hkv_backbone_decode: layer %d: %s", l, hkv_last_error(bb->kv));
         }
         // h = h + Wo attn (:5790-5791)
-        st = bb_cuda(bb, launch_gemv<kPlain>(plain_params(L.attn_output, w.hidden, bb->q_rows, n, bb->attn,
-                                                          nullptr, eps, bb->hidden, bb->hidden, bb->err), s),
+        st = bb_cuda(bb, launch_gemv<kPlain>(with_tc(plain_params(L.attn_output, w.hidden, bb->q_rows, n, bb->attn,
+                                                                  nullptr, eps, bb->hidden, bb->hidden, bb->err)),
+                                             s),
                      "hkv_backbone_decode: o_proj");
         if (st != HKV_OK) return st;
         // g = silu(Wg m) * (Wu m), m = rms_norm(h) * ffn_norm (:5806-5822)
         GemvParams f = plain_params(L.ffn_gate, w.ffn, w.hidden, n, bb->hidden, L.ffn_norm, eps, nullptr,
                                     bb->gated, bb->err);
         f.w[1] = static_cast<const uint8_t *>(L.ffn_up);
+        f.tensor = tc;
         st = bb_cuda(bb, launch_gemv<kSwiglu>(f, s), "hkv_backbone_decode: gate/up");
         if (st != HKV_OK) return st;
         // h = h + Wd g (:5823, :5843)
-        st = bb_cuda(bb, launch_gemv<kPlain>(plain_params(L.ffn_down, w.hidden, w.ffn, n, bb->gated, nullptr,
-                                                          eps, bb->hidden, bb->hidden, bb->err), s),
+        st = bb_cuda(bb, launch_gemv<kPlain>(with_tc(plain_params(L.ffn_down, w.hidden, w.ffn, n, bb->gated,
+                                                                  nullptr, eps, bb->hidden, bb->hidden, bb->err)),
+                                             s),
                      "hkv_backbone_decode: down");
         if (st != HKV_OK) return st;
     }
@@ -1563,9 +1868,10 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
     }
     if (want_logits) {
         // logits = a.output (rms_norm(h) * output_norm) (:5858-5863), greedy codes
-        st = bb_cuda(bb, launch_gemv<kPlain>(plain_params(w.audio_output, bb->logit_rows, w.hidden, n,
-                                                          bb->hidden, w.output_norm, eps, nullptr,
-                                                          bb->logits, bb->err), s),
+        st = bb_cuda(bb, launch_gemv<kPlain>(with_tc(plain_params(w.audio_output, bb->logit_rows, w.hidden, n,
+                                                                  bb->hidden, w.output_norm, eps, nullptr,
+                                                                  bb->logits, bb->err)),
+                                             s),
                      "hkv_backbone_decode: output head");
         if (st != HKV_OK) return st;
         st = bb_cuda(bb, launch_argmax(bb->logits, w.n_codebooks, w.codebook_size, n, bb->codes, s),

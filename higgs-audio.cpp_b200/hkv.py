@@ -105,7 +105,7 @@ class Q4kGemvArgs(ctypes.Structure):
     _fields_ = [("w", ctypes.c_void_p), ("w_up", ctypes.c_void_p), ("rows", ctypes.c_int64),
                 ("cols", ctypes.c_int64), ("n", ctypes.c_int32), ("x", ctypes.c_void_p),
                 ("norm", ctypes.c_void_p), ("eps", ctypes.c_float), ("residual", ctypes.c_void_p),
-                ("y", ctypes.c_void_p)]
+                ("y", ctypes.c_void_p), ("tensor_cores", ctypes.c_int32)]
 
 
 class Q4kQkvArgs(ctypes.Structure):
@@ -114,7 +114,8 @@ class Q4kQkvArgs(ctypes.Structure):
                 ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32), ("cols", ctypes.c_int64),
                 ("n", ctypes.c_int32), ("x", ctypes.c_void_p), ("norm", ctypes.c_void_p),
                 ("eps", ctypes.c_float), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
-                ("q_out", ctypes.c_void_p), ("k_out", ctypes.c_void_p), ("v_out", ctypes.c_void_p)]
+                ("q_out", ctypes.c_void_p), ("k_out", ctypes.c_void_p), ("v_out", ctypes.c_void_p),
+                ("tensor_cores", ctypes.c_int32)]
 
 
 class BackboneLayer(ctypes.Structure):
@@ -529,22 +530,24 @@ def q4k_quantize(w, rows: int, cols: int, blocks, stream=None, lib=None) -> None
 
 
 def q4k_gemv(w, rows: int, cols: int, x, y, n: int = 1, norm=None, eps: float = 1e-6,
-             residual=None, w_up=None, stream=None, lib=None) -> None:
-    """hkv_q4k_gemv: y = [residual +] W x' or silu(W x') * (W_up x')."""
+             residual=None, w_up=None, stream=None, lib=None, tensor_cores: bool = False) -> None:
+    """hkv_q4k_gemv: y = [residual +] W x' or silu(W x') * (W_up x');
+    tensor_cores: the tensor-core kernel even for n == 1."""
     lib = lib or load_library()
     a = Q4kGemvArgs(_ptr(w), _ptr(w_up), rows, cols, n, _ptr(x), _ptr(norm), eps, _ptr(residual),
-                    _ptr(y))
+                    _ptr(y), 1 if tensor_cores else 0)
     msg = ctypes.create_string_buffer(512)
     _raise_msg(lib.hkv_q4k_gemv(ctypes.byref(a), _stream(stream), msg, len(msg)), msg)
 
 
 def q4k_qkv(wq, wk, wv, cols: int, x, q_norm, k_norm, q_out, k_out, v_out, n: int = 1,
             norm=None, eps: float = 1e-6, n_head: int = 32, n_head_kv: int = 8, stream=None,
-            lib=None) -> None:
+            lib=None, tensor_cores: bool = False) -> None:
     """hkv_q4k_qkv: q/k/v projections with the per-head norms of q and k."""
     lib = lib or load_library()
     a = Q4kQkvArgs(_ptr(wq), _ptr(wk), _ptr(wv), n_head, n_head_kv, cols, n, _ptr(x), _ptr(norm),
-                   eps, _ptr(q_norm), _ptr(k_norm), _ptr(q_out), _ptr(k_out), _ptr(v_out))
+                   eps, _ptr(q_norm), _ptr(k_norm), _ptr(q_out), _ptr(k_out), _ptr(v_out),
+                   1 if tensor_cores else 0)
     msg = ctypes.create_string_buffer(512)
     _raise_msg(lib.hkv_q4k_qkv(ctypes.byref(a), _stream(stream), msg, len(msg)), msg)
 

@@ -45,7 +45,7 @@
 extern "C" {
 #endif
 
-#define HKV_ABI_VERSION 2  /* 2: hkv_pool_stats.kernel_launches */
+#define HKV_ABI_VERSION 3  /* 2: hkv_pool_stats.kernel_launches; 3: tensor_cores in the q4k args */
 
 typedef enum hkv_status {
     HKV_OK = 0,
@@ -345,6 +345,11 @@ typedef struct hkv_q4k_gemv_args {
     float eps;
     const float *residual;  /* NULL or [n][rows]; may equal y (in place)         */
     float *y;               /* [n][rows]                                        */
+    int32_t tensor_cores;   /* 0: n == 1 on the CUDA cores (dp4a), n > 1 on the
+                               tensor cores; 1: tensor cores for every n.  The
+                               two sum in different orders (both within 1e-5
+                               of GGML's); a backbone created with max_batch
+                               > 1 uses 1 throughout                           */
 } hkv_q4k_gemv_args;
 int hkv_q4k_gemv(const hkv_q4k_gemv_args *args, hkv_stream stream, char *err_msg,
                  size_t err_len);
@@ -364,6 +369,7 @@ typedef struct hkv_q4k_qkv_args {
     const float *k_norm;        /* [128]                                         */
     float *q_out;               /* [n][n_head*128]                               */
     float *k_out, *v_out;       /* [n][n_head_kv*128]                            */
+    int32_t tensor_cores;       /* as in hkv_q4k_gemv_args                       */
 } hkv_q4k_qkv_args;
 int hkv_q4k_qkv(const hkv_q4k_qkv_args *args, hkv_stream stream, char *err_msg, size_t err_len);
 

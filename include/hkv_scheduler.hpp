@@ -75,6 +75,14 @@ class StepScheduler {
   public:
     static constexpr int kCodebooks = 8;
     using Frame = std::array<int32_t, kCodebooks>;
+    // Host time of step() since the last reset_times(): `wait_us` blocked in
+    // the stream synchronisations (the GPU still running the step),
+    // `host_us` everything else (planning, launch calls, retirement).
+    struct StepTimes {
+        int64_t steps = 0;
+        double host_us = 0.0;
+        double wait_us = 0.0;
+    };
 
     StepScheduler(PagedKvRuntime &rt, hkv_backbone *bb, int32_t max_batch, hkv_stream stream)
         : rt_(rt), bb_(bb), max_batch_(max_batch), stream_(stream) {
@@ -104,6 +112,8 @@ class StepScheduler {
 
     // One scheduling step; returns the number of requests still queued or live.
     size_t step() {
+        const auto t0 = std::chrono::steady_clock::now();
+        const double wait0 = times_.wait_us;
         expire();
         admit();
         std::vector<Live *> prompt, gen;
@@ -120,6 +130,9 @@ class StepScheduler {
                 ++it;
             }
         }
+        const double us = std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+        times_.host_us += us - (times_.wait_us - wait0);
+        ++times_.steps;
         return queue_.size() + live_.size();
     }
 
@@ -147,6 +160,8 @@ class StepScheduler {
         auto l = live_.find(id);
         return l != live_.end() ? l->second->refreshes : 0;
     }
+    const StepTimes &times() const { return times_; }
+    void reset_times() { times_ = StepTimes{}; }
     size_t live() const { return live_.size(); }
     size_t queued() const { return queue_.size(); }
     // Prompt steps whose batch held requests at their last prompt token beside
@@ -242,8 +257,7 @@ class StepScheduler {
         check(nullptr, cudaMemcpyAsync(host_codes_, dev_codes_out_, bytes, cudaMemcpyDeviceToHost,
                                        static_cast<cudaStream_t>(stream_)) == cudaSuccess ? HKV_OK : HKV_ERR_CUDA,
               "StepScheduler: read codes");
-        check(nullptr, cudaStreamSynchronize(static_cast<cudaStream_t>(stream_)) == cudaSuccess ? HKV_OK : HKV_ERR_CUDA,
-              "StepScheduler: synchronise");
+        synchronise("StepScheduler: synchronise");
         check_backbone(hkv_backbone_sync_check(bb_, stream_), "StepScheduler: device check");
         for (size_t e = 0; e < batch.size(); ++e) batch[e]->last = host_codes_[e];
     }
@@ -347,9 +361,9 @@ class StepScheduler {
             host_logits_.resize(ready.size() * kCodebooks * 1026);
             cudaStream_t st = static_cast<cudaStream_t>(stream_);
             check(nullptr, cudaMemcpyAsync(host_logits_.data(), dev_logits_, host_logits_.size() * sizeof(float),
-                                           cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-                                   cudaStreamSynchronize(st) == cudaSuccess ? HKV_OK : HKV_ERR_CUDA,
+                                           cudaMemcpyDeviceToHost, st) == cudaSuccess ? HKV_OK : HKV_ERR_CUDA,
                   "StepScheduler: read logits");
+            synchronise("StepScheduler: synchronise logits");
             std::vector<Live *> low;
             for (size_t e = 0; e < ready.size(); ++e) {
                 Live *l = ready[e];
@@ -361,6 +375,13 @@ class StepScheduler {
             for (Live *l : low) refresh(l);
         }
         for (Live *l : ready) l->frames.push_back(l->last);
+    }
+
+    void synchronise(const char *what) {
+        const auto t0 = std::chrono::steady_clock::now();
+        const bool ok = cudaStreamSynchronize(static_cast<cudaStream_t>(stream_)) == cudaSuccess;
+        times_.wait_us += std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+        check(nullptr, ok ? HKV_OK : HKV_ERR_CUDA, what);
     }
 
     void check_backbone(int status, const char *what) {
@@ -380,6 +401,7 @@ class StepScheduler {
     std::vector<float> host_logits_;
     int64_t next_id_ = 0;
     int64_t mixed_prompt_steps_ = 0;
+    StepTimes times_;
     std::deque<std::pair<int64_t, GenerateRequest>> queue_;
     LiveMap live_;
     std::map<int64_t, Ended> done_;

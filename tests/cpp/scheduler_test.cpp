@@ -22,6 +22,7 @@
 #include <map>
 #include <vector>
 
+#include "backbone_fixture.hpp"
 #include "hkv_scheduler.hpp"
 
 #define EXPECT(c)                                                                \
@@ -34,42 +35,9 @@
 
 namespace {
 
-uint64_t g_rng = 0x9E3779B97F4A7C15ull;
-float next_normal() {  // sum of four uniforms, unit variance (test data only)
-    float s = 0.f;
-    for (int i = 0; i < 4; ++i) {
-        g_rng = g_rng * 6364136223846793005ull + 1442695040888963407ull;
-        s += static_cast<float>((g_rng >> 40) & 0xFFFFFF) / 16777216.0f - 0.5f;
-    }
-    return s * 1.7320508f;
-}
-
-std::vector<void *> g_allocs;
-void *dmalloc(size_t bytes) {
-    void *p = nullptr;
-    if (cudaMalloc(&p, bytes) != cudaSuccess) throw std::runtime_error("cudaMalloc");
-    g_allocs.push_back(p);
-    return p;
-}
-
-const void *q4k(int64_t rows, int64_t cols) {
-    std::vector<float> h(static_cast<size_t>(rows * cols));
-    for (float &x : h) x = 0.02f * next_normal();
-    float *f = static_cast<float *>(dmalloc(h.size() * 4));
-    cudaMemcpy(f, h.data(), h.size() * 4, cudaMemcpyHostToDevice);
-    void *b = dmalloc(static_cast<size_t>(rows * cols / 256 * 144));
-    char msg[256];
-    if (hkv_q4k_quantize(f, rows, cols, b, nullptr, msg, sizeof msg) != HKV_OK) throw std::runtime_error(msg);
-    return b;
-}
-
-const float *norm(int64_t n) {
-    std::vector<float> h(static_cast<size_t>(n));
-    for (float &x : h) x = 1.0f + 0.1f * next_normal();
-    float *d = static_cast<float *>(dmalloc(h.size() * 4));
-    cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice);
-    return d;
-}
+using fixture::dmalloc;
+using fixture::norm;
+using fixture::q4k;
 
 using Sched = hkv_pipeline::StepScheduler;
 using Frames = std::vector<Sched::Frame>;
@@ -245,7 +213,7 @@ int main() {
             if (r != 0) EXPECT(br.caches.at(r) == batched.caches.at(r));
         }
     }
-    for (void *p : g_allocs) cudaFree(p);
+    fixture::free_all();
     std::printf("scheduler ok\n");
     return 0;
 }

@@ -34,7 +34,7 @@ def test_exports_every_declared_symbol(hkv_lib):
     for name in declared:
         assert hasattr(hkv_lib, name), name
     assert declared == set(hkv.SIGNATURES), declared ^ set(hkv.SIGNATURES)
-    assert hkv_lib.hkv_abi_version() == 2
+    assert hkv_lib.hkv_abi_version() == 3
 
 
 def test_config_default_is_the_backbone_shape(hkv_lib):

@@ -56,21 +56,25 @@ def test_encoder_round_trip(hkv_lib, oracle):
     assert np.sqrt(np.mean((dec - wn) ** 2)) < 0.12 * np.sqrt(np.mean(wn ** 2))
 
 
-@pytest.mark.parametrize("rows,cols,n,use_norm,use_res", [
-    (2560, 4096, 1, False, True),    # o_proj + residual (a warp per row)
-    (2560, 9728, 1, False, True),    # ffn_down + residual
-    (8208, 2560, 1, True, False),    # output head after output_norm
-    (4096, 2560, 3, True, False),    # several vectors (8-vector kernel)
-    (300, 2560, 9, False, True),     # rows not a multiple of 32, n > 8 (two launches)
+@pytest.mark.parametrize("rows,cols,n,use_norm,use_res,tc", [
+    (2560, 4096, 1, False, True, False),    # o_proj + residual (a warp per row)
+    (2560, 9728, 1, False, True, False),    # ffn_down + residual
+    (8208, 2560, 1, True, False, False),    # output head after output_norm
+    (4096, 2560, 3, True, False, False),    # several vectors: tensor cores
+    (300, 2560, 9, False, True, False),     # rows not a multiple of 16, n > 8 (two launches)
+    (2560, 4096, 1, False, True, True),     # o_proj, one vector on the tensor cores
+    (2560, 9728, 1, False, True, True),     # ffn_down (rows in flight beside a 9728-wide image)
+    (8208, 2560, 16, True, False, False),   # the output head at batch 16
+    (4096, 2560, 2, True, False, False),
 ])
-def test_gemv_matches_oracle(hkv_lib, oracle, rows, cols, n, use_norm, use_res):
+def test_gemv_matches_oracle(hkv_lib, oracle, rows, cols, n, use_norm, use_res, tc):
     import hkv
     _, b = q4k_matrix(hkv, rows, cols, 10 + rows + n)
     x = vec(20 + n, (n, cols))
     norm = vec(30, (cols,), 0.1, 1.0) if use_norm else None
     res = vec(40, (n, rows)) if use_res else None
     y = torch.full((n, rows), float("nan"), device=DEV)
-    hkv.q4k_gemv(b, rows, cols, x, y, n=n, norm=norm, eps=EPS, residual=res)
+    hkv.q4k_gemv(b, rows, cols, x, y, n=n, norm=norm, eps=EPS, residual=res, tensor_cores=tc)
     torch.cuda.synchronize()
     xn = x.cpu().numpy()
     if use_norm:
@@ -96,15 +100,15 @@ def test_gemv_in_place_residual(hkv_lib, oracle):
     assert rel_err(h.cpu().numpy(), ref) <= PROJ_TOL
 
 
-@pytest.mark.parametrize("n", [1, 2])
-def test_swiglu_matches_oracle(hkv_lib, oracle, n):
+@pytest.mark.parametrize("n,tc", [(1, False), (2, False), (1, True), (8, False)])
+def test_swiglu_matches_oracle(hkv_lib, oracle, n, tc):
     import hkv
     _, bg = q4k_matrix(hkv, 9728, 2560, 50)
     _, bu = q4k_matrix(hkv, 9728, 2560, 51)
     x = vec(52, (n, 2560))
     norm = vec(53, (2560,), 0.1, 1.0)
     y = torch.full((n, 9728), float("nan"), device=DEV)
-    hkv.q4k_gemv(bg, 9728, 2560, x, y, n=n, norm=norm, eps=EPS, w_up=bu)
+    hkv.q4k_gemv(bg, 9728, 2560, x, y, n=n, norm=norm, eps=EPS, w_up=bu, tensor_cores=tc)
     torch.cuda.synchronize()
     m = oracle.rms_norm_mul(x.cpu().numpy(), EPS, norm.cpu().numpy())
     ref = oracle.silu_mul(oracle.q4k_gemv(bg.cpu().numpy(), 9728, 2560, m),
@@ -112,8 +116,8 @@ def test_swiglu_matches_oracle(hkv_lib, oracle, n):
     assert rel_err(y.cpu().numpy(), ref) <= PROJ_TOL
 
 
-@pytest.mark.parametrize("n", [1, 3])
-def test_qkv_head_norm_matches_oracle(hkv_lib, oracle, n):
+@pytest.mark.parametrize("n,tc", [(1, False), (3, False), (1, True)])
+def test_qkv_head_norm_matches_oracle(hkv_lib, oracle, n, tc):
     import hkv
     _, bq = q4k_matrix(hkv, 4096, 2560, 60)
     _, bk = q4k_matrix(hkv, 1024, 2560, 61)
@@ -125,7 +129,7 @@ def test_qkv_head_norm_matches_oracle(hkv_lib, oracle, n):
     q = torch.full((n, 4096), float("nan"), device=DEV)
     k = torch.full((n, 1024), float("nan"), device=DEV)
     v = torch.full((n, 1024), float("nan"), device=DEV)
-    hkv.q4k_qkv(bq, bk, bv, 2560, x, qn, kn, q, k, v, n=n, norm=norm, eps=EPS)
+    hkv.q4k_qkv(bq, bk, bv, 2560, x, qn, kn, q, k, v, n=n, norm=norm, eps=EPS, tensor_cores=tc)
     torch.cuda.synchronize()
     xn = oracle.rms_norm_mul(x.cpu().numpy(), EPS, norm.cpu().numpy())
     rq = oracle.q4k_gemv(bq.cpu().numpy(), 4096, 2560, xn).reshape(n, 32, 128)
@@ -136,6 +140,28 @@ def test_qkv_head_norm_matches_oracle(hkv_lib, oracle, n):
     assert rel_err(q.cpu().numpy().reshape(-1, 128), rq.reshape(-1, 128)) <= PROJ_TOL
     assert rel_err(k.cpu().numpy().reshape(-1, 128), rk.reshape(-1, 128)) <= PROJ_TOL
     assert rel_err(v.cpu().numpy(), rv) <= PROJ_TOL
+
+
+@pytest.mark.parametrize("rows,cols,swiglu", [(2560, 4096, False), (9728, 2560, True),
+                                             (2560, 9728, False)])
+def test_tensor_core_results_do_not_depend_on_batch(hkv_lib, rows, cols, swiglu):
+    """On the tensor cores a vector's result is the same bits alone (n = 1)
+    or among 4 or 11 others (one and two launches): the tiles, block slices
+    and summation order depend on the matrix shape only."""
+    import hkv
+    _, b = q4k_matrix(hkv, rows, cols, 70 + rows)
+    bu = q4k_matrix(hkv, rows, cols, 71 + rows)[1] if swiglu else None
+    norm = vec(72, (cols,), 0.1, 1.0) if swiglu else None
+    x = vec(73, (12, cols))
+    outs = {}
+    for n in (1, 5, 12):
+        y = torch.empty((n, rows), device=DEV)
+        hkv.q4k_gemv(b, rows, cols, x[:n], y, n=n, norm=norm, eps=EPS, w_up=bu, tensor_cores=True)
+        outs[n] = y
+    torch.cuda.synchronize()
+    assert torch.equal(outs[1][0], outs[5][0]) and torch.equal(outs[1][0], outs[12][0])
+    assert torch.equal(outs[5], outs[12][:5])
+    hkv.q4k_sync_check()
 
 
 def test_gemv_rejects_bad_shapes(hkv_lib):
@@ -196,8 +222,9 @@ class SerialStep:
 
     ATTN_TOL = 2e-3
 
-    def __init__(self, hkv, oracle, eng, dev, host, n_layers):
+    def __init__(self, hkv, oracle, eng, dev, host, n_layers, tc):
         self.hkv, self.o, self.eng, self.dev, self.host, self.L = hkv, oracle, eng, dev, host, n_layers
+        self.tc = tc  # the projection kernels of the backbone under test
         self.cos, self.sin = oracle.rope_table()
 
     def run(self, h, slots, want_logits):
@@ -216,7 +243,7 @@ class SerialStep:
             hn = h.cpu().numpy()
             hkv.q4k_qkv(dev[p + "attn_q"], dev[p + "attn_k"], dev[p + "attn_v"], 2560, h,
                         dev[p + "attn_q_norm"], dev[p + "attn_k_norm"], q, k, v, n=n,
-                        norm=dev[p + "attn_norm"], eps=EPS)
+                        norm=dev[p + "attn_norm"], eps=EPS, tensor_cores=self.tc)
             torch.cuda.synchronize()
             xn = o.rms_norm_mul(hn, EPS, host[p + "attn_norm"])
             rq = o.rms_norm_mul(o.q4k_gemv(host[p + "attn_q"], 4096, 2560, xn).reshape(n, 32, 128),
@@ -243,20 +270,22 @@ class SerialStep:
             assert rel_err(attn.cpu().numpy(), o.decode_attn(qr, ks, vs)) <= self.ATTN_TOL
             # h += Wo attn; g = silu(Wg m) * (Wu m); h += Wd g
             an, hn = attn.cpu().numpy(), h.cpu().numpy()
-            hkv.q4k_gemv(dev[p + "attn_output"], 2560, 4096, attn, h, n=n, residual=h)
+            hkv.q4k_gemv(dev[p + "attn_output"], 2560, 4096, attn, h, n=n, residual=h,
+                         tensor_cores=self.tc)
             torch.cuda.synchronize()
             ref = hn + o.q4k_gemv(host[p + "attn_output"], 2560, 4096, an)
             assert rel_err(h.cpu().numpy(), ref) <= PROJ_TOL
             hn = h.cpu().numpy()
             hkv.q4k_gemv(dev[p + "ffn_gate"], 9728, 2560, h, g, n=n, norm=dev[p + "ffn_norm"],
-                         eps=EPS, w_up=dev[p + "ffn_up"])
+                         eps=EPS, w_up=dev[p + "ffn_up"], tensor_cores=self.tc)
             torch.cuda.synchronize()
             m = o.rms_norm_mul(hn, EPS, host[p + "ffn_norm"])
             ref = o.silu_mul(o.q4k_gemv(host[p + "ffn_gate"], 9728, 2560, m),
                              o.q4k_gemv(host[p + "ffn_up"], 9728, 2560, m))
             assert rel_err(g.cpu().numpy(), ref) <= PROJ_TOL
             gn = g.cpu().numpy()
-            hkv.q4k_gemv(dev[p + "ffn_down"], 2560, 9728, g, h, n=n, residual=h)
+            hkv.q4k_gemv(dev[p + "ffn_down"], 2560, 9728, g, h, n=n, residual=h,
+                         tensor_cores=self.tc)
             torch.cuda.synchronize()
             ref = hn + o.q4k_gemv(host[p + "ffn_down"], 2560, 9728, gn)
             assert rel_err(h.cpu().numpy(), ref) <= PROJ_TOL
@@ -265,7 +294,7 @@ class SerialStep:
         if want_logits:
             logits = torch.empty((n, 8 * 1026), device=DEV)
             hkv.q4k_gemv(dev["a.output"], 8 * 1026, 2560, h, logits, n=n, norm=dev["output_norm"],
-                         eps=EPS)
+                         eps=EPS, tensor_cores=self.tc)
             torch.cuda.synchronize()
             ref = o.q4k_gemv(host["a.output"], 8 * 1026, 2560,
                              o.rms_norm_mul(h.cpu().numpy(), EPS, host["output_norm"]))
@@ -288,7 +317,8 @@ def test_backbone_steps_match_oracle(hkv_lib, oracle):
     e_ser = hkv.Engine(n_layers=n_layers, n_pages=64, max_slots=2, device=0, shuffle_seed=4,
                        lib=hkv_lib)
     bb = hkv.Backbone(e_bb, dev, text_vocab=vocab, rms_eps=EPS, max_batch=2)
-    ser = SerialStep(hkv, oracle, e_ser, dev, host, n_layers)
+    # max_batch 2: the backbone runs every projection on the tensor cores
+    ser = SerialStep(hkv, oracle, e_ser, dev, host, n_layers, tc=True)
     emb = oracle.BackboneOracle(host, n_layers, eps=EPS)
     stream = torch.cuda.current_stream().cuda_stream
     hidden = torch.as_tensor(hkv.DeviceArray(bb.hidden_ptr, (2, 2560)), device=DEV)
