@@ -86,6 +86,8 @@ struct GemvParams {
     int32_t lanes_per_row;    // one vector: 8 or 16 consumer lanes share a row's dot product
     int32_t ksplit;           // several vectors: warps sharing one tile's blocks
     int32_t tensor;           // 1: the tensor-core kernel even for one vector
+    int32_t grid_ctas;        // several vectors: CTAs (a multiple of share_ctas)
+    int32_t share_ctas;       // several vectors: CTAs of a cluster sharing the activation image
     DeviceError *err;         // bounded-wait timeouts are recorded here
 };
 
@@ -164,7 +166,8 @@ struct Q8View {
     int8_t *q;   // rows: [n][cols]; fragments: [cols / 64][NB][64]
     float *d;    // [n][nsb]
     int32_t *s;  // rows only: [n][nsb * 8]
-    double *red; // [kWarps + 1] reduction scratch
+    double *red; // rows: [kWarps + 1] reduction scratch; fragments: [n * nsb]
+                 // per-block sums of squares, then [n] float scales
     int frag;    // 0, or NB of the fragment layout
 };
 
@@ -176,7 +179,9 @@ __host__ __device__ inline size_t q8_smem_bytes(int n, int cols, bool frag) {
     b = (b + 15) & ~size_t(15);
     if (!frag) b += static_cast<size_t>(n) * nsb * 8 * 4;  // s
     b = (b + 15) & ~size_t(15);
-    b += (kWarps + 1) * sizeof(double);                // red
+    // red: kWarps + 1 doubles; fragments: per-block sums of squares and scales
+    b += frag ? static_cast<size_t>(n) * nsb * sizeof(double) + static_cast<size_t>(n) * sizeof(float)
+              : (kWarps + 1) * sizeof(double);
     b = (b + 15) & ~size_t(15);
     return b;
 }
@@ -221,9 +226,9 @@ __device__ __forceinline__ void consumer_sync() {
 // Q8_K quantisation of one 256-element block held 8 per lane across a warp
 // (GGML's quantize_row_q8_K: iscale = -127 / (element of largest magnitude,
 // the first on ties), q = min(127, round-half-even(iscale * x)),
-// d = 1 / iscale), written to the shared-memory image.
-__device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View &a, int cols, int nsb,
-                                               int e, int b, int lane) {
+// d = 1 / iscale): the lane's 8 bytes (lo, hi), d and the lane's sum of q.
+__device__ __forceinline__ void q8_pack(const float (&v)[8], int lane, uint32_t &lo, uint32_t &hi, float &d,
+                                        int &qsum) {
     float am = 0.0f, mx = 0.0f;
     int idx = 0x7fffffff;
 #pragma unroll
@@ -247,7 +252,7 @@ __device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View
         }
     }
     int q[8];
-    float d = 0.0f;
+    d = 0.0f;
     if (am == 0.0f) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) q[i] = 0;
@@ -257,17 +262,25 @@ __device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View
         for (int i = 0; i < 8; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, v[i])));
         d = 1.0f / iscale;
     }
-    uint32_t lo = 0, hi = 0;
+    lo = hi = 0;
+    qsum = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         lo |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
         hi |= (static_cast<uint32_t>(q[i + 4]) & 0xFFu) << (8 * i);
+        qsum += q[i] + q[i + 4];
     }
+}
+
+// The same, written to the shared-memory image.
+__device__ __forceinline__ void quantize_block(const float (&v)[8], const Q8View &a, int cols, int nsb,
+                                               int e, int b, int lane) {
+    uint32_t lo, hi;
+    float d;
+    int qs;
+    q8_pack(v, lane, lo, hi, d, qs);
     *reinterpret_cast<uint2 *>(q8_store_at(a, cols, e, b, lane)) = make_uint2(lo, hi);
     if (a.frag == 0) {
-        int qs = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) qs += q[i];
         qs += __shfl_xor_sync(0xffffffffu, qs, 1);
         qs += __shfl_xor_sync(0xffffffffu, qs, 2);
         if ((lane & 3) == 0) a.s[(e * nsb + b) * 8 + (lane >> 2)] = qs;
@@ -457,6 +470,122 @@ __device__ bool quantize_activations(const GemvParams &p, const float *x0, int n
     return true;
 }
 
+// Every thread of every CTA of the cluster (the producer warp included).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The fragment-order Q8_K image of n_vec vectors (a.frag != 0), shared by
+// the kClusterCtas CTAs of a cluster: CTA rank r quantises blocks
+// [nsb r / C, nsb (r + 1) / C) of every vector and stores them into the
+// image of every CTA of the cluster (distributed shared memory), so each CTA
+// reads 1 / C of the activations.  Item it = (vector, block of the share),
+// warp w taking items w, w + kWarps, ... with kQuantBatch blocks of loads
+// in flight.  With a norm, a first pass stores each block's sum of squares
+// (double, 256 products rounded to float as GGML forms them) into every
+// CTA, and after a cluster barrier thread e < n_vec adds vector e's in
+// block order -- the same scale in every CTA, not depending on the other
+// vectors; a second pass reloads, scales (x * scale) * norm and quantises.
+// ssp: [n_vec * nsb] doubles then [n_vec] floats.  The caller has passed a
+// cluster barrier after every CTA started; this takes one more with a norm
+// and ends with one after the image is complete (the producer warp takes the
+// same barriers).
+constexpr int kQuantBatch = 8;
+
+__device__ bool quantize_activations_frag(const GemvParams &p, const float *x0, int n_vec, const Q8View &a,
+                                          double *ssp, const float *normbuf, uint32_t normbar) {
+    cg::cluster_group cl = cg::this_cluster();
+    const unsigned csize = cl.num_blocks(), rank = cl.block_rank();
+    const int nsb = p.cols / kQK;
+    const int b0 = static_cast<int>(nsb * rank / csize), nb = static_cast<int>(nsb * (rank + 1) / csize) - b0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int items = n_vec * nb;
+    float *scale_s = reinterpret_cast<float *>(ssp + n_vec * nsb);
+    bool norm_ok = true;
+    auto load = [&](int it, float (&v)[8]) {
+        const int e = it / nb, b = b0 + it - e * nb;
+        const float *x = x0 + static_cast<size_t>(e) * p.cols + b * kQK + lane * 8;
+        const float4 u0 = *reinterpret_cast<const float4 *>(x);
+        const float4 u1 = *reinterpret_cast<const float4 *>(x + 4);
+        v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+        v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+    };
+    // one batch of blocks per warp: the values stay in registers across the
+    // norm's barrier; otherwise the second pass loads them again
+    const bool one_batch = items <= kWarps * kQuantBatch;
+    float v[kQuantBatch][8];
+    auto load_batch = [&](int base) {
+#pragma unroll
+        for (int u = 0; u < kQuantBatch; ++u) {
+            if (base + kWarps * u < items) load(base + kWarps * u, v[u]);
+        }
+    };
+    if (p.norm != nullptr) {
+        for (int base = warp; base < items; base += kWarps * kQuantBatch) {
+            load_batch(base);
+#pragma unroll
+            for (int u = 0; u < kQuantBatch; ++u) {
+                const int it = base + kWarps * u;
+                if (it >= items) continue;
+                double ss = 0.0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) ss += static_cast<double>(__fmul_rn(v[u][i], v[u][i]));
+                ss = warp_sum_double(ss);
+                const int e = it / nb, b = b0 + it - e * nb;
+                if (lane < static_cast<int>(csize)) *cl.map_shared_rank(ssp + e * nsb + b, lane) = ss;
+            }
+        }
+        cluster_sync_all();
+        if (threadIdx.x < n_vec) {
+            double t = 0.0;
+            for (int b = 0; b < nsb; ++b) t += ssp[threadIdx.x * nsb + b];
+            const float mean = static_cast<float>(t / static_cast<double>(p.cols));
+            scale_s[threadIdx.x] = 1.0f / sqrtf(mean + p.eps);
+        }
+        // the norm weights were copied into shared memory before the kernel
+        // waited for its predecessor; a warp that gave up still takes every
+        // barrier below
+        norm_ok = __all_sync(0xffffffffu, mbar_wait_bounded(normbar, 0));
+        consumer_sync();
+    }
+    for (int base = warp; base < items; base += kWarps * kQuantBatch) {
+        if (p.norm == nullptr || !one_batch) load_batch(base);
+#pragma unroll
+        for (int u = 0; u < kQuantBatch; ++u) {
+            const int it = base + kWarps * u;
+            if (it >= items) continue;
+            const int e = it / nb, b = b0 + it - e * nb;
+            float w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = v[u][i];
+            if (p.norm != nullptr && norm_ok) {
+                const float scale = scale_s[e];
+                const float4 w0 = *reinterpret_cast<const float4 *>(normbuf + b * kQK + lane * 8);
+                const float4 w1 = *reinterpret_cast<const float4 *>(normbuf + b * kQK + lane * 8 + 4);
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) w[i] = __fmul_rn(__fmul_rn(w[i], scale), wv[i]);
+            }
+            uint32_t lo, hi;
+            float d;
+            int qs;
+            q8_pack(w, lane, lo, hi, d, qs);
+            // lanes l and l + 4 (l & 4 == 0) hold the two halves of one
+            // 16-byte chunk of the image: one 16-byte store per chunk
+            const uint32_t lo2 = __shfl_down_sync(0xffffffffu, lo, 4);
+            const uint32_t hi2 = __shfl_down_sync(0xffffffffu, hi, 4);
+            uint4 *dst = reinterpret_cast<uint4 *>(q8_store_at(a, p.cols, e, b, lane));
+            float *dd = a.d + e * nsb + b;
+            for (unsigned r = 0; r < csize; ++r) {
+                if ((lane & 4) == 0) *cl.map_shared_rank(dst, r) = make_uint4(lo, hi, lo2, hi2);
+                if (lane == 0) *cl.map_shared_rank(dd, r) = d;
+            }
+        }
+    }
+    cluster_sync_all();
+    return norm_ok;
+}
+
 // Scales and mins of sub-blocks 2*part and 2*part+1 from the packed words
 // (bytes 4..15 of a block), branch-free: words of the 6-bit values of
 // sub-blocks 0-3 and 4-7, then the two bytes of this pair.
@@ -535,6 +664,15 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The same with C = 0.
+__device__ __forceinline__ void mma_u8s8_zero(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
 // Packed 6-bit scales (sc) and mins (mn) of sub-blocks 0-3 (lo) and 4-7
 // (hi), one byte each, from bytes 4..15 of a Q4_K block.
 struct BlockScales {
@@ -553,7 +691,7 @@ __device__ __forceinline__ BlockScales block_scales(uint32_t s0, uint32_t s1, ui
 // Scale of sub-block sb (0..7; a constant after unrolling), and its min
 // copied into all 4 bytes of a word.
 __device__ __forceinline__ int sub_scale(const BlockScales &s, int sb) {
-    return static_cast<int>(((sb < 4 ? s.sc_lo : s.sc_hi) >> (8 * (sb & 3))) & 0xFFu);
+    return static_cast<int>(__byte_perm(sb < 4 ? s.sc_lo : s.sc_hi, 0u, 0x4440u | static_cast<uint32_t>(sb & 3)));
 }
 __device__ __forceinline__ uint32_t sub_min4(const BlockScales &s, int sb) {
     const uint32_t b = static_cast<uint32_t>(sb & 3);
@@ -641,8 +779,31 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
     bool bad = false;
 
     if (producer) {
+        const uint64_t policy = evict_first_policy();
+        const uint8_t *wbase[kMats];
+#pragma unroll
+        for (int k = 0; k < kMats; ++k) {
+            wbase[k] = p.w[MODE == kSwiglu ? k : m] + static_cast<size_t>(mrow0) * row_bytes;
+        }
+        int issued = 0;
+        // chunk c into its stage (lane 0)
+        auto issue = [&](int c) {
+            const int r0 = c * R;
+            const int rows_c = min(R, nrows - r0);
+            const uint32_t bytes = static_cast<uint32_t>(rows_c * row_bytes);
+            const uint32_t stage = smem_u32(ring + (c % n_stages) * stage_bytes);
+            const uint32_t bar = full_of(c);
+            mbar_arrive_expect_tx(bar, bytes * kMats);
+#pragma unroll
+            for (int k = 0; k < kMats; ++k) {
+                // several vectors: a stage holds each matrix's rows of the
+                // chunk back to back (the ring holds exactly the CTA's rows)
+                bulk_load(stage + k * (NB > 1 ? rows_c : R) * row_bytes,
+                          wbase[k] + static_cast<size_t>(r0) * row_bytes, bytes, bar, policy);
+            }
+            issued = c + 1;
+        };
         if (lane == 0) {
-            const uint64_t policy = evict_first_policy();
             if (p.norm != nullptr) {  // the RMSNorm weights, before any weight stage
                 const uint32_t bytes = static_cast<uint32_t>(p.cols) * 4u;
                 mbar_arrive_expect_tx(normbar, bytes);
@@ -652,36 +813,29 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
                     "l"(p.norm), "r"(bytes), "r"(normbar)
                     : "memory");
             }
-            const uint8_t *wbase[kMats];
-#pragma unroll
-            for (int k = 0; k < kMats; ++k) {
-                wbase[k] = p.w[MODE == kSwiglu ? k : m] + static_cast<size_t>(mrow0) * row_bytes;
-            }
-            int issued = 0;
-            for (int c = 0; c < n_chunks; ++c) {
-                if (c >= n_stages) {  // wait until every row of chunk c - n_stages is done
-                    const int prev = c - n_stages;
-                    if (!mbar_wait_bounded(empty0 + 8 * (prev % n_stages),
-                                           static_cast<uint32_t>((prev / n_stages) & 1))) {
-                        if (p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
-                            p.err->where = HKV_KERNEL_GEMV;
-                            p.err->a = blockIdx.x;
-                            p.err->b = c;
-                        }
-                        break;
+            for (int c = 0; c < min(n_chunks, n_stages); ++c) issue(c);  // stages still free
+        }
+        if constexpr (NB > 1) {
+            // the cluster barriers of the consumers' activation prologue:
+            // started, sums of squares (with a norm), image complete
+            __syncwarp();
+            cluster_sync_all();
+            if (p.norm != nullptr) cluster_sync_all();
+            cluster_sync_all();
+        }
+        if (lane == 0) {
+            for (int c = n_stages; c < n_chunks; ++c) {
+                // wait until every row of chunk c - n_stages is done
+                const int prev = c - n_stages;
+                if (!mbar_wait_bounded(empty0 + 8 * (prev % n_stages), static_cast<uint32_t>((prev / n_stages) & 1))) {
+                    if (p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
+                        p.err->where = HKV_KERNEL_GEMV;
+                        p.err->a = blockIdx.x;
+                        p.err->b = c;
                     }
+                    break;
                 }
-                const int r0 = c * R;
-                const uint32_t bytes = static_cast<uint32_t>(min(R, nrows - r0) * row_bytes);
-                const uint32_t stage = smem_u32(ring + (c % n_stages) * stage_bytes);
-                const uint32_t bar = full_of(c);
-                mbar_arrive_expect_tx(bar, bytes * kMats);
-#pragma unroll
-                for (int k = 0; k < kMats; ++k) {
-                    bulk_load(stage + k * R * row_bytes, wbase[k] + static_cast<size_t>(r0) * row_bytes,
-                              bytes, bar, policy);
-                }
-                issued = c + 1;
+                issue(c);
             }
             // the CTA must not exit with copies in flight: wait (bounded) for
             // the last copy issued into each stage
@@ -691,8 +845,14 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
             if (p.norm != nullptr) mbar_wait_bounded(normbar, 0);
         }
     } else {
+        if constexpr (NB > 1) cluster_sync_all();  // every CTA of the cluster has started
         pdl_wait();  // x (and y, residual) belong to the kernels before
-        const bool qok = quantize_activations(p, p.x, p.n, a, a.red, normbuf, normbar);
+        bool qok;
+        if constexpr (NB > 1) {
+            qok = quantize_activations_frag(p, p.x, p.n, a, a.red, normbuf, normbar);
+        } else {
+            qok = quantize_activations(p, p.x, p.n, a, a.red, normbuf, normbar);
+        }
         if (!qok) {
             if (tid == 0 && p.err != nullptr && atomicCAS(&p.err->code, 0, kErrTimeout) == 0) {
                 p.err->where = HKV_KERNEL_GEMV;
@@ -803,70 +963,95 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
                     break;
                 }
                 const unsigned char *stage = ring + (tile % n_stages) * stage_bytes;
+                const int rows_t = min(kTileRows, nrows - tile * kTileRows);  // >= 1
                 const int r_lo = tile * kTileRows + g;  // CTA rows r_lo and r_lo + 8
-                const bool v_lo = r_lo < nrows, v_hi = r_lo + 8 < nrows;
+                // rows past the tile read its last row; their sums are dropped
+                const int gl = min(g, rows_t - 1), gh = min(g + 8, rows_t - 1);
                 const int sb0 = nsb * slice / ks, sb1 = nsb * (slice + 1) / ks;
+                const unsigned char *wl0[kMats], *wh0[kMats];  // rows gl, gh at block 0
+#pragma unroll
+                for (int k = 0; k < kMats; ++k) {
+                    wl0[k] = stage + static_cast<size_t>(k * rows_t + gl) * row_bytes;
+                    wh0[k] = stage + static_cast<size_t>(k * rows_t + gh) * row_bytes;
+                }
+                const int8_t *act = a.q + static_cast<size_t>(g) * 64 + tq * 16;
                 float acc[kMats][4];
 #pragma unroll
                 for (int k = 0; k < kMats; ++k)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) acc[k][i] = 0.0f;
-                for (int sb = sb0; sb < sb1; ++sb) {
-                    const unsigned char *blk[kMats];
-                    BlockScales sl[kMats], sh[kMats];
-                    uint32_t dl[kMats], dh[kMats];  // f16 bits: d | dmin << 16
-                    int isum[kMats][4], ma[kMats][4], mb[kMats][4];
+                // (d4 d8) isum - (dmin4 d8) msum of block sb, per matrix and
+                // accumulator element
+                auto block_terms = [&](int sb, float (&t)[kMats][4]) {
+                const int boff = sb * kQ4Bytes;
+                BlockScales sl[kMats], sh[kMats];
+                uint32_t dl[kMats], dh[kMats];  // f16 bits: d | dmin << 16
+                int isum[kMats][4], ma[kMats][4], mb[kMats][4];
+#pragma unroll
+                for (int k = 0; k < kMats; ++k) {
+                    const uint4 hl = *reinterpret_cast<const uint4 *>(wl0[k] + boff);
+                    const uint4 hh = *reinterpret_cast<const uint4 *>(wh0[k] + boff);
+                    sl[k] = block_scales(hl.y, hl.z, hl.w);
+                    sh[k] = block_scales(hh.y, hh.z, hh.w);
+                    dl[k] = hl.x;
+                    dh[k] = hh.x;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) isum[k][i] = ma[k][i] = mb[k][i] = 0;
+                }
+#pragma unroll
+                for (int pp = 0; pp < 4; ++pp) {
+                    const uint4 bq = *reinterpret_cast<const uint4 *>(act + static_cast<size_t>(sb * 4 + pp) * NB * 64);
+                    const int qoff = boff + 16 + 32 * pp + 8 * tq;
 #pragma unroll
                     for (int k = 0; k < kMats; ++k) {
-                        blk[k] = stage + static_cast<size_t>(k * kTileRows + g) * row_bytes +
-                                 static_cast<size_t>(sb) * kQ4Bytes;
-                        const uint4 hl = v_lo ? *reinterpret_cast<const uint4 *>(blk[k]) : make_uint4(0, 0, 0, 0);
-                        const uint4 hh = v_hi ? *reinterpret_cast<const uint4 *>(blk[k] + 8 * row_bytes)
-                                              : make_uint4(0, 0, 0, 0);
-                        sl[k] = block_scales(hl.y, hl.z, hl.w);
-                        sh[k] = block_scales(hh.y, hh.z, hh.w);
-                        dl[k] = hl.x;
-                        dh[k] = hh.x;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) isum[k][i] = ma[k][i] = mb[k][i] = 0;
+                        const uint2 wl = *reinterpret_cast<const uint2 *>(wl0[k] + qoff);
+                        const uint2 wh = *reinterpret_cast<const uint2 *>(wh0[k] + qoff);
+                        int c0[4], c1[4];
+                        mma_u8s8_zero(c0, wl.x & kLo, wh.x & kLo, wl.y & kLo, wh.y & kLo, bq.x, bq.y);
+                        mma_u8s8_zero(c1, (wl.x >> 4) & kLo, (wh.x >> 4) & kLo, (wl.y >> 4) & kLo,
+                                      (wh.y >> 4) & kLo, bq.z, bq.w);
+                        const uint32_t m0l = sub_min4(sl[k], 2 * pp), m0h = sub_min4(sh[k], 2 * pp);
+                        const uint32_t m1l = sub_min4(sl[k], 2 * pp + 1), m1h = sub_min4(sh[k], 2 * pp + 1);
+                        mma_u8s8(ma[k], m0l, m0h, m0l, m0h, bq.x, bq.y);
+                        mma_u8s8(mb[k], m1l, m1h, m1l, m1h, bq.z, bq.w);
+                        const int s0l = sub_scale(sl[k], 2 * pp), s1l = sub_scale(sl[k], 2 * pp + 1);
+                        const int s0h = sub_scale(sh[k], 2 * pp), s1h = sub_scale(sh[k], 2 * pp + 1);
+                        isum[k][0] += s0l * c0[0] + s1l * c1[0];
+                        isum[k][1] += s0l * c0[1] + s1l * c1[1];
+                        isum[k][2] += s0h * c0[2] + s1h * c1[2];
+                        isum[k][3] += s0h * c0[3] + s1h * c1[3];
                     }
+                }
+                const float d8[2] = {a.d[(2 * tq) * nsb + sb], a.d[(2 * tq + 1) * nsb + sb]};
 #pragma unroll
-                    for (int pp = 0; pp < 4; ++pp) {
-                        const uint4 bq = *reinterpret_cast<const uint4 *>(
-                            a.q + (static_cast<size_t>(sb * 4 + pp) * NB + g) * 64 + tq * 16);
+                for (int k = 0; k < kMats; ++k) {
 #pragma unroll
-                        for (int k = 0; k < kMats; ++k) {
-                            const unsigned char *q = blk[k] + 16 + 32 * pp + 8 * tq;
-                            const uint2 wl = v_lo ? *reinterpret_cast<const uint2 *>(q) : make_uint2(0, 0);
-                            const uint2 wh = v_hi ? *reinterpret_cast<const uint2 *>(q + 8 * row_bytes)
-                                                  : make_uint2(0, 0);
-                            int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
-                            mma_u8s8(c0, wl.x & kLo, wh.x & kLo, wl.y & kLo, wh.y & kLo, bq.x, bq.y);
-                            mma_u8s8(c1, (wl.x >> 4) & kLo, (wh.x >> 4) & kLo, (wl.y >> 4) & kLo, (wh.y >> 4) & kLo,
-                                     bq.z, bq.w);
-                            const uint32_t m0l = sub_min4(sl[k], 2 * pp), m0h = sub_min4(sh[k], 2 * pp);
-                            const uint32_t m1l = sub_min4(sl[k], 2 * pp + 1), m1h = sub_min4(sh[k], 2 * pp + 1);
-                            mma_u8s8(ma[k], m0l, m0h, m0l, m0h, bq.x, bq.y);
-                            mma_u8s8(mb[k], m1l, m1h, m1l, m1h, bq.z, bq.w);
-                            const int s0l = sub_scale(sl[k], 2 * pp), s1l = sub_scale(sl[k], 2 * pp + 1);
-                            const int s0h = sub_scale(sh[k], 2 * pp), s1h = sub_scale(sh[k], 2 * pp + 1);
-                            isum[k][0] += s0l * c0[0] + s1l * c1[0];
-                            isum[k][1] += s0l * c0[1] + s1l * c1[1];
-                            isum[k][2] += s0h * c0[2] + s1h * c1[2];
-                            isum[k][3] += s0h * c0[3] + s1h * c1[3];
-                        }
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t dd = i < 2 ? dl[k] : dh[k];
+                        const float y8 = d8[i & 1];
+                        t[k][i] = __fmul_rn(half_bits(dd), y8) * static_cast<float>(isum[k][i]) -
+                                  __fmul_rn(half_bits(dd >> 16), y8) * static_cast<float>(ma[k][i] + mb[k][i]);
                     }
-                    const float d8[2] = {a.d[(2 * tq) * nsb + sb], a.d[(2 * tq + 1) * nsb + sb]};
+                }
+                            };
+                // two blocks per round: two independent mma / integer chains
+                int sb = sb0;
+                for (; sb + 1 < sb1; sb += 2) {
+                    float t0[kMats][4], t1[kMats][4];
+                    block_terms(sb, t0);
+                    block_terms(sb + 1, t1);
 #pragma unroll
-                    for (int k = 0; k < kMats; ++k) {
+                    for (int k = 0; k < kMats; ++k)
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint32_t dd = i < 2 ? dl[k] : dh[k];
-                            const float y8 = d8[i & 1];
-                            acc[k][i] += __fmul_rn(half_bits(dd), y8) * static_cast<float>(isum[k][i]) -
-                                         __fmul_rn(half_bits(dd >> 16), y8) * static_cast<float>(ma[k][i] + mb[k][i]);
-                        }
-                    }
+                        for (int i = 0; i < 4; ++i) acc[k][i] += t0[k][i] + t1[k][i];
+                }
+                if (sb < sb1) {
+                    float t0[kMats][4];
+                    block_terms(sb, t0);
+#pragma unroll
+                    for (int k = 0; k < kMats; ++k)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) acc[k][i] += t0[k][i];
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty0 + 8 * (tile % n_stages));  // this slice of the tile is read
@@ -1103,11 +1288,11 @@ __global__ void argmax_kernel(const float *logits, int32_t n_books, int32_t size
 }
 
 // ------------------------------------------------------------- launchers
-size_t gemv_smem(int mode, int nb, int n, int cols, int ring_bytes, bool has_norm) {
+size_t gemv_smem(int mode, int nb, int n, int cols, int ring_bytes, bool has_norm, int ksplit = 1) {
     const bool frag = nb > 1;
     size_t b = static_cast<size_t>(ring_bytes) + kBarBytes + q8_smem_bytes(frag ? nb : n, cols, frag) +
                (has_norm ? static_cast<size_t>(cols) * 4 : 0) + qkv_extra_bytes(mode, nb);
-    if (frag) b += static_cast<size_t>(kWarps) * (mode == kSwiglu ? 2 : 1) * 32 * sizeof(float4);  // partials
+    if (frag && ksplit > 1) b += static_cast<size_t>(kWarps) * (mode == kSwiglu ? 2 : 1) * 32 * sizeof(float4);
     return b;
 }
 
@@ -1144,7 +1329,7 @@ int num_sms_of(int dev) {
 template <int MODE, int NB>
 cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     auto kern = gemv_kernel<MODE, NB>;
-    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.ring_bytes, p.norm != nullptr);
+    const size_t smem = gemv_smem(MODE, NB, p.n, p.cols, p.ring_bytes, p.norm != nullptr, p.ksplit);
     static std::mutex mu;
     static bool done[64] = {};
     int dev = 0;
@@ -1165,7 +1350,7 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
         }
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((p.rows + p.rows_per_cta - 1) / p.rows_per_cta));
+    cfg.gridDim = dim3(static_cast<unsigned>(NB > 1 ? p.grid_ctas : (p.rows + p.rows_per_cta - 1) / p.rows_per_cta));
     cfg.blockDim = dim3(kThreads + 32);  // kWarps consumer warps + one producer warp
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -1173,9 +1358,9 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     int na = 1;
-    if (MODE == kQkv) {
+    if (MODE == kQkv || NB > 1) {  // a head's 4 CTAs; the CTAs sharing an activation image
         attr[1].id = cudaLaunchAttributeClusterDimension;
-        attr[1].val.clusterDim.x = kClusterCtas;
+        attr[1].val.clusterDim.x = NB > 1 ? p.share_ctas : kClusterCtas;
         attr[1].val.clusterDim.y = 1;
         attr[1].val.clusterDim.z = 1;
         na = 2;
@@ -1264,8 +1449,49 @@ void plan_rows(GemvParams &p, int mode, int dev) {
     p.ksplit = 1;
 }
 
-// Plan of a several-vector (tensor-core) launch: one CTA per SM with
-// ceil(rows / SMs) rows (32 for q/k/v, a quarter head), stages of kTileRows
+// CTAs sharing one activation image in the tensor-core kernel: the 4 of a
+// head for q/k/v; 4 (each reads a quarter of the activations) where the rows
+// of ceil(rows / 132) CTAs -- as many 4-CTA clusters as fit on a B200 at one
+// CTA per SM -- fit in shared memory; 2 for the FFN's gate/up pair, whose
+// 9728 rows need all 148 SMs to stay in flight.
+int share_ctas_of(int mode) { return mode == kSwiglu ? 2 : kClusterCtas; }
+
+// Clusters of csize CTAs that fit on `dev` at once with one CTA per SM (the
+// tensor-core kernel's shared memory), for grids of one wave.
+int max_clusters_of(int dev, int csize) {
+    static std::mutex mu;
+    static int cache[64][kClusterCtas + 1] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    const bool cached = dev >= 0 && dev < 64 && csize >= 1 && csize <= kClusterCtas;
+    if (cached && cache[dev][csize] != 0) return cache[dev][csize];
+    int v = num_sms_of(dev) / csize;
+    auto kern = gemv_kernel<kPlain, kMaxVec>;
+    const int smem = smem_cap_of(dev);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(num_sms_of(dev)));
+        cfg.blockDim = dim3(kThreads + 32);
+        cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = static_cast<unsigned>(csize);
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) v = std::min(v, n);
+    }
+    (void)cudaGetLastError();
+    v = std::max(v, 1);
+    if (cached) cache[dev][csize] = v;
+    return v;
+}
+
+// Plan of a several-vector (tensor-core) launch, in clusters of
+// kClusterCtas CTAs sharing the activation image: as many CTAs as fit at
+// once with one per SM (a multiple of kClusterCtas; 32 rows each for q/k/v,
+// a quarter head), ceil(rows / CTAs) rows each, stages of kTileRows
 // rows; ksplit warps share a tile's blocks when the CTA has fewer tiles than
 // warps (each slice at least 2 blocks).  All rows in flight when they fit
 // beside the activation image, else as many 16-row stages as fit (>= 2).
@@ -1275,8 +1501,17 @@ bool plan_tiles(GemvParams &p, int mode, int dev) {
     const int mats = mode == kSwiglu ? 2 : 1;
     const int nsb = p.cols / kQK;
     const int unit = nsb * kQ4Bytes * mats;
-    const int sms = num_sms_of(dev);
-    p.rows_per_cta = mode == kQkv ? kQkvRows : std::max(1, (p.rows + sms - 1) / sms);
+    const int csize = share_ctas_of(mode);
+    p.share_ctas = csize;
+    if (mode == kQkv) {
+        p.rows_per_cta = kQkvRows;
+        p.grid_ctas = (p.rows + kQkvRows - 1) / kQkvRows;  // whole heads: a multiple of 4
+    } else {
+        const int ctas = csize * max_clusters_of(dev, csize);
+        p.rows_per_cta = std::max(1, (p.rows + ctas - 1) / ctas);
+        const int used = (p.rows + p.rows_per_cta - 1) / p.rows_per_cta;
+        p.grid_ctas = (used + csize - 1) / csize * csize;
+    }
     const int rpc = p.rows_per_cta;
     const int tiles = (rpc + kTileRows - 1) / kTileRows;
     if (tiles > kMaxTiles) return false;
@@ -1285,15 +1520,13 @@ bool plan_tiles(GemvParams &p, int mode, int dev) {
     p.ksplit = std::max(1, std::min(kWarps / tiles, nsb / 2));
     p.empty_count = p.ksplit;
     p.lanes_per_row = 1;
-    const size_t fixed = gemv_smem(mode, kMaxVec, kMaxVec, p.cols, 0, p.norm != nullptr);
+    const size_t fixed = gemv_smem(mode, kMaxVec, kMaxVec, p.cols, 0, p.norm != nullptr, p.ksplit);
     const size_t cap = static_cast<size_t>(smem_cap_of(dev));
     if (fixed >= cap) return false;
     const size_t budget = cap - fixed;
-    // the last stage holds rpc - 16 (tiles - 1) rows of each matrix, the
-    // second matrix of kSwiglu at a full stage's offset
-    const int rows_last = rpc - (tiles - 1) * kTileRows;
-    const size_t all = static_cast<size_t>(tiles - 1) * p.stage_bytes +
-                       (mats == 1 ? static_cast<size_t>(rows_last) * unit : static_cast<size_t>(p.stage_bytes));
+    // a stage holds each matrix's rows of its tile back to back: all rows
+    // in flight take rpc * unit bytes
+    const size_t all = static_cast<size_t>(rpc) * unit;
     if (tiles <= kMaxStages && all <= budget) {
         p.n_stages = tiles;
         p.ring_bytes = static_cast<int32_t>(all);
