@@ -17,8 +17,10 @@ Workloads (synthetic N(0,1) data, random physical page order):
              slots finish with p=0.01 per step and are replaced at once.
   headsplit  one request near the 32768-position context, split by KV head
              over the N GPUs with an NCCL all-gather per layer.
-  backbone   the whole 36-layer Q4_K backbone decode step at batch 1 (the
-             projections, norms and output head around the KV path): a
+  backbone   the whole 36-layer Q4_K backbone decode step (the projections,
+             norms and output head around the KV path) at batch 1, or with
+             --batch B for B requests per step (hkv_backbone_decode with
+             max_batch B: the projections run on the tensor cores): a
              1024-token prompt, then greedy steps.
 
 Reported: `value` = tokens/s over all ranks (slots advanced one position
@@ -880,14 +882,16 @@ def make_backbone_weights(hkv, n_layers: int, text_vocab: int, dev: str, seed: i
 
 
 def bench_backbone(args):
-    """The whole 36-layer Q4_K backbone decode step at batch 1 (Qwen3-4B
-    shape: hidden 2560, FFN 9728, GQA 32/8): a 1024-token prompt of uniform
-    random text ids fed one token per decode call, then greedy steps (the
-    first maximum of each of the 8 codebooks' logits, whose embedding rows
-    are summed into the next input).  A step = embedding + 36 x (q/k/v with
-    per-head norms, RoPE + append + attention, o_proj + residual, SwiGLU FFN,
-    down + residual) + output head + greedy codes.  Under torchrun each rank
-    runs its own replica."""
+    """The whole 36-layer Q4_K backbone decode step (Qwen3-4B shape: hidden
+    2560, FFN 9728, GQA 32/8) for args.batch requests: a 1024-token prompt of
+    uniform random text ids per request, fed one token per request per decode
+    call, then greedy steps (the first maximum of each of the 8 codebooks'
+    logits, whose embedding rows are summed into the next input).  A step =
+    embedding + 36 x (q/k/v with per-head norms, RoPE + append + attention,
+    o_proj + residual, SwiGLU FFN, down + residual) + output head + greedy
+    codes, for every request at once.  Batch 1 uses the one-vector (dp4a)
+    projections; a backbone created for batches runs them on the tensor
+    cores.  Under torchrun each rank runs its own replica."""
     import datetime
 
     import torch
@@ -905,24 +909,25 @@ def bench_backbone(args):
         dist = tdist
     dev = f"cuda:{local}"
     text_vocab, prompt_len = 151936, args.prompt_len
+    B = args.batch
     weights, weight_bytes = make_backbone_weights(hkv, N_LAYERS, text_vocab, dev, 1234 + rank)
     total = prompt_len + args.warmup + args.steps + args.e2e_steps + 4
-    eng = hkv.Engine(n_layers=N_LAYERS, n_pages=total // 16 + 4, max_slots=1, device=local,
+    eng = hkv.Engine(n_layers=N_LAYERS, n_pages=B * (total // 16 + 4), max_slots=B, device=local,
                      shuffle_seed=99 + rank)
-    bb = hkv.Backbone(eng, weights, text_vocab=text_vocab, rms_eps=1e-6, max_batch=1)
+    bb = hkv.Backbone(eng, weights, text_vocab=text_vocab, rms_eps=1e-6, max_batch=B)
     stream = torch.cuda.Stream(device=local)
     sh = stream.cuda_stream
-    slot = eng.acquire(total)
-    ids = np.random.default_rng(5 + rank).integers(0, text_vocab, prompt_len)
+    slots = [eng.acquire(total) for _ in range(B)]
+    ids = np.random.default_rng(5 + rank).integers(0, text_vocab, (prompt_len, B))
     with torch.cuda.stream(stream):
-        for t, tok in enumerate(ids):
-            bb.embed_text([int(tok)], sh)
-            bb.decode([slot], want_logits=(t == prompt_len - 1), stream=sh)
+        for t in range(prompt_len):
+            bb.embed_text([int(i) for i in ids[t]], sh)
+            bb.decode(slots, want_logits=(t == prompt_len - 1), stream=sh)
     bb.sync_check(sh)
 
     def step():
-        bb.embed_codes(1, None, sh)
-        bb.decode([slot], want_logits=True, stream=sh)
+        bb.embed_codes(B, None, sh)
+        bb.decode(slots, want_logits=True, stream=sh)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -930,7 +935,7 @@ def bench_backbone(args):
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
-    ctx0 = eng.length(slot)
+    ctx0 = eng.length(slots[0])
     launches0 = eng.stats()["kernel_launches"]
     clocks = ClockSampler(local)
     clocks.start()
@@ -962,9 +967,11 @@ def bench_backbone(args):
         return float(t.item())
 
     ms = max_ranks(ms_local)
-    # Algorithmic bytes per step: every Q4_K matrix of the step once, the
-    # norms, 8 embedding rows, and per layer the KV path's 4096 L + 45056.
-    kv_bytes = sum(N_LAYERS * (4096 * (ctx0 + s + 1) + 45056) for s in range(args.steps))
+    # Algorithmic bytes per step: every Q4_K matrix of the step once (a
+    # tensor-core launch takes up to 8 requests), the norms, 8 embedding
+    # rows per request, and per layer and request the KV path's
+    # 4096 L + 45056.
+    kv_bytes = B * sum(N_LAYERS * (4096 * (ctx0 + s + 1) + 45056) for s in range(args.steps))
     step_bytes = weight_bytes + kv_bytes / args.steps
     peak, peak_kind = measured_peaks()
     gbs = step_bytes / (ms / args.steps / 1e3) / 1e9
@@ -974,9 +981,9 @@ def bench_backbone(args):
     # handed back as the next step's input.
     e2e = None
     if args.e2e_steps > 0:
-        hcodes = torch.empty((1, 8), dtype=torch.int32).pin_memory()
-        dcodes = torch.empty((1, 8), dtype=torch.int32, device=dev)
-        codes_view = torch.as_tensor(hkv.DeviceArray(bb.codes_ptr, (1, 8), "<i4"), device=dev)
+        hcodes = torch.empty((B, 8), dtype=torch.int32).pin_memory()
+        dcodes = torch.empty((B, 8), dtype=torch.int32, device=dev)
+        codes_view = torch.as_tensor(hkv.DeviceArray(bb.codes_ptr, (B, 8), "<i4"), device=dev)
 
         def e2e_step():
             with torch.cuda.stream(stream):
@@ -984,8 +991,8 @@ def bench_backbone(args):
             stream.synchronize()
             with torch.cuda.stream(stream):
                 dcodes.copy_(hcodes, non_blocking=True)
-            bb.embed_codes(1, dcodes, sh)
-            bb.decode([slot], want_logits=True, stream=sh)
+            bb.embed_codes(B, dcodes, sh)
+            bb.decode(slots, want_logits=True, stream=sh)
 
         e2e_step()
         torch.cuda.synchronize()
@@ -999,8 +1006,8 @@ def bench_backbone(args):
         e1.record(stream)
         torch.cuda.synchronize()
         e_ms = max_ranks(e0.elapsed_time(e1))
-        e2e = {"value": world * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 32, "steps": args.e2e_steps,
+        e2e = {"value": world * B * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": 32 * B, "d2h_bytes_per_step": 32 * B, "steps": args.e2e_steps,
                "ms_per_step": e_ms / args.e2e_steps,
                "path": "codes read back to pinned host memory and fed back through "
                        "hkv_backbone_embed_codes + hkv_backbone_decode each step"}
@@ -1009,27 +1016,34 @@ def bench_backbone(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_backbone(weights, ctx0)
+        if B > 1:
+            cpu["sample"] += ("; the reference decodes one request at a time, so B requests "
+                              "take B of these steps: the same tokens/s")
+    per_launch = (B + 7) // 8  # tensor-core launches per projection
     if rank == 0:
         print(json.dumps({
             "metric": "backbone decode tokens/s (36-layer Q4_K step incl. KV append + attention)",
-            "value": world * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "value": world * B * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "q4_k weights x q8_k activations (int dp4a), f32 accumulate, f16 KV",
+            "dtype": ("q4_k weights x q8_k activations (int dp4a), f32 accumulate, f16 KV" if B == 1 else
+                      "q4_k weights x q8_k activations (int8 mma m16n8k32 on the tensor cores), "
+                      "f32 accumulate, f16 KV"),
             "data": "synthetic: N(0,0.02) weights quantised to Q4_K on the device, uniform "
                     "random prompt ids",
-            "config": {"workload": f"backbone decode, batch 1: 36 layers, hidden 2560, FFN 9728, "
+            "config": {"workload": f"backbone decode, batch {B}: 36 layers, hidden 2560, FFN 9728, "
                                    f"GQA 32/8, {prompt_len}-token prompt then greedy steps "
                                    f"(contexts {ctx0 + 1}..{ctx0 + args.steps})",
-                       "global_batch": world, "layers": N_LAYERS,
+                       "global_batch": world * B, "batch_per_gpu": B, "layers": N_LAYERS,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: 2.2 GB of weights read per step"},
-            "roofline": {"kernel": "whole decode step (183 launches)", "bound": "hbm",
+            "roofline": {"kernel": f"whole decode step ({2 + (4 * N_LAYERS + 1) * per_launch} "
+                                   "projection/embedding launches + the engine's)", "bound": "hbm",
                          "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "traffic": None, "algorithmic_bytes_per_step": step_bytes,
                          "peak_kind": peak_kind},
             "cpu_baseline": cpu, "clocks": clk, "e2e": e2e,
-            "gpu_launches": (3 + 4 * N_LAYERS) * args.steps + engine_launches,
+            "gpu_launches": (2 + (4 * N_LAYERS + 1) * per_launch) * args.steps + engine_launches,
             "host_enqueue_ms_per_step": host_ms / args.steps,
         }), flush=True)
     bb.close()
@@ -1136,13 +1150,14 @@ def reference_backbone(args):
         "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights x q8_k activations, f32",
         "data": "synthetic random Q4_K blocks", "impl": "reference",
-        "config": {"workload": f"backbone decode, batch 1, context {ctx}", "global_batch": 1,
-                   "layers": 36, "parallelism": "host cores"},
+        "config": {"workload": f"backbone decode, batch {args.batch}, context {ctx}",
+                   "global_batch": args.batch, "layers": 36, "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{steps} decode steps of 2 of the 36 layers, scaled"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": ("the reference's GGML CPU graph cannot be built here (ggml submodule absent); "
-                 "this times its restatement in oracle/ on the host cores"),
+                 "this times its restatement in oracle/ on the host cores; the reference decodes "
+                 "one request at a time, so its tokens/s does not depend on the batch"),
     }), flush=True)
 
 
@@ -1224,6 +1239,9 @@ def main():
                          "(8/N KV heads) without the exchange")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
                     help="headsplit: how the per-head outputs reach every rank")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="backbone: requests per decode step (1: the reference's one request at a "
+                         "time; more: a backbone created for batches, tensor-core projections)")
     ap.add_argument("--prompt-len", type=int, default=1024,
                     help="backbone: prompt tokens before the greedy steps (1024 for every "
                          "reported number; fewer only for profiler captures)")

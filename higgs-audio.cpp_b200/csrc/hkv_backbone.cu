@@ -983,56 +983,57 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
                 // (d4 d8) isum - (dmin4 d8) msum of block sb, per matrix and
                 // accumulator element
                 auto block_terms = [&](int sb, float (&t)[kMats][4]) {
-                const int boff = sb * kQ4Bytes;
-                BlockScales sl[kMats], sh[kMats];
-                uint32_t dl[kMats], dh[kMats];  // f16 bits: d | dmin << 16
-                int isum[kMats][4], ma[kMats][4], mb[kMats][4];
-#pragma unroll
-                for (int k = 0; k < kMats; ++k) {
-                    const uint4 hl = *reinterpret_cast<const uint4 *>(wl0[k] + boff);
-                    const uint4 hh = *reinterpret_cast<const uint4 *>(wh0[k] + boff);
-                    sl[k] = block_scales(hl.y, hl.z, hl.w);
-                    sh[k] = block_scales(hh.y, hh.z, hh.w);
-                    dl[k] = hl.x;
-                    dh[k] = hh.x;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) isum[k][i] = ma[k][i] = mb[k][i] = 0;
-                }
-#pragma unroll
-                for (int pp = 0; pp < 4; ++pp) {
-                    const uint4 bq = *reinterpret_cast<const uint4 *>(act + static_cast<size_t>(sb * 4 + pp) * NB * 64);
-                    const int qoff = boff + 16 + 32 * pp + 8 * tq;
+                    const int boff = sb * kQ4Bytes;
+                    BlockScales sl[kMats], sh[kMats];
+                    uint32_t dl[kMats], dh[kMats];  // f16 bits: d | dmin << 16
+                    int isum[kMats][4], ma[kMats][4], mb[kMats][4];
 #pragma unroll
                     for (int k = 0; k < kMats; ++k) {
-                        const uint2 wl = *reinterpret_cast<const uint2 *>(wl0[k] + qoff);
-                        const uint2 wh = *reinterpret_cast<const uint2 *>(wh0[k] + qoff);
-                        int c0[4], c1[4];
-                        mma_u8s8_zero(c0, wl.x & kLo, wh.x & kLo, wl.y & kLo, wh.y & kLo, bq.x, bq.y);
-                        mma_u8s8_zero(c1, (wl.x >> 4) & kLo, (wh.x >> 4) & kLo, (wl.y >> 4) & kLo,
-                                      (wh.y >> 4) & kLo, bq.z, bq.w);
-                        const uint32_t m0l = sub_min4(sl[k], 2 * pp), m0h = sub_min4(sh[k], 2 * pp);
-                        const uint32_t m1l = sub_min4(sl[k], 2 * pp + 1), m1h = sub_min4(sh[k], 2 * pp + 1);
-                        mma_u8s8(ma[k], m0l, m0h, m0l, m0h, bq.x, bq.y);
-                        mma_u8s8(mb[k], m1l, m1h, m1l, m1h, bq.z, bq.w);
-                        const int s0l = sub_scale(sl[k], 2 * pp), s1l = sub_scale(sl[k], 2 * pp + 1);
-                        const int s0h = sub_scale(sh[k], 2 * pp), s1h = sub_scale(sh[k], 2 * pp + 1);
-                        isum[k][0] += s0l * c0[0] + s1l * c1[0];
-                        isum[k][1] += s0l * c0[1] + s1l * c1[1];
-                        isum[k][2] += s0h * c0[2] + s1h * c1[2];
-                        isum[k][3] += s0h * c0[3] + s1h * c1[3];
-                    }
-                }
-                const float d8[2] = {a.d[(2 * tq) * nsb + sb], a.d[(2 * tq + 1) * nsb + sb]};
+                        const uint4 hl = *reinterpret_cast<const uint4 *>(wl0[k] + boff);
+                        const uint4 hh = *reinterpret_cast<const uint4 *>(wh0[k] + boff);
+                        sl[k] = block_scales(hl.y, hl.z, hl.w);
+                        sh[k] = block_scales(hh.y, hh.z, hh.w);
+                        dl[k] = hl.x;
+                        dh[k] = hh.x;
 #pragma unroll
-                for (int k = 0; k < kMats; ++k) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t dd = i < 2 ? dl[k] : dh[k];
-                        const float y8 = d8[i & 1];
-                        t[k][i] = __fmul_rn(half_bits(dd), y8) * static_cast<float>(isum[k][i]) -
-                                  __fmul_rn(half_bits(dd >> 16), y8) * static_cast<float>(ma[k][i] + mb[k][i]);
+                        for (int i = 0; i < 4; ++i) isum[k][i] = ma[k][i] = mb[k][i] = 0;
                     }
-                }
+#pragma unroll
+                    for (int pp = 0; pp < 4; ++pp) {
+                        const uint4 bq =
+                            *reinterpret_cast<const uint4 *>(act + static_cast<size_t>(sb * 4 + pp) * NB * 64);
+                        const int qoff = boff + 16 + 32 * pp + 8 * tq;
+#pragma unroll
+                        for (int k = 0; k < kMats; ++k) {
+                            const uint2 wl = *reinterpret_cast<const uint2 *>(wl0[k] + qoff);
+                            const uint2 wh = *reinterpret_cast<const uint2 *>(wh0[k] + qoff);
+                            int c0[4], c1[4];
+                            mma_u8s8_zero(c0, wl.x & kLo, wh.x & kLo, wl.y & kLo, wh.y & kLo, bq.x, bq.y);
+                            mma_u8s8_zero(c1, (wl.x >> 4) & kLo, (wh.x >> 4) & kLo, (wl.y >> 4) & kLo,
+                                          (wh.y >> 4) & kLo, bq.z, bq.w);
+                            const uint32_t m0l = sub_min4(sl[k], 2 * pp), m0h = sub_min4(sh[k], 2 * pp);
+                            const uint32_t m1l = sub_min4(sl[k], 2 * pp + 1), m1h = sub_min4(sh[k], 2 * pp + 1);
+                            mma_u8s8(ma[k], m0l, m0h, m0l, m0h, bq.x, bq.y);
+                            mma_u8s8(mb[k], m1l, m1h, m1l, m1h, bq.z, bq.w);
+                            const int s0l = sub_scale(sl[k], 2 * pp), s1l = sub_scale(sl[k], 2 * pp + 1);
+                            const int s0h = sub_scale(sh[k], 2 * pp), s1h = sub_scale(sh[k], 2 * pp + 1);
+                            isum[k][0] += s0l * c0[0] + s1l * c1[0];
+                            isum[k][1] += s0l * c0[1] + s1l * c1[1];
+                            isum[k][2] += s0h * c0[2] + s1h * c1[2];
+                            isum[k][3] += s0h * c0[3] + s1h * c1[3];
+                        }
+                    }
+                    const float d8[2] = {a.d[(2 * tq) * nsb + sb], a.d[(2 * tq + 1) * nsb + sb]};
+#pragma unroll
+                    for (int k = 0; k < kMats; ++k) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t dd = i < 2 ? dl[k] : dh[k];
+                            const float y8 = d8[i & 1];
+                            t[k][i] = __fmul_rn(half_bits(dd), y8) * static_cast<float>(isum[k][i]) -
+                                      __fmul_rn(half_bits(dd >> 16), y8) * static_cast<float>(ma[k][i] + mb[k][i]);
+                        }
+                    }
                             };
                 // two blocks per round: two independent mma / integer chains
                 int sb = sb0;
