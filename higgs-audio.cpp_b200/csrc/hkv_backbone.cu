@@ -13,22 +13,27 @@
 // and dots it with the weight blocks in integers.  The kernels here do the
 // same arithmetic on the GPU:
 //
-//   * gemv_kernel: one pass over a Q4_K matrix, HBM-bound.  Every CTA first
-//     issues its first weight loads, then (after the previous kernel in the
-//     stream has finished: griddepcontrol.wait) quantises the activation
-//     vectors to Q8_K in shared memory -- optionally after the RMSNorm, done
-//     in double like GGML -- and streams the rest of its rows with 16-byte
-//     loads two superblocks ahead, dotting 4-bit weights with 8-bit
-//     activations by dp4a.  Epilogues: store, add a residual, SwiGLU of two
-//     matrices, or the per-head RMSNorm of q and k, whose 128 rows span a
-//     cluster of 4 CTAs that add their sums of squares through distributed
-//     shared memory.
+//   * gemv_kernel<mode, 1>: one pass over a Q4_K matrix for one activation
+//     vector.  Every CTA first issues its weight loads (1-D bulk copies into a
+//     shared-memory ring), then (after the previous kernel in the stream has
+//     finished: griddepcontrol.wait) quantises the activation vector to Q8_K
+//     in shared memory -- optionally after the RMSNorm, done in double like
+//     GGML -- and dots 4-bit weights with 8-bit activations by dp4a.
+//   * gemv_kernel<mode, 8>: up to 8 vectors on the tensor cores (integer
+//     mma.sync m16n8k32, one k-step = one 32-weight sub-block): 16-row tiles
+//     of weights x 8 vectors, the sub-block mins through the same mma.  The
+//     CTAs of a cluster share one fragment-order Q8_K image, each quantising
+//     a share of the blocks into every CTA's shared memory (distributed
+//     shared memory stores).
+//     Epilogues of both: store, add a residual, SwiGLU of two matrices, or
+//     the per-head RMSNorm of q and k, whose 128 rows span a cluster of 4
+//     CTAs that add their sums of squares through distributed shared memory.
 //   * q4k_quantize_kernel: the repo's Q4_K encoder (weights for tests and the
 //     benchmark; the reference quantises with GGML's tools offline).
 //   * embed_kernel / argmax_kernel: embedding rows (text ids or the sum of
 //     8 audio-codebook rows) and greedy codes per codebook.
 //
-// No TMA, no multicast: plain vector loads of this GPU's own memory.
+// Every copy reads this GPU's own memory into one CTA's shared memory.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
