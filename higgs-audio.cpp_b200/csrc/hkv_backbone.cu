@@ -62,7 +62,8 @@ constexpr int kQK = 256;        // weights per Q4_K / Q8_K block
 constexpr int kQ4Bytes = 144;   // bytes per Q4_K block
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxVec = 8;      // activation vectors per launch (one mma n-tile)
+constexpr int kMaxVec = 8;      // activation vectors of a tensor-core launch: one mma n-tile
+constexpr int kMaxVec2 = 16;    // or two n-tiles, when the image of 16 vectors fits
 constexpr int kTileRows = 16;   // weight rows of an mma tile
 constexpr int kClusterCtas = 4; // CTAs per head in the q/k/v launch (32 rows each)
 constexpr int kMaxCols = 16384;
@@ -74,7 +75,7 @@ struct GemvParams {
     int32_t row_end[3];       // virtual row boundaries of the matrices (kQkv)
     int32_t rows;             // virtual rows
     int32_t cols;
-    int32_t n;                // activation vectors, <= kMaxVec
+    int32_t n;                // activation vectors, <= kMaxVec2
     const float *x;           // [n][cols]
     const float *norm;        // nullptr or [cols]
     float eps;
@@ -731,14 +732,17 @@ __device__ __forceinline__ void store_row(const GemvParams &p, float *res, int r
 // item is the limit at batch 1, not bandwidth); the row sum is a fixed-order
 // shuffle reduction (deterministic), and the row's stage slot is released by
 // one arrival on the stage's "empty" barrier -- no CTA-wide barrier in the
-// loop.  NB activation vectors: 1, or kMaxVec with the products on the
-// tensor cores (mma m16n8k32, integer): stages of kTileRows rows, each tile
-// of 16 rows x 8 vectors taken by p.ksplit warps over disjoint block ranges,
-// whose partial sums are added in a fixed order after one consumer barrier.
+// loop.  NB activation vectors: 1, or 8 / 16 with the products on the
+// tensor cores (mma m16n8k32, integer; NB / 8 n-tiles sharing each weight
+// fragment): stages of kTileRows rows, each tile of 16 rows x NB vectors
+// taken by p.ksplit warps over disjoint block ranges, whose partial sums
+// are added in a fixed order after one consumer barrier.
 template <int MODE, int NB>
 __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2) gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int kMats = MODE == kSwiglu ? 2 : 1;
+    constexpr int NT = NB > 1 ? NB / 8 : 1;  // mma n-tiles of 8 vectors
+    static_assert(NB == 1 || NB % 8 == 0, "the tensor-core kernel takes 8 vectors per n-tile");
     const int nsb = p.cols / kQK;
     const int row_bytes = nsb * kQ4Bytes;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -980,18 +984,18 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
                     wh0[k] = stage + static_cast<size_t>(k * rows_t + gh) * row_bytes;
                 }
                 const int8_t *act = a.q + static_cast<size_t>(g) * 64 + tq * 16;
-                float acc[kMats][4];
+                float acc[kMats][NT][4];
 #pragma unroll
                 for (int k = 0; k < kMats; ++k)
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[k][i] = 0.0f;
-                // (d4 d8) isum - (dmin4 d8) msum of block sb, per matrix and
-                // accumulator element
-                auto block_terms = [&](int sb, float (&t)[kMats][4]) {
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) acc[k][nt][i] = 0.0f;
+                for (int sb = sb0; sb < sb1; ++sb) {
                     const int boff = sb * kQ4Bytes;
                     BlockScales sl[kMats], sh[kMats];
                     uint32_t dl[kMats], dh[kMats];  // f16 bits: d | dmin << 16
-                    int isum[kMats][4], ma[kMats][4], mb[kMats][4];
+                    int isum[kMats][NT][4], ma[kMats][NT][4], mb[kMats][NT][4];
 #pragma unroll
                     for (int k = 0; k < kMats; ++k) {
                         const uint4 hl = *reinterpret_cast<const uint4 *>(wl0[k] + boff);
@@ -1001,102 +1005,112 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
                         dl[k] = hl.x;
                         dh[k] = hh.x;
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) isum[k][i] = ma[k][i] = mb[k][i] = 0;
+                        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) isum[k][nt][i] = ma[k][nt][i] = mb[k][nt][i] = 0;
                     }
 #pragma unroll
                     for (int pp = 0; pp < 4; ++pp) {
-                        const uint4 bq =
-                            *reinterpret_cast<const uint4 *>(act + static_cast<size_t>(sb * 4 + pp) * NB * 64);
+                        uint4 bq[NT];
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            bq[nt] = *reinterpret_cast<const uint4 *>(
+                                act + (static_cast<size_t>(sb * 4 + pp) * NB + nt * 8) * 64);
+                        }
                         const int qoff = boff + 16 + 32 * pp + 8 * tq;
 #pragma unroll
                         for (int k = 0; k < kMats; ++k) {
                             const uint2 wl = *reinterpret_cast<const uint2 *>(wl0[k] + qoff);
                             const uint2 wh = *reinterpret_cast<const uint2 *>(wh0[k] + qoff);
-                            int c0[4], c1[4];
-                            mma_u8s8_zero(c0, wl.x & kLo, wh.x & kLo, wl.y & kLo, wh.y & kLo, bq.x, bq.y);
-                            mma_u8s8_zero(c1, (wl.x >> 4) & kLo, (wh.x >> 4) & kLo, (wl.y >> 4) & kLo,
-                                          (wh.y >> 4) & kLo, bq.z, bq.w);
+                            const uint32_t a0 = wl.x & kLo, a1 = wh.x & kLo, a2 = wl.y & kLo, a3 = wh.y & kLo;
+                            const uint32_t h0 = (wl.x >> 4) & kLo, h1 = (wh.x >> 4) & kLo;
+                            const uint32_t h2 = (wl.y >> 4) & kLo, h3 = (wh.y >> 4) & kLo;
                             const uint32_t m0l = sub_min4(sl[k], 2 * pp), m0h = sub_min4(sh[k], 2 * pp);
                             const uint32_t m1l = sub_min4(sl[k], 2 * pp + 1), m1h = sub_min4(sh[k], 2 * pp + 1);
-                            mma_u8s8(ma[k], m0l, m0h, m0l, m0h, bq.x, bq.y);
-                            mma_u8s8(mb[k], m1l, m1h, m1l, m1h, bq.z, bq.w);
                             const int s0l = sub_scale(sl[k], 2 * pp), s1l = sub_scale(sl[k], 2 * pp + 1);
                             const int s0h = sub_scale(sh[k], 2 * pp), s1h = sub_scale(sh[k], 2 * pp + 1);
-                            isum[k][0] += s0l * c0[0] + s1l * c1[0];
-                            isum[k][1] += s0l * c0[1] + s1l * c1[1];
-                            isum[k][2] += s0h * c0[2] + s1h * c1[2];
-                            isum[k][3] += s0h * c0[3] + s1h * c1[3];
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                int c0[4], c1[4];
+                                mma_u8s8_zero(c0, a0, a1, a2, a3, bq[nt].x, bq[nt].y);
+                                mma_u8s8_zero(c1, h0, h1, h2, h3, bq[nt].z, bq[nt].w);
+                                mma_u8s8(ma[k][nt], m0l, m0h, m0l, m0h, bq[nt].x, bq[nt].y);
+                                mma_u8s8(mb[k][nt], m1l, m1h, m1l, m1h, bq[nt].z, bq[nt].w);
+                                isum[k][nt][0] += s0l * c0[0] + s1l * c1[0];
+                                isum[k][nt][1] += s0l * c0[1] + s1l * c1[1];
+                                isum[k][nt][2] += s0h * c0[2] + s1h * c1[2];
+                                isum[k][nt][3] += s0h * c0[3] + s1h * c1[3];
+                            }
                         }
                     }
-                    const float d8[2] = {a.d[(2 * tq) * nsb + sb], a.d[(2 * tq + 1) * nsb + sb]};
 #pragma unroll
-                    for (int k = 0; k < kMats; ++k) {
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const int e0 = nt * 8 + 2 * tq;
+                        const float d8[2] = {a.d[e0 * nsb + sb], a.d[(e0 + 1) * nsb + sb]};
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint32_t dd = i < 2 ? dl[k] : dh[k];
-                            const float y8 = d8[i & 1];
-                            t[k][i] = __fmul_rn(half_bits(dd), y8) * static_cast<float>(isum[k][i]) -
-                                      __fmul_rn(half_bits(dd >> 16), y8) * static_cast<float>(ma[k][i] + mb[k][i]);
+                        for (int k = 0; k < kMats; ++k) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t dd = i < 2 ? dl[k] : dh[k];
+                                const float y8 = d8[i & 1];
+                                acc[k][nt][i] += __fmul_rn(half_bits(dd), y8) * static_cast<float>(isum[k][nt][i]) -
+                                                 __fmul_rn(half_bits(dd >> 16), y8) *
+                                                     static_cast<float>(ma[k][nt][i] + mb[k][nt][i]);
+                            }
                         }
                     }
-                            };
-                // two blocks per round: two independent mma / integer chains
-                int sb = sb0;
-                for (; sb + 1 < sb1; sb += 2) {
-                    float t0[kMats][4], t1[kMats][4];
-                    block_terms(sb, t0);
-                    block_terms(sb + 1, t1);
-#pragma unroll
-                    for (int k = 0; k < kMats; ++k)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) acc[k][i] += t0[k][i] + t1[k][i];
-                }
-                if (sb < sb1) {
-                    float t0[kMats][4];
-                    block_terms(sb, t0);
-#pragma unroll
-                    for (int k = 0; k < kMats; ++k)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) acc[k][i] += t0[k][i];
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty0 + 8 * (tile % n_stages));  // this slice of the tile is read
                 if (ks == 1) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int r = r_lo + 8 * (i >> 1), e = 2 * tq + (i & 1);
-                        if (r < nrows && e < p.n) store_row<MODE>(p, res, row0, r, e, acc[0][i], acc[kMats - 1][i]);
-                    }
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int r = r_lo + 8 * (i >> 1), e = nt * 8 + 2 * tq + (i & 1);
+                            if (r < nrows && e < p.n) {
+                                store_row<MODE>(p, res, row0, r, e, acc[0][nt][i], acc[kMats - 1][nt][i]);
+                            }
+                        }
                 } else {
 #pragma unroll
-                    for (int k = 0; k < kMats; ++k) {
-                        part4[(it * kMats + k) * 32 + lane] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
-                    }
+                    for (int k = 0; k < kMats; ++k)
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            part4[((it * kMats + k) * NT + nt) * 32 + lane] =
+                                make_float4(acc[k][nt][0], acc[k][nt][1], acc[k][nt][2], acc[k][nt][3]);
+                        }
                 }
             }
             if (ks > 1) {
                 // tiles * ks <= kWarps: every item above was one warp's only one
                 consumer_sync();
                 for (int tile = warp; tile < tiles && !bad; tile += kWarps) {
-                    float t[kMats][4];
+                    float t[kMats][NT][4];
 #pragma unroll
-                    for (int k = 0; k < kMats; ++k) {
+                    for (int k = 0; k < kMats; ++k)
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) t[k][i] = 0.0f;
-                        for (int s2 = 0; s2 < ks; ++s2) {
-                            const float4 v = part4[((tile * ks + s2) * kMats + k) * 32 + lane];
-                            t[k][0] += v.x;
-                            t[k][1] += v.y;
-                            t[k][2] += v.z;
-                            t[k][3] += v.w;
+                        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) t[k][nt][i] = 0.0f;
+                            for (int s2 = 0; s2 < ks; ++s2) {
+                                const float4 v = part4[(((tile * ks + s2) * kMats + k) * NT + nt) * 32 + lane];
+                                t[k][nt][0] += v.x;
+                                t[k][nt][1] += v.y;
+                                t[k][nt][2] += v.z;
+                                t[k][nt][3] += v.w;
+                            }
                         }
-                    }
                     const int r_lo = tile * kTileRows + g;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int r = r_lo + 8 * (i >> 1), e = 2 * tq + (i & 1);
-                        if (r < nrows && e < p.n) store_row<MODE>(p, res, row0, r, e, t[0][i], t[kMats - 1][i]);
-                    }
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int r = r_lo + 8 * (i >> 1), e = nt * 8 + 2 * tq + (i & 1);
+                            if (r < nrows && e < p.n) {
+                                store_row<MODE>(p, res, row0, r, e, t[0][nt][i], t[kMats - 1][nt][i]);
+                            }
+                        }
                 }
             }
         }
@@ -1298,7 +1312,9 @@ size_t gemv_smem(int mode, int nb, int n, int cols, int ring_bytes, bool has_nor
     const bool frag = nb > 1;
     size_t b = static_cast<size_t>(ring_bytes) + kBarBytes + q8_smem_bytes(frag ? nb : n, cols, frag) +
                (has_norm ? static_cast<size_t>(cols) * 4 : 0) + qkv_extra_bytes(mode, nb);
-    if (frag && ksplit > 1) b += static_cast<size_t>(kWarps) * (mode == kSwiglu ? 2 : 1) * 32 * sizeof(float4);
+    if (frag && ksplit > 1) {  // partial sums of the split tiles
+        b += static_cast<size_t>(kWarps) * (mode == kSwiglu ? 2 : 1) * (nb / 8) * 32 * sizeof(float4);
+    }
     return b;
 }
 
@@ -1503,7 +1519,7 @@ int max_clusters_of(int dev, int csize) {
 // beside the activation image, else as many 16-row stages as fit (>= 2).
 // The split depends on the shape only, so a vector's results do not depend
 // on how many others share the launch.  False when not even two stages fit.
-bool plan_tiles(GemvParams &p, int mode, int dev) {
+bool plan_tiles(GemvParams &p, int mode, int dev, int nb) {
     const int mats = mode == kSwiglu ? 2 : 1;
     const int nsb = p.cols / kQK;
     const int unit = nsb * kQ4Bytes * mats;
@@ -1526,7 +1542,7 @@ bool plan_tiles(GemvParams &p, int mode, int dev) {
     p.ksplit = std::max(1, std::min(kWarps / tiles, nsb / 2));
     p.empty_count = p.ksplit;
     p.lanes_per_row = 1;
-    const size_t fixed = gemv_smem(mode, kMaxVec, kMaxVec, p.cols, 0, p.norm != nullptr, p.ksplit);
+    const size_t fixed = gemv_smem(mode, nb, nb, p.cols, 0, p.norm != nullptr, p.ksplit);
     const size_t cap = static_cast<size_t>(smem_cap_of(dev));
     if (fixed >= cap) return false;
     const size_t budget = cap - fixed;
@@ -1556,9 +1572,9 @@ GemvParams vector_slice(const GemvParams &p, int mode, int e0, int count) {
 }
 
 // One vector: the dp4a kernel (plan_rows), unless p.tensor.  Several (or
-// p.tensor): the tensor-core kernel, kMaxVec vectors per launch (each launch
-// reads the weights once); if its plan does not fit shared memory, one dp4a
-// launch per vector.  The two kernels sum in different orders: a caller that
+// p.tensor): the tensor-core kernel, kMaxVec2 or kMaxVec vectors per launch
+// (each launch reads the weights once); if no plan fits shared memory, one
+// dp4a launch per vector.  The two kernels sum in different orders: a caller that
 // wants a vector's result not to depend on its batch-mates fixes p.tensor.
 template <int MODE>
 cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
@@ -1566,8 +1582,18 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
     cudaError_t st = cudaGetDevice(&dev);
     if (st != cudaSuccess) return st;
     if (p.n > 1 || p.tensor != 0) {
+        // 16 vectors per launch where their image fits beside the weights
+        // (the same tiles, slices and sums as 8 per launch: bit-identical)
+        GemvParams t2 = p;
+        if (p.n > kMaxVec && plan_tiles(t2, MODE, dev, kMaxVec2)) {
+            for (int e0 = 0; e0 < p.n; e0 += kMaxVec2) {
+                st = launch_one<MODE, kMaxVec2>(vector_slice(t2, MODE, e0, std::min(kMaxVec2, p.n - e0)), stream);
+                if (st != cudaSuccess) return st;
+            }
+            return cudaSuccess;
+        }
         GemvParams t = p;
-        if (plan_tiles(t, MODE, dev)) {
+        if (plan_tiles(t, MODE, dev, kMaxVec)) {
             for (int e0 = 0; e0 < p.n; e0 += kMaxVec) {
                 st = launch_one<MODE, kMaxVec>(vector_slice(t, MODE, e0, std::min(kMaxVec, p.n - e0)), stream);
                 if (st != cudaSuccess) return st;
