@@ -937,6 +937,7 @@ def bench_backbone(args):
         dist.barrier()
     ctx0 = eng.length(slots[0])
     launches0 = eng.stats()["kernel_launches"]
+    bb_launches0 = bb.kernel_launches
     clocks = ClockSampler(local)
     clocks.start()
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -956,8 +957,9 @@ def bench_backbone(args):
     bb.sync_check(sh)
     # the engine counts its own launches (append + attention, and a combine
     # launch where the plan merges split partials after the grid); the
-    # backbone adds embedding, 4 projections per layer, the head and argmax
+    # backbone counts its embedding, projection and argmax launches
     engine_launches = eng.stats()["kernel_launches"] - launches0
+    backbone_launches = bb.kernel_launches - bb_launches0
 
     def max_ranks(x):
         if dist is None:
@@ -1019,7 +1021,6 @@ def bench_backbone(args):
         if B > 1:
             cpu["sample"] += ("; the reference decodes one request at a time, so B requests "
                               "take B of these steps: the same tokens/s")
-    per_launch = (B + 7) // 8  # tensor-core launches per projection
     if rank == 0:
         print(json.dumps({
             "metric": "backbone decode tokens/s (36-layer Q4_K step incl. KV append + attention)",
@@ -1037,13 +1038,13 @@ def bench_backbone(args):
                        "global_batch": world * B, "batch_per_gpu": B, "layers": N_LAYERS,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: 2.2 GB of weights read per step"},
-            "roofline": {"kernel": f"whole decode step ({2 + (4 * N_LAYERS + 1) * per_launch} "
-                                   "projection/embedding launches + the engine's)", "bound": "hbm",
+            "roofline": {"kernel": f"whole decode step ({backbone_launches // args.steps} "
+                                   "embedding/projection/argmax launches + the engine's)", "bound": "hbm",
                          "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "traffic": None, "algorithmic_bytes_per_step": step_bytes,
                          "peak_kind": peak_kind},
             "cpu_baseline": cpu, "clocks": clk, "e2e": e2e,
-            "gpu_launches": (2 + (4 * N_LAYERS + 1) * per_launch) * args.steps + engine_launches,
+            "gpu_launches": backbone_launches + engine_launches,
             "host_enqueue_ms_per_step": host_ms / args.steps,
         }), flush=True)
     bb.close()

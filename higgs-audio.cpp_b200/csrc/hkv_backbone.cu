@@ -1577,7 +1577,7 @@ GemvParams vector_slice(const GemvParams &p, int mode, int e0, int count) {
 // dp4a launch per vector.  The two kernels sum in different orders: a caller that
 // wants a vector's result not to depend on its batch-mates fixes p.tensor.
 template <int MODE>
-cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
+cudaError_t launch_gemv(GemvParams p, cudaStream_t stream, int64_t *launches = nullptr) {
     int dev = 0;
     cudaError_t st = cudaGetDevice(&dev);
     if (st != cudaSuccess) return st;
@@ -1589,6 +1589,7 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
             for (int e0 = 0; e0 < p.n; e0 += kMaxVec2) {
                 st = launch_one<MODE, kMaxVec2>(vector_slice(t2, MODE, e0, std::min(kMaxVec2, p.n - e0)), stream);
                 if (st != cudaSuccess) return st;
+                if (launches != nullptr) ++*launches;
             }
             return cudaSuccess;
         }
@@ -1597,6 +1598,7 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
             for (int e0 = 0; e0 < p.n; e0 += kMaxVec) {
                 st = launch_one<MODE, kMaxVec>(vector_slice(t, MODE, e0, std::min(kMaxVec, p.n - e0)), stream);
                 if (st != cudaSuccess) return st;
+                if (launches != nullptr) ++*launches;
             }
             return cudaSuccess;
         }
@@ -1608,6 +1610,7 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream) {
     for (int e0 = 0; e0 < p.n; ++e0) {
         st = launch_one<MODE, 1>(vector_slice(p, MODE, e0, 1), stream);
         if (st != cudaSuccess) return st;
+        if (launches != nullptr) ++*launches;
     }
     return cudaSuccess;
 }
@@ -1862,6 +1865,7 @@ struct hkv_backbone {
     int32_t *ids_host = nullptr;      // pinned staging for hkv_backbone_embed_text
     cudaEvent_t ids_done = nullptr;   // the staging copy has been read
     hkv::DeviceError *err = nullptr;
+    int64_t launches = 0;             // kernels launched by this backbone (the engine counts its own)
     std::string last_error;
 };
 
@@ -2036,6 +2040,7 @@ int hkv_backbone_embed_text(hkv_backbone *bb, int32_t n, const int32_t *ids, hkv
     if (st != HKV_OK) return st;
     st = bb_cuda(bb, cudaEventRecord(bb->ids_done, s), "hkv_backbone_embed_text");
     if (st != HKV_OK) return st;
+    ++bb->launches;
     return bb_cuda(bb, launch_embed(static_cast<const uint8_t *>(bb->w.token_embd), bb->w.text_vocab,
                                     bb->w.hidden, bb->ids, 1, 0, n, bb->hidden, bb->err, s),
                    "hkv_backbone_embed_text");
@@ -2050,6 +2055,7 @@ int hkv_backbone_embed_codes(hkv_backbone *bb, int32_t n, const int32_t *codes, 
         return bb_fail(bb, HKV_ERR_INVALID, "hkv_backbone_embed_codes: codes must be 4-byte aligned");
     }
     DeviceGuard g(bb->cfg.device);
+    ++bb->launches;
     return bb_cuda(bb, launch_embed(static_cast<const uint8_t *>(bb->w.audio_embd),
                                     static_cast<int64_t>(bb->logit_rows), bb->w.hidden,
                                     codes != nullptr ? codes : bb->codes, bb->w.n_codebooks,
@@ -2100,7 +2106,7 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
         p.head_norm[1] = L.attn_k_norm;
         p.err = bb->err;
         p.tensor = tc;
-        int st = bb_cuda(bb, launch_gemv<kQkv>(p, s), "hkv_backbone_decode: q/k/v");
+        int st = bb_cuda(bb, launch_gemv<kQkv>(p, s, &bb->launches), "hkv_backbone_decode: q/k/v");
         if (st != HKV_OK) return st;
         // RoPE + append + attention (:5734-5786)
         st = hkv_decode_step(bb->kv, l, n, slots, bb->q, bb->k, bb->v, bb->attn, stream);
@@ -2110,7 +2116,7 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
         // h = h + Wo attn (:5790-5791)
         st = bb_cuda(bb, launch_gemv<kPlain>(with_tc(plain_params(L.attn_output, w.hidden, bb->q_rows, n, bb->attn,
                                                                   nullptr, eps, bb->hidden, bb->hidden, bb->err)),
-                                             s),
+                                             s, &bb->launches),
                      "hkv_backbone_decode: o_proj");
         if (st != HKV_OK) return st;
         // g = silu(Wg m) * (Wu m), m = rms_norm(h) * ffn_norm (:5806-5822)
@@ -2118,12 +2124,12 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
                                     bb->gated, bb->err);
         f.w[1] = static_cast<const uint8_t *>(L.ffn_up);
         f.tensor = tc;
-        st = bb_cuda(bb, launch_gemv<kSwiglu>(f, s), "hkv_backbone_decode: gate/up");
+        st = bb_cuda(bb, launch_gemv<kSwiglu>(f, s, &bb->launches), "hkv_backbone_decode: gate/up");
         if (st != HKV_OK) return st;
         // h = h + Wd g (:5823, :5843)
         st = bb_cuda(bb, launch_gemv<kPlain>(with_tc(plain_params(L.ffn_down, w.hidden, w.ffn, n, bb->gated,
                                                                   nullptr, eps, bb->hidden, bb->hidden, bb->err)),
-                                             s),
+                                             s, &bb->launches),
                      "hkv_backbone_decode: down");
         if (st != HKV_OK) return st;
     }
@@ -2136,13 +2142,20 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
         st = bb_cuda(bb, launch_gemv<kPlain>(with_tc(plain_params(w.audio_output, bb->logit_rows, w.hidden, n,
                                                                   bb->hidden, w.output_norm, eps, nullptr,
                                                                   bb->logits, bb->err)),
-                                             s),
+                                             s, &bb->launches),
                      "hkv_backbone_decode: output head");
         if (st != HKV_OK) return st;
         st = bb_cuda(bb, launch_argmax(bb->logits, w.n_codebooks, w.codebook_size, n, bb->codes, s),
                      "hkv_backbone_decode: argmax");
         if (st != HKV_OK) return st;
+        ++bb->launches;
     }
+    return HKV_OK;
+}
+
+int hkv_backbone_kernel_launches(const hkv_backbone *bb, int64_t *launches) {
+    if (bb == nullptr || launches == nullptr) return HKV_ERR_INVALID;
+    *launches = bb->launches;
     return HKV_OK;
 }
 

@@ -191,6 +191,7 @@ SIGNATURES = {
     "hkv_backbone_buffers": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)],
                              ctypes.c_int),
     "hkv_backbone_sync_check": ([_P, _P], ctypes.c_int),
+    "hkv_backbone_kernel_launches": ([_P, _I64P], ctypes.c_int),
     "hkv_profile_enable": ([_P, ctypes.c_int], ctypes.c_int),
     "hkv_profile_reset": ([_P], ctypes.c_int),
     "hkv_profile_read": ([_P, ctypes.c_int, _I64P, ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
@@ -615,6 +616,13 @@ class Backbone:
 
     def sync_check(self, stream=None) -> None:
         self._check(self.lib.hkv_backbone_sync_check(self.handle, _stream(stream)))
+
+    @property
+    def kernel_launches(self) -> int:
+        """Kernels this backbone has launched (embedding, projections, argmax)."""
+        v = ctypes.c_int64(0)
+        self._check(self.lib.hkv_backbone_kernel_launches(self.handle, ctypes.byref(v)))
+        return v.value
 
     def close(self) -> None:
         if getattr(self, "handle", None):

@@ -45,7 +45,8 @@
 extern "C" {
 #endif
 
-#define HKV_ABI_VERSION 3  /* 2: hkv_pool_stats.kernel_launches; 3: tensor_cores in the q4k args */
+#define HKV_ABI_VERSION 3  /* 2: hkv_pool_stats.kernel_launches; 3: tensor_cores in the q4k args,
+                              hkv_backbone_kernel_launches */
 
 typedef enum hkv_status {
     HKV_OK = 0,
@@ -439,6 +440,9 @@ int hkv_backbone_decode(hkv_backbone *bb, int32_t n, const int32_t *slots, int32
 int hkv_backbone_buffers(const hkv_backbone *bb, float **hidden, float **logits, int32_t **codes);
 /* Synchronises `stream` and reports a bad embedding id recorded on the GPU. */
 int hkv_backbone_sync_check(hkv_backbone *bb, hkv_stream stream);
+/* Kernels this backbone has launched (embedding, projections, argmax; the
+ * engine counts the KV path's in hkv_pool_stats.kernel_launches). */
+int hkv_backbone_kernel_launches(const hkv_backbone *bb, int64_t *launches);
 
 /* ---------------------------------------------------------- profiling -- */
 

@@ -344,6 +344,7 @@ def test_backbone_steps_match_oracle(hkv_lib, oracle):
                 assert torch.equal(logits[:1], lg_ser)
     # joint greedy steps of both slots (the several-vector kernels)
     for step in range(3):
+        launches0 = bb.kernel_launches
         if step == 0:
             bb.embed_text([1, 2], stream)
         else:
@@ -353,6 +354,8 @@ def test_backbone_steps_match_oracle(hkv_lib, oracle):
         if step > 0:
             assert np.array_equal(h0.cpu().numpy(), emb.embed_codes(prev_codes))
         bb.decode(slots_bb, stream=stream)
+        # embedding + 4 projections x 2 layers + output head + argmax
+        assert bb.kernel_launches - launches0 == 1 + 4 * n_layers + 2
         h_ser, lg_ser = ser.run(h0, slots_ser, True)
         torch.cuda.synchronize()
         assert torch.equal(hidden, h_ser), step
