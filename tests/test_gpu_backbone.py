@@ -66,6 +66,10 @@ def test_encoder_round_trip(hkv_lib, oracle):
     (2560, 9728, 1, False, True, True),     # ffn_down (rows in flight beside a 9728-wide image)
     (8208, 2560, 16, True, False, False),   # the output head at batch 16
     (4096, 2560, 2, True, False, False),
+    (40, 256, 3, True, True, False),        # one block per row, one partial tile
+    (1000, 512, 16, False, True, False),    # 16 vectors in one launch, residual
+    (130, 16384, 5, False, False, False),   # the widest rows, CTAs without rows
+    (2560, 9728, 13, False, True, False),   # down: 8 + 5 vectors (two launches)
 ])
 def test_gemv_matches_oracle(hkv_lib, oracle, rows, cols, n, use_norm, use_res, tc):
     import hkv
@@ -116,7 +120,7 @@ def test_swiglu_matches_oracle(hkv_lib, oracle, n, tc):
     assert rel_err(y.cpu().numpy(), ref) <= PROJ_TOL
 
 
-@pytest.mark.parametrize("n,tc", [(1, False), (3, False), (1, True)])
+@pytest.mark.parametrize("n,tc", [(1, False), (3, False), (1, True), (16, False)])
 def test_qkv_head_norm_matches_oracle(hkv_lib, oracle, n, tc):
     import hkv
     _, bq = q4k_matrix(hkv, 4096, 2560, 60)
