@@ -1442,22 +1442,15 @@ int single_vector_rows(const GemvParams &p, int mode, int dev) {
     return pair_fits && (!one_fits || r2 < r1) ? rpc2 : rpc1;
 }
 
-// Ring plan.  A single vector takes single_vector_rows; several vectors one
-// CTA per SM.  The lanes per row -- and with them the order in which a row's
-// products are summed -- come from the single-vector plan of the shape, so a
-// vector's results do not depend on how many others share the launch.  A
-// ring that cannot hold its CTA's rows streams them through stages of about
-// kStreamStageBytes.
+// Ring plan of a one-vector (dp4a) launch: single_vector_rows.  The lanes
+// per row -- and with them the order in which a row's products are summed --
+// come from the shape alone.  A ring that cannot hold its CTA's rows streams
+// them through stages of about kStreamStageBytes.
 void plan_rows(GemvParams &p, int mode, int dev) {
     const int mats = mode == kSwiglu ? 2 : 1;
     const int unit = p.cols / kQK * kQ4Bytes * mats;
     const int rpc_single = single_vector_rows(p, mode, dev);
-    if (mode == kQkv || p.n == 1) {
-        p.rows_per_cta = rpc_single;
-    } else {
-        const int sms = num_sms_of(dev);
-        p.rows_per_cta = std::max(1, (p.rows + sms - 1) / sms);
-    }
+    p.rows_per_cta = rpc_single;
     if (static_cast<int64_t>(p.rows_per_cta) * unit <= kRingCap) {
         ring_all_in_flight(p.rows_per_cta, unit, p);
     } else {
@@ -1603,12 +1596,14 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream, int64_t *launches = n
             return cudaSuccess;
         }
     }
-    plan_rows(p, MODE, dev);
-    if (gemv_smem(MODE, 1, 1, p.cols, p.ring_bytes, p.norm != nullptr) > static_cast<size_t>(smem_cap_of(dev))) {
+    GemvParams one = p;  // one vector per launch
+    one.n = 1;
+    plan_rows(one, MODE, dev);
+    if (gemv_smem(MODE, 1, 1, p.cols, one.ring_bytes, p.norm != nullptr) > static_cast<size_t>(smem_cap_of(dev))) {
         return cudaErrorInvalidValue;
     }
     for (int e0 = 0; e0 < p.n; ++e0) {
-        st = launch_one<MODE, 1>(vector_slice(p, MODE, e0, 1), stream);
+        st = launch_one<MODE, 1>(vector_slice(one, MODE, e0, 1), stream);
         if (st != cudaSuccess) return st;
         if (launches != nullptr) ++*launches;
     }
