@@ -192,6 +192,19 @@ __host__ __device__ inline size_t q8_smem_bytes(int n, int cols, bool frag) {
     return b;
 }
 
+// Shared-memory stride of a weight row in the tensor-core kernel: the row's
+// bytes padded to an odd multiple of 32 modulo 128, so the 8-byte fragment
+// loads of four consecutive rows (one 16-lane load phase) fall in four
+// different 32-byte bank groups (o_proj's 2304-byte rows are a multiple of
+// 128 and would put all four in the same banks).
+__host__ __device__ constexpr int smem_row_stride(int row_bytes) {
+    return row_bytes + ((row_bytes % 128 == 32 || row_bytes % 128 == 96) ? 0
+                        : (row_bytes % 128 < 32 ? 32 - row_bytes % 128
+                                                : (row_bytes % 128 < 96 ? 96 - row_bytes % 128 : 160 - row_bytes % 128)));
+}
+static_assert(smem_row_stride(2304) % 128 == 32 && smem_row_stride(1440) == 1440 && smem_row_stride(5472) == 5472,
+              "row strides of the backbone's shapes");
+
 // kQkv: the projected rows [nb][kQkvRows] and the cluster's sums of
 // squares [kClusterCtas][nb] after the activation image.
 __host__ __device__ constexpr int qkv_extra_bytes(int mode, int nb) {
@@ -481,6 +494,11 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The same with nothing to publish: every CTA of the cluster has started.
+__device__ __forceinline__ void cluster_sync_started() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
 // The fragment-order Q8_K image of n_vec vectors (a.frag != 0), shared by
 // the kClusterCtas CTAs of a cluster: CTA rank r quantises blocks
 // [nsb r / C, nsb (r + 1) / C) of every vector and stores them into the
@@ -745,6 +763,7 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
     static_assert(NB == 1 || NB % 8 == 0, "the tensor-core kernel takes 8 vectors per n-tile");
     const int nsb = p.cols / kQK;
     const int row_bytes = nsb * kQ4Bytes;
+    const int srow = NB > 1 ? smem_row_stride(row_bytes) : row_bytes;  // row stride in the ring
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool producer = warp == kWarps;
     const int row0 = blockIdx.x * p.rows_per_cta;
@@ -805,10 +824,24 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
             mbar_arrive_expect_tx(bar, bytes * kMats);
 #pragma unroll
             for (int k = 0; k < kMats; ++k) {
-                // several vectors: a stage holds each matrix's rows of the
-                // chunk back to back (the ring holds exactly the CTA's rows)
-                bulk_load(stage + k * (NB > 1 ? rows_c : R) * row_bytes,
-                          wbase[k] + static_cast<size_t>(r0) * row_bytes, bytes, bar, policy);
+                if (NB > 1) {
+                    // a stage holds each matrix's rows of the chunk back to
+                    // back (the ring holds exactly the CTA's rows), one copy
+                    // per row where the stride is padded
+                    if (srow == row_bytes) {
+                        bulk_load(stage + k * rows_c * row_bytes, wbase[k] + static_cast<size_t>(r0) * row_bytes,
+                                  bytes, bar, policy);
+                    } else {
+                        for (int r = 0; r < rows_c; ++r) {
+                            bulk_load(stage + (k * rows_c + r) * srow,
+                                      wbase[k] + static_cast<size_t>(r0 + r) * row_bytes,
+                                      static_cast<uint32_t>(row_bytes), bar, policy);
+                        }
+                    }
+                } else {
+                    bulk_load(stage + k * R * row_bytes, wbase[k] + static_cast<size_t>(r0) * row_bytes, bytes,
+                              bar, policy);
+                }
             }
             issued = c + 1;
         };
@@ -828,7 +861,7 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
             // the cluster barriers of the consumers' activation prologue:
             // started, sums of squares (with a norm), image complete
             __syncwarp();
-            cluster_sync_all();
+            cluster_sync_started();
             if (p.norm != nullptr) cluster_sync_all();
             cluster_sync_all();
         }
@@ -854,7 +887,7 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
             if (p.norm != nullptr) mbar_wait_bounded(normbar, 0);
         }
     } else {
-        if constexpr (NB > 1) cluster_sync_all();  // every CTA of the cluster has started
+        if constexpr (NB > 1) cluster_sync_started();
         pdl_wait();  // x (and y, residual) belong to the kernels before
         bool qok;
         if constexpr (NB > 1) {
@@ -980,8 +1013,8 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
                 const unsigned char *wl0[kMats], *wh0[kMats];  // rows gl, gh at block 0
 #pragma unroll
                 for (int k = 0; k < kMats; ++k) {
-                    wl0[k] = stage + static_cast<size_t>(k * rows_t + gl) * row_bytes;
-                    wh0[k] = stage + static_cast<size_t>(k * rows_t + gh) * row_bytes;
+                    wl0[k] = stage + static_cast<size_t>(k * rows_t + gl) * srow;
+                    wh0[k] = stage + static_cast<size_t>(k * rows_t + gh) * srow;
                 }
                 const int8_t *act = a.q + static_cast<size_t>(g) * 64 + tq * 16;
                 float acc[kMats][NT][4];
@@ -1515,7 +1548,7 @@ int max_clusters_of(int dev, int csize) {
 bool plan_tiles(GemvParams &p, int mode, int dev, int nb) {
     const int mats = mode == kSwiglu ? 2 : 1;
     const int nsb = p.cols / kQK;
-    const int unit = nsb * kQ4Bytes * mats;
+    const int unit = smem_row_stride(nsb * kQ4Bytes) * mats;  // ring bytes per row
     const int csize = share_ctas_of(mode);
     p.share_ctas = csize;
     if (mode == kQkv) {
