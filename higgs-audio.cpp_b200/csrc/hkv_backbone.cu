@@ -62,6 +62,7 @@ constexpr int kQK = 256;        // weights per Q4_K / Q8_K block
 constexpr int kQ4Bytes = 144;   // bytes per Q4_K block
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
+constexpr int kWarpsWide = 12;  // consumer warps of the one-CTA-per-SM tensor-core kernels
 constexpr int kMaxVec = 8;      // activation vectors of a tensor-core launch: one mma n-tile
 constexpr int kMaxVec2 = 16;    // or two n-tiles, when the image of 16 vectors fits
 constexpr int kTileRows = 16;   // weight rows of an mma tile
@@ -69,6 +70,12 @@ constexpr int kClusterCtas = 4; // CTAs per head in the q/k/v launch (32 rows ea
 constexpr int kMaxCols = 16384;
 
 enum Mode { kPlain = 0, kSwiglu = 1, kQkv = 2 };
+
+// Consumer warps of gemv_kernel<mode, nb>: 8, or kWarpsWide for the tensor-core
+// kernels that run one CTA per SM (q/k/v keeps 8 to fit two CTAs per SM).
+__host__ __device__ constexpr int consumer_warps(int mode, int nb) {
+    return nb > 1 && mode != kQkv ? kWarpsWide : kWarps;
+}
 
 struct GemvParams {
     const uint8_t *w[3];      // kPlain: w[0]; kSwiglu: gate, up; kQkv: q, k, v
@@ -240,6 +247,12 @@ __device__ __forceinline__ int8_t *q8_store_at(const Q8View &a, int cols, int e,
 // Barrier of the kWarps consumer warps only (the producer warp never joins).
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");
+}
+
+// The same for W consumer warps.
+template <int W>
+__device__ __forceinline__ void consumer_sync_w() {
+    asm volatile("bar.sync 1, %0;" ::"r"(W * 32) : "memory");
 }
 
 // Q8_K quantisation of one 256-element block held 8 per lane across a warp
@@ -516,6 +529,7 @@ __device__ __forceinline__ void cluster_sync_started() {
 // same barriers).
 constexpr int kQuantBatch = 8;
 
+template <int W>
 __device__ bool quantize_activations_frag(const GemvParams &p, const float *x0, int n_vec, const Q8View &a,
                                           double *ssp, const float *normbuf, uint32_t normbar) {
     cg::cluster_group cl = cg::this_cluster();
@@ -536,20 +550,20 @@ __device__ bool quantize_activations_frag(const GemvParams &p, const float *x0, 
     };
     // one batch of blocks per warp: the values stay in registers across the
     // norm's barrier; otherwise the second pass loads them again
-    const bool one_batch = items <= kWarps * kQuantBatch;
+    const bool one_batch = items <= W * kQuantBatch;
     float v[kQuantBatch][8];
     auto load_batch = [&](int base) {
 #pragma unroll
         for (int u = 0; u < kQuantBatch; ++u) {
-            if (base + kWarps * u < items) load(base + kWarps * u, v[u]);
+            if (base + W * u < items) load(base + W * u, v[u]);
         }
     };
     if (p.norm != nullptr) {
-        for (int base = warp; base < items; base += kWarps * kQuantBatch) {
+        for (int base = warp; base < items; base += W * kQuantBatch) {
             load_batch(base);
 #pragma unroll
             for (int u = 0; u < kQuantBatch; ++u) {
-                const int it = base + kWarps * u;
+                const int it = base + W * u;
                 if (it >= items) continue;
                 double ss = 0.0;
 #pragma unroll
@@ -570,13 +584,13 @@ __device__ bool quantize_activations_frag(const GemvParams &p, const float *x0, 
         // waited for its predecessor; a warp that gave up still takes every
         // barrier below
         norm_ok = __all_sync(0xffffffffu, mbar_wait_bounded(normbar, 0));
-        consumer_sync();
+        consumer_sync_w<W>();
     }
-    for (int base = warp; base < items; base += kWarps * kQuantBatch) {
+    for (int base = warp; base < items; base += W * kQuantBatch) {
         if (p.norm == nullptr || !one_batch) load_batch(base);
 #pragma unroll
         for (int u = 0; u < kQuantBatch; ++u) {
-            const int it = base + kWarps * u;
+            const int it = base + W * u;
             if (it >= items) continue;
             const int e = it / nb, b = b0 + it - e * nb;
             float w[8];
@@ -756,7 +770,8 @@ __device__ __forceinline__ void store_row(const GemvParams &p, float *res, int r
 // taken by p.ksplit warps over disjoint block ranges, whose partial sums
 // are added in a fixed order after one consumer barrier.
 template <int MODE, int NB>
-__global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2) gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(consumer_warps(MODE, NB) * 32 + 32, NB > 1 && MODE != kQkv ? 1 : 2)
+    gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int kMats = MODE == kSwiglu ? 2 : 1;
     constexpr int NT = NB > 1 ? NB / 8 : 1;  // mma n-tiles of 8 vectors
@@ -765,7 +780,8 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
     const int row_bytes = nsb * kQ4Bytes;
     const int srow = NB > 1 ? smem_row_stride(row_bytes) : row_bytes;  // row stride in the ring
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool producer = warp == kWarps;
+    constexpr int kW = consumer_warps(MODE, NB);  // consumer warps; warp kW is the producer
+    const bool producer = warp == kW;
     const int row0 = blockIdx.x * p.rows_per_cta;
     const int nrows = max(0, min(p.rows, row0 + p.rows_per_cta) - row0);
     const int R = p.chunk_rows;
@@ -802,7 +818,7 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
     const Q8View a = carve_q8(after_ring, NB > 1 ? NB : p.n, p.cols, NB > 1);
     float *normbuf = reinterpret_cast<float *>(after_ring + q8_smem_bytes(NB > 1 ? NB : p.n, p.cols, NB > 1));
     float *res = normbuf + (p.norm != nullptr ? p.cols : 0);  // kQkv [NB][32]
-    // several vectors: partial sums [kWarps][kMats][32 lanes][4]
+    // several vectors: partial sums [kW][kMats][NT][32 lanes][4]
     float *part = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(res) + qkv_extra_bytes(MODE, NB));
     bool bad = false;
 
@@ -891,7 +907,7 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
         pdl_wait();  // x (and y, residual) belong to the kernels before
         bool qok;
         if constexpr (NB > 1) {
-            qok = quantize_activations_frag(p, p.x, p.n, a, a.red, normbuf, normbar);
+            qok = quantize_activations_frag<kW>(p, p.x, p.n, a, a.red, normbuf, normbar);
         } else {
             qok = quantize_activations(p, p.x, p.n, a, a.red, normbuf, normbar);
         }
@@ -992,7 +1008,7 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
             const int n_items = tiles * ks;
             const int g = lane >> 2, tq = lane & 3;
             float4 *part4 = reinterpret_cast<float4 *>(part);
-            for (int it = warp; it < n_items && !bad; it += kWarps) {
+            for (int it = warp; it < n_items && !bad; it += kW) {
                 const int tile = it / ks, slice = it - tile * ks;
                 const bool ok = mbar_wait_bounded(full_of(tile), full_parity(tile));
                 if (!__all_sync(0xffffffffu, ok)) {
@@ -1116,9 +1132,9 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
                 }
             }
             if (ks > 1) {
-                // tiles * ks <= kWarps: every item above was one warp's only one
-                consumer_sync();
-                for (int tile = warp; tile < tiles && !bad; tile += kWarps) {
+                // tiles * ks <= kW: every item above was one warp's only one
+                consumer_sync_w<kW>();
+                for (int tile = warp; tile < tiles && !bad; tile += kW) {
                     float t[kMats][NT][4];
 #pragma unroll
                     for (int k = 0; k < kMats; ++k)
@@ -1178,7 +1194,7 @@ __global__ void __launch_bounds__(kThreads + 32, NB > 1 && MODE != kQkv ? 1 : 2)
         __syncthreads();
         if (!bad) {
             const int dim0 = static_cast<int>(cl.block_rank()) * kQkvRows;
-            for (int i = tid; i < p.n * kQkvRows; i += kThreads + 32) {
+            for (int i = tid; i < p.n * kQkvRows; i += static_cast<int>(blockDim.x)) {
                 const int e = i / kQkvRows, r = i % kQkvRows;
                 if (r < nrows) {
                     float v = res[e * kQkvRows + r];
@@ -1346,7 +1362,8 @@ size_t gemv_smem(int mode, int nb, int n, int cols, int ring_bytes, bool has_nor
     size_t b = static_cast<size_t>(ring_bytes) + kBarBytes + q8_smem_bytes(frag ? nb : n, cols, frag) +
                (has_norm ? static_cast<size_t>(cols) * 4 : 0) + qkv_extra_bytes(mode, nb);
     if (frag && ksplit > 1) {  // partial sums of the split tiles
-        b += static_cast<size_t>(kWarps) * (mode == kSwiglu ? 2 : 1) * (nb / 8) * 32 * sizeof(float4);
+        b += static_cast<size_t>(consumer_warps(mode, nb)) * (mode == kSwiglu ? 2 : 1) * (nb / 8) * 32 *
+             sizeof(float4);
     }
     return b;
 }
@@ -1406,7 +1423,7 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(NB > 1 ? p.grid_ctas : (p.rows + p.rows_per_cta - 1) / p.rows_per_cta));
-    cfg.blockDim = dim3(kThreads + 32);  // kWarps consumer warps + one producer warp
+    cfg.blockDim = dim3(consumer_warps(MODE, NB) * 32 + 32);  // consumer warps + one producer warp
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -1518,7 +1535,7 @@ int max_clusters_of(int dev, int csize) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(static_cast<unsigned>(num_sms_of(dev)));
-        cfg.blockDim = dim3(kThreads + 32);
+        cfg.blockDim = dim3(consumer_warps(kPlain, kMaxVec) * 32 + 32);
         cfg.dynamicSmemBytes = static_cast<size_t>(smem);
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
@@ -1565,7 +1582,7 @@ bool plan_tiles(GemvParams &p, int mode, int dev, int nb) {
     if (tiles > kMaxTiles) return false;
     p.chunk_rows = kTileRows;
     p.stage_bytes = kTileRows * unit;
-    p.ksplit = std::max(1, std::min(kWarps / tiles, nsb / 2));
+    p.ksplit = std::max(1, std::min(consumer_warps(mode, nb) / tiles, nsb / 2));
     p.empty_count = p.ksplit;
     p.lanes_per_row = 1;
     const size_t fixed = gemv_smem(mode, nb, nb, p.cols, 0, p.norm != nullptr, p.ksplit);
