@@ -758,17 +758,18 @@ __device__ __forceinline__ void store_row(const GemvParams &p, float *res, int r
 // producer warp: the first stages before waiting for the previous kernel,
 // the rest as stages are released.  Dependents are released at once, so
 // consecutive projections overlap their weight streams with each other's
-// activation prologue and tail.  Each of the kWarps consumer warps owns whole
-// rows, 32 / p.lanes_per_row at a time; a lane's items are independent
-// dot products kept in four accumulators (the latency of one Q4_K x Q8_K
-// item is the limit at batch 1, not bandwidth); the row sum is a fixed-order
-// shuffle reduction (deterministic), and the row's stage slot is released by
-// one arrival on the stage's "empty" barrier -- no CTA-wide barrier in the
-// loop.  NB activation vectors: 1, or 8 / 16 with the products on the
-// tensor cores (mma m16n8k32, integer; NB / 8 n-tiles sharing each weight
-// fragment): stages of kTileRows rows, each tile of 16 rows x NB vectors
-// taken by p.ksplit warps over disjoint block ranges, whose partial sums
-// are added in a fixed order after one consumer barrier.
+// activation prologue and tail.
+//   NB = 1 (one vector, dp4a): each of the kWarps consumer warps owns whole
+// rows, 32 / p.lanes_per_row at a time; a lane's items are independent dot
+// products kept in four accumulators (the latency of one Q4_K x Q8_K item is
+// the limit at batch 1, not bandwidth); the row sum is a fixed-order shuffle
+// reduction (deterministic), and the row's stage slot is released by one
+// arrival on the stage's "empty" barrier -- no CTA-wide barrier in the loop.
+//   NB = 8 / 16 (tensor cores, mma m16n8k32 integer, NB / 8 n-tiles sharing
+// each weight fragment): consumer_warps(MODE, NB) consumer warps; the CTAs of
+// a cluster build one shared Q8_K image; stages of kTileRows rows, each tile
+// of 16 rows x NB vectors taken by p.ksplit warps over disjoint block ranges,
+// whose partial sums are added in a fixed order after one consumer barrier.
 template <int MODE, int NB>
 __global__ void __launch_bounds__(consumer_warps(MODE, NB) * 32 + 32, NB > 1 && MODE != kQkv ? 1 : 2)
     gemv_kernel(GemvParams p) {
