@@ -66,6 +66,8 @@ inline bool plan_cta_merge(int64_t n_segments, int64_t W) { return W >= 2 * kAtt
 // (a few long requests: one request near 32k positions +11%, the batch-1
 // backbone step +7%, measured against the in-launch merge), whose in-launch
 // merge would sit in the tail behind fences, tickets and a second level.
+// The combine launch for warp-partial plans too lost: 16 slots of 256-4096
+// positions -8%, 32 slots of 2k-16k -2.5%.
 constexpr int32_t kCombineMaxParts = 32;
 inline bool plan_combine(bool cta_merge, int32_t max_parts) {
     return cta_merge && max_parts > 1 && max_parts <= kCombineMaxParts;
