@@ -121,11 +121,15 @@ struct RopeView {
 };
 
 // Attention launch geometry (fixed per build; the -D overrides exist for
-// tuning sweeps).  Default: 6 warps per CTA, one CTA per SM, 2 stages each
-// (113 KB of shared memory): the best of the measured 4-12 warp x 1-6 stage
-// grid on both the 32-slot and the 16-slot decode workloads.
+// tuning sweeps).  Default: 8 warps per CTA, one CTA per SM, 2 stages each
+// (150 KB of shared memory): two warps on each of the SM's 4 schedulers.
+// With 6, warps 2 and 3 had a scheduler each while warps 0/4 and 1/5 shared
+// theirs, and per-warp timestamps showed the shared ones finishing ~1 us
+// later, every launch; 8 x 2 measured 16 slots of 256-4096 positions +3.3%,
+// one request near 32k positions +2.2%, 32 slots of 2k-16k +0.5%, the
+// batch-1 backbone step -1.2% against 6 x 2 (4 x 3-4: -12% to -22%).
 #ifndef HKV_ATTN_WARPS
-#define HKV_ATTN_WARPS 6
+#define HKV_ATTN_WARPS 8
 #endif
 #ifndef HKV_ATTN_STAGES
 #define HKV_ATTN_STAGES 2

@@ -35,7 +35,7 @@ from pathlib import Path
 import pytest
 
 REPO = Path(__file__).resolve().parents[1]
-WPC = 6  # warps per CTA (kAttnWarps)
+WPC = 8  # warps per CTA (kAttnWarps)
 UNIT, LEAVE_WHOLE, LEAVE_SHARED = 16, 32, 80
 
 
@@ -143,7 +143,7 @@ def n_groups_of(nparts):
     return 0 if nparts <= SINGLE_MAX else -(-nparts // group_size(nparts))
 
 
-def walk(plan_dump, npages, G=8, w_full=148 * 6):
+def walk(plan_dump, npages, G=8, w_full=148 * WPC):
     pos = [16 * np_ - 1 - (j % 16) for j, np_ in enumerate(npages)]  # np_ pages each
     got = plan_dump([(G, min(sum(npages) * G, w_full), pos)])[0]
     ref = restate(npages, G, w_full)
@@ -274,7 +274,7 @@ def test_plan_random_batches(plan_dump):
     rng = random.Random(0)
     for _ in range(40):
         walk(plan_dump, [rng.randint(1, 1025) for _ in range(rng.randint(1, 64))],
-             G=rng.choice([1, 2, 4, 8]), w_full=rng.choice([148 * 6, 37, 6]))
+             G=rng.choice([1, 2, 4, 8]), w_full=rng.choice([148 * WPC, 37, 6]))
 
 
 def test_shares_balance_segment_switches():
@@ -282,10 +282,10 @@ def test_shares_balance_segment_switches():
     # segments hold fewer units, and every share costs about the same
     rng = random.Random(2000)
     npages = [rng.randint(256, 4096) // 16 + 1 for _ in range(16)]
-    ref = restate(npages, 8, 148 * 6)
+    ref = restate(npages, 8, 148 * WPC)
     starts, U = ref["starts"], ref["U"]
     sizes = [starts[k + 1] - starts[k] for k in range(ref["shares"])]
-    assert ref["shares"] <= 148 * 6
+    assert ref["shares"] <= 148 * WPC
     assert max(sizes) == ref["B"] // UNIT
     assert min(sizes[:-1]) >= max(sizes) - LEAVE_SHARED // UNIT - 1
     assert sum(sizes) == U
@@ -294,7 +294,7 @@ def test_shares_balance_segment_switches():
 def test_cta_merge_rule():
     # long segments (one request near the context limit) merge per CTA;
     # many short ones (16 slots) keep one partial per warp
-    assert restate([2048], 8, 148 * 6)["cta_merge"]
-    assert restate([2048], 1, 148 * 6)["cta_merge"]
-    assert not restate([100] * 16, 8, 148 * 6)["cta_merge"]
-    assert not restate([600] * 32, 8, 148 * 6)["cta_merge"]
+    assert restate([2048], 8, 148 * WPC)["cta_merge"]
+    assert restate([2048], 1, 148 * WPC)["cta_merge"]
+    assert not restate([100] * 16, 8, 148 * WPC)["cta_merge"]
+    assert not restate([600] * 32, 8, 148 * WPC)["cta_merge"]
