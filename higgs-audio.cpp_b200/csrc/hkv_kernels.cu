@@ -830,10 +830,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
         // Publish the partial; the last of a group of partials merges the
         // group, and the last group (or the only one) produces the output.
-        __threadfence();
+        const int n_groups = merge_groups(nparts);
+        if (n_groups != 0) __threadfence();
         __syncwarp();
         const int j_part = part - p_first;
-        const int n_groups = merge_groups(nparts);
         const int n_seg = batch.n * G;  // segment counters come first, then group counters
         auto finish = [&](const Merged &res) {
             for (int r = 0; r < n_dst; ++r) {
@@ -849,13 +849,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
             signal_arrival(xchg, layer, lane);
         };
         if (n_groups == 0) {
+            // One acquire-release ticket instead of a fence on either side of
+            // a relaxed one: its release publishes the whole warp's partial
+            // (the lanes' stores are ordered before it by the warp barrier
+            // above), and for the last warp its acquire orders the merge's
+            // loads (after the barrier below) after every other warp's
+            // release.  16 slots of 256-4096 positions +1.2%.
             int ticket = 0;
             if (lane == 0) {
-                ticket = atomicAdd(counters + eh, 1);
+                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                             : "=r"(ticket)
+                             : "l"(counters + eh)
+                             : "memory");
             }
             ticket = __shfl_sync(0xffffffffu, ticket, 0);
+            __syncwarp();
             if (ticket == nparts - 1) {
-                __threadfence();
                 Merged res;
                 if (after_loop) {
                     merge_partials_wide(part_o, part_ml, p_first, nparts, lane, res);
