@@ -70,6 +70,8 @@ def test_encoder_round_trip(hkv_lib, oracle):
     (1000, 512, 16, False, True, False),    # 16 vectors in one launch, residual
     (130, 16384, 5, False, False, False),   # the widest rows, CTAs without rows
     (2560, 9728, 13, False, True, False),   # down: 8 + 5 vectors (two launches)
+    (2560, 4096, 17, False, True, False),   # o_proj: 16 + 1 vectors
+    (2560, 9728, 17, False, True, False),   # down: 8 + 8 + 1 vectors
 ])
 def test_gemv_matches_oracle(hkv_lib, oracle, rows, cols, n, use_norm, use_res, tc):
     import hkv
@@ -104,7 +106,7 @@ def test_gemv_in_place_residual(hkv_lib, oracle):
     assert rel_err(h.cpu().numpy(), ref) <= PROJ_TOL
 
 
-@pytest.mark.parametrize("n,tc", [(1, False), (2, False), (1, True), (8, False)])
+@pytest.mark.parametrize("n,tc", [(1, False), (2, False), (1, True), (8, False), (17, False)])
 def test_swiglu_matches_oracle(hkv_lib, oracle, n, tc):
     import hkv
     _, bg = q4k_matrix(hkv, 9728, 2560, 50)
