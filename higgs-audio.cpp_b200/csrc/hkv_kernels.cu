@@ -416,12 +416,28 @@ __device__ __forceinline__ void merge_partials(const float *part_o, const float 
 
 // The same merge with every load of kBatch partials issued before their
 // weighted sums (a merge is a chain of L2 round trips, so the batch size sets
-// its latency); the sums are taken in the same partial order.  Used for the
-// merges of a warp's last segment, after its main loop, where the registers
-// of the loop are free.
+// its latency); the sums are taken in the same partial order.  The first
+// batch of outputs goes out with the (m, l) loads, since the outputs do not
+// depend on the weights.  Used for the merges of a warp's last segment, after
+// its main loop, where the registers of the loop are free.
 __device__ __forceinline__ void merge_partials_wide(const float *part_o, const float *part_ml, int p0,
                                                int nparts, int lane, Merged &res) {
     constexpr int kBatch = 8;  // partial outputs in flight per lane
+    float4 ov[kBatch][kGqa];
+    auto load_batch = [&](int t0) {
+#pragma unroll
+        for (int t = 0; t < kBatch; ++t) {
+            if (t0 + t < nparts) {
+                const float4 *po = reinterpret_cast<const float4 *>(
+                    part_o + static_cast<int64_t>(p0 + t0 + t) * (kGqa * kHeadDim));
+#pragma unroll
+                for (int j = 0; j < kGqa; ++j) {
+                    ov[t][j] = __ldcg(po + j * (kHeadDim / 4) + lane);
+                }
+            }
+        }
+    };
+    load_batch(0);
     float mx[kGqa];
 #pragma unroll
     for (int j = 0; j < kGqa; ++j) {
@@ -479,18 +495,10 @@ __device__ __forceinline__ void merge_partials_wide(const float *part_o, const f
         }
         const int cnt = min(32, nparts - base);
         for (int t0 = 0; t0 < cnt; t0 += kBatch) {
-            // all loads of the batch first, then the weighted sums in order
-            float4 ov[kBatch][kGqa];
-#pragma unroll
-            for (int t = 0; t < kBatch; ++t) {
-                if (t0 + t < cnt) {
-                    const float4 *po = reinterpret_cast<const float4 *>(
-                        part_o + static_cast<int64_t>(p0 + base + t0 + t) * (kGqa * kHeadDim));
-#pragma unroll
-                    for (int j = 0; j < kGqa; ++j) {
-                        ov[t][j] = __ldcg(po + j * (kHeadDim / 4) + lane);
-                    }
-                }
+            // all loads of the batch first (the first batch is in flight
+            // already), then the weighted sums in order
+            if (base + t0 > 0) {
+                load_batch(base + t0);
             }
 #pragma unroll
             for (int t = 0; t < kBatch; ++t) {
@@ -1237,7 +1245,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 // partials the attention launch before it stored (segments held by one warp
 // or one CTA were written there).  Up to kCombineWarps warps each merge a
 // contiguous chunk of ceil(p / warps) partials -- eight loads in flight
-// before their sums -- leave (o, m, l) in shared memory, and warp 0 merges
+// before their sums, the first eight issued with the (m, l) loads -- leave
+// (o, m, l) in shared memory, and warp 0 merges
 // those in warp order: a fixed summation order, so results do not depend on
 // timing.  It waits for the attention grid (griddepcontrol.wait) and lets the
 // next launch in the stream be scheduled at once.  One head's 128 dims (a
@@ -1272,9 +1281,29 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
         const int p0 = sg.x + wid * chunk;
         const int cnt = min(chunk, nparts - wid * chunk);
         const float2 *mlp = reinterpret_cast<const float2 *>(part_ml) + j;  // (m, l) of head j
+        // this lane's float4 of head j in partial p0 + t
+        const float4 *pob = reinterpret_cast<const float4 *>(part_o + static_cast<int64_t>(p0) * (kGqa * kHeadDim) +
+                                                             j * kHeadDim) + lane;
+        float4 ov[kCombineBatch];
+        auto load_batch = [&](int t0) {
+#pragma unroll
+            for (int t = 0; t < kCombineBatch; ++t) {
+                if (t0 + t < cnt) {
+                    ov[t] = __ldcg(pob + static_cast<int64_t>(t0 + t) * (kGqa * kHeadDim / 4));
+                }
+            }
+        };
+        // the first batch of outputs goes out with the (m, l) loads: the
+        // outputs do not depend on the weights
+        load_batch(0);
         float mx = -INFINITY;
+        float2 own = make_float2(-INFINITY, 0.f);  // (m, l) of partial p0 + lane
         for (int b = lane; b < cnt; b += 32) {
-            mx = fmaxf(mx, __ldcg(mlp + static_cast<int64_t>(p0 + b) * kGqa).x);
+            const float2 ml = __ldcg(mlp + static_cast<int64_t>(p0 + b) * kGqa);
+            if (b == lane) {
+                own = ml;
+            }
+            mx = fmaxf(mx, ml.x);
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
@@ -1285,20 +1314,14 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
         for (int b = 0; b < cnt; b += 32) {
             float w = 0.f;
             if (b + lane < cnt) {
-                const float2 ml = __ldcg(mlp + static_cast<int64_t>(p0 + b + lane) * kGqa);
+                const float2 ml = b == 0 ? own : __ldcg(mlp + static_cast<int64_t>(p0 + b + lane) * kGqa);
                 w = exp2f(ml.x - mx);
                 den += w * ml.y;
             }
             const int cb = min(32, cnt - b);
             for (int t0 = 0; t0 < cb; t0 += kCombineBatch) {
-                float4 ov[kCombineBatch];
-#pragma unroll
-                for (int t = 0; t < kCombineBatch; ++t) {
-                    if (t0 + t < cb) {
-                        ov[t] = __ldcg(reinterpret_cast<const float4 *>(
-                                           part_o + static_cast<int64_t>(p0 + b + t0 + t) * (kGqa * kHeadDim) +
-                                           j * kHeadDim) + lane);
-                    }
+                if (b + t0 > 0) {
+                    load_batch(b + t0);
                 }
 #pragma unroll
                 for (int t = 0; t < kCombineBatch; ++t) {
