@@ -31,6 +31,9 @@ through the C ABI with q/k/v copied in from pinned host memory and the
 attention outputs copied back (one copy each way per 9 layers) every step;
 `roofline` of the attention kernel (live per-launch CUDA events); `cpu_baseline` = the reference's F32 GGML
 decode graph restated in C (oracle/hkv_oracle_graph.c) on a bounded sample.
+The default one-GPU run adds two short legs to its line: `headsplit` (one
+request near 32768 positions) and `batched16` (the batched16 workload, run as
+a child process on the same GPU and reported with its own roofline and e2e).
 """
 from __future__ import annotations
 
@@ -575,6 +578,11 @@ def bench_ours(args):
         if churn is not None:
             cpu["sample"] += "; slots do not churn in this sample"
 
+    batched = None
+    if rank == 0 and world == 1 and args.workload == "scaleout" and not args.no_batched16:
+        torch.cuda.empty_cache()
+        batched = batched16_leg()
+
     if rank == 0:
         groups_all, desc_all = workload_all(args.workload, world, args.prefix)
         traffic = None
@@ -617,11 +625,33 @@ def bench_ours(args):
             "cpu_baseline": cpu,
             "clocks": clk,
             "headsplit": split,
+            "batched16": batched,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def batched16_leg(steps: int = 20, warmup: int = 3, e2e_steps: int = 10) -> dict:
+    """The batched16 workload (16 slots, contexts U[256, 4096]) as a child
+    process on this GPU, with the same timing rules as the main run; returns
+    the figures of its JSON line (or why it failed)."""
+    import subprocess
+
+    cmd = [sys.executable, str(REPO / "bench.py"), "--workload", "batched16", "--steps", str(steps),
+           "--warmup", str(warmup), "--e2e-steps", str(e2e_steps), "--no-cpu-baseline",
+           "--no-headsplit", "--no-batched16"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"failed": f"exit {r.returncode}: {r.stderr.strip().splitlines()[-1:]}"}
+    d = json.loads(lines[-1])
+    return {"value": d["value"], "unit": d["unit"], "steps": d["steps"], "warmup": d["warmup"],
+            "ms_per_step": d["ms_per_step"], "config": d["config"],
+            "roofline_frac": d["roofline"]["frac"], "roofline_achieved": d["roofline"]["achieved"],
+            "e2e_value": (d["e2e"] or {}).get("value"), "clocks": d["clocks"],
+            "gpu_launches": d["gpu_launches"], "command": " ".join(cmd[1:])}
 
 
 def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, warmup: int):
@@ -1232,6 +1262,8 @@ def main():
                     help="e2e: layers per host<->device copy (and per event wait)")
     ap.add_argument("--no-headsplit", action="store_true",
                     help="skip the KV-head split leg that follows the slot-sharded measurement")
+    ap.add_argument("--no-batched16", action="store_true",
+                    help="skip the batched16 leg that the default one-GPU run adds")
     ap.add_argument("--prefix", type=int, default=768,
                     help="churn: shared prefix length (770 puts the first append of every "
                          "replacement slot into a shared partial page: copy-on-write)")
