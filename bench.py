@@ -651,7 +651,7 @@ def batched16_leg(steps: int = 20, warmup: int = 3, e2e_steps: int = 10) -> dict
             "ms_per_step": d["ms_per_step"], "config": d["config"],
             "roofline_frac": d["roofline"]["frac"], "roofline_achieved": d["roofline"]["achieved"],
             "e2e_value": (d["e2e"] or {}).get("value"), "clocks": d["clocks"],
-            "gpu_launches": d["gpu_launches"], "command": " ".join(cmd[1:])}
+            "gpu_launches": d["gpu_launches"], "command": "python bench.py " + " ".join(cmd[2:])}
 
 
 def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, warmup: int):
