@@ -67,7 +67,12 @@ inline bool plan_cta_merge(int64_t n_segments, int64_t W) { return W >= 2 * kAtt
 // backbone step +7%, measured against the in-launch merge), whose in-launch
 // merge would sit in the tail behind fences, tickets and a second level.
 // The combine launch for warp-partial plans too lost: 16 slots of 256-4096
-// positions -8%, 32 slots of 2k-16k -2.5%.
+// positions -8%, 32 slots of 2k-16k -2.5%.  So did the combine launch for
+// segments of up to 256 CTA partials (one request near 32k positions split
+// by KV head, one or two KV heads per GPU: -22% / -12%), whose four or eight
+// combine CTAs read every partial with little parallelism, and plans of at
+// least 4 units per warp (-1.5% on one KV head of that request, -6% on the
+// batch-1 backbone step).
 constexpr int32_t kCombineMaxParts = 32;
 inline bool plan_combine(bool cta_merge, int32_t max_parts) {
     return cta_merge && max_parts > 1 && max_parts <= kCombineMaxParts;
