@@ -31,9 +31,10 @@ through the C ABI with q/k/v copied in from pinned host memory and the
 attention outputs copied back (one copy each way per 9 layers) every step;
 `roofline` of the attention kernel (live per-launch CUDA events); `cpu_baseline` = the reference's F32 GGML
 decode graph restated in C (oracle/hkv_oracle_graph.c) on a bounded sample.
-The default one-GPU run adds two short legs to its line: `headsplit` (one
-request near 32768 positions) and `batched16` (the batched16 workload, run as
-a child process on the same GPU and reported with its own roofline and e2e).
+The default one-GPU run adds short legs to its line: `headsplit` (one
+request near 32768 positions), and `batched16`, `backbone_batch1` and
+`backbone_batch16` (those workloads run as child processes on the same GPU,
+each reported with its own roofline, e2e and clocks).
 """
 from __future__ import annotations
 
@@ -578,10 +579,11 @@ def bench_ours(args):
         if churn is not None:
             cpu["sample"] += "; slots do not churn in this sample"
 
-    batched = None
-    if rank == 0 and world == 1 and args.workload == "scaleout" and not args.no_batched16:
+    legs = {}
+    if rank == 0 and world == 1 and args.workload == "scaleout" and not args.no_extra_legs:
         torch.cuda.empty_cache()
-        batched = batched16_leg()
+        for name, argv in EXTRA_LEGS.items():
+            legs[name] = child_leg(argv + ["--no-cpu-baseline", "--no-headsplit", "--no-extra-legs"])
 
     if rank == 0:
         groups_all, desc_all = workload_all(args.workload, world, args.prefix)
@@ -625,7 +627,7 @@ def bench_ours(args):
             "cpu_baseline": cpu,
             "clocks": clk,
             "headsplit": split,
-            "batched16": batched,
+            **legs,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -633,25 +635,33 @@ def bench_ours(args):
         dist.destroy_process_group()
 
 
-def batched16_leg(steps: int = 20, warmup: int = 3, e2e_steps: int = 10) -> dict:
-    """The batched16 workload (16 slots, contexts U[256, 4096]) as a child
-    process on this GPU, with the same timing rules as the main run; returns
-    the figures of its JSON line (or why it failed)."""
+def child_leg(argv: list, timeout_s: int = 600) -> dict:
+    """One more workload as a child process on this GPU (`python bench.py
+    <argv>`), with the same timing rules as the main run; returns the figures
+    of its JSON line (or why it failed)."""
     import subprocess
 
-    cmd = [sys.executable, str(REPO / "bench.py"), "--workload", "batched16", "--steps", str(steps),
-           "--warmup", str(warmup), "--e2e-steps", str(e2e_steps), "--no-cpu-baseline",
-           "--no-headsplit", "--no-batched16"]
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    cmd = [sys.executable, str(REPO / "bench.py")] + argv
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s)
     lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
     if r.returncode != 0 or not lines:
         return {"failed": f"exit {r.returncode}: {r.stderr.strip().splitlines()[-1:]}"}
     d = json.loads(lines[-1])
     return {"value": d["value"], "unit": d["unit"], "steps": d["steps"], "warmup": d["warmup"],
-            "ms_per_step": d["ms_per_step"], "config": d["config"],
+            "ms_per_step": d["ms_per_step"], "config": d["config"], "dtype": d["dtype"],
             "roofline_frac": d["roofline"]["frac"], "roofline_achieved": d["roofline"]["achieved"],
             "e2e_value": (d["e2e"] or {}).get("value"), "clocks": d["clocks"],
-            "gpu_launches": d["gpu_launches"], "command": "python bench.py " + " ".join(cmd[2:])}
+            "gpu_launches": d["gpu_launches"], "command": "python bench.py " + " ".join(argv)}
+
+
+# Legs the default one-GPU run adds to its line: the small-batch attention
+# workload and the whole backbone decode step at batch 1 and 16.
+EXTRA_LEGS = {
+    "batched16": ["--workload", "batched16", "--steps", "20", "--warmup", "3", "--e2e-steps", "10"],
+    "backbone_batch1": ["--workload", "backbone", "--steps", "60", "--warmup", "5", "--e2e-steps", "10"],
+    "backbone_batch16": ["--workload", "backbone", "--batch", "16", "--steps", "60", "--warmup", "5",
+                         "--e2e-steps", "10"],
+}
 
 
 def headsplit_run(args, dist, rank: int, world: int, local: int, steps: int, warmup: int):
@@ -1262,8 +1272,8 @@ def main():
                     help="e2e: layers per host<->device copy (and per event wait)")
     ap.add_argument("--no-headsplit", action="store_true",
                     help="skip the KV-head split leg that follows the slot-sharded measurement")
-    ap.add_argument("--no-batched16", action="store_true",
-                    help="skip the batched16 leg that the default one-GPU run adds")
+    ap.add_argument("--no-extra-legs", action="store_true",
+                    help="skip the batched16 and backbone legs that the default one-GPU run adds")
     ap.add_argument("--prefix", type=int, default=768,
                     help="churn: shared prefix length (770 puts the first append of every "
                          "replacement slot into a shared partial page: copy-on-write)")
