@@ -655,7 +655,17 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
         return fail(eng, HKV_ERR_RANGE, "batch too large (%lld units)",
                     static_cast<long long>(total_pages * G));
     }
-    const int32_t W = plan_warps(total_pages * G, static_cast<int64_t>(eng->num_sms) * kAttnWarps);
+    const int64_t max_warps = static_cast<int64_t>(eng->num_sms) * kAttnWarps;
+    // One long request: one thread-block cluster per KV head (plan_cluster).
+    int32_t C = 0;
+    if (n == 1) {
+        int32_t fit[5] = {0, 0, 0, 0, 0};
+        for (int i = 1; i < 5; ++i) {
+            fit[i] = attention_cluster_fit(1 << i);
+        }
+        C = plan_cluster(n, G, total_pages, max_warps, fit);
+    }
+    const int32_t W = C > 0 ? G * C * kAttnWarps : plan_warps(total_pages * G, max_warps);
     const size_t words = plan_words(n, G, total_pages, W);
     if (bc.consumed) {
         HKV_CUDA_TRY(eng, eng->batch_stage.mark_used(bc.consumer_stream));
@@ -664,7 +674,8 @@ int ensure_batch(hkv_engine *eng, int32_t n, const int32_t *slots, cudaStream_t 
     void *host = nullptr;
     HKV_CUDA_TRY(eng, eng->batch_stage.begin(words * sizeof(int32_t), &host));
     const PlanSummary plan =
-        build_plan(static_cast<int32_t *>(host), n, G, pos.data(), lists.data(), total_pages, W);
+        C > 0 ? build_cluster_plan(static_cast<int32_t *>(host), G, pos[0], lists[0], C)
+              : build_plan(static_cast<int32_t *>(host), n, G, pos.data(), lists.data(), total_pages, W);
     if (static_cast<int64_t>(plan.n_parts) + plan.n_groups > eng->part_cap) {
         return fail(eng, HKV_ERR_OOM, "split plan needs %d partials, capacity %lld",
                     plan.n_parts + plan.n_groups, static_cast<long long>(eng->part_cap));

@@ -69,6 +69,9 @@ struct BatchView {
     int32_t split_segments;   // segments with more than one partial
     int32_t combine;          // 1: split partials are only stored; the combine launch
                               // that follows merges them (plan_combine)
+    int32_t cluster;          // > 0: CTAs per thread-block cluster; cluster k holds segment
+                              // k, whose CTA partials meet in the shared memory of the
+                              // cluster's first CTA (plan_cluster); 0: no clusters
 };
 
 // Partials of one (entry, KV head) are merged by one warp when there are at
@@ -174,6 +177,10 @@ void launch_cow_copy(const PoolView &pool, const int32_t *pairs, int32_t n_pairs
 void launch_gather(const PoolView &pool, const int32_t *slot_pages, int64_t pos0, int64_t n,
                    int layer, uint16_t *k_out, uint16_t *v_out, DeviceError *err,
                    cudaStream_t stream);
-size_t attention_smem_bytes(bool cta_merge);
+size_t attention_smem_bytes(bool cta_merge, bool cluster = false);
+// Clusters of csize attention CTAs (2..16, the cluster-merge variant) that
+// can be resident at once on the current device; 0 if none (cached per
+// device).
+int attention_cluster_fit(int csize);
 
 }  // namespace hkv

@@ -30,6 +30,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "hkv_device.cuh"
 #include "hkv_internal.h"
 
@@ -49,6 +51,10 @@ constexpr int kWarpSmem = kAttnStages * kStageBytes + kQcBytes + kPBufBytes + kB
 constexpr int kCtaPartFloats = kGqa * kHeadDim + 2 * kGqa;
 constexpr int kCtaPartBytes = kCtaPartFloats * 4;
 constexpr int kCtaSmem = kAttnWarps * 2 * kCtaPartBytes + 32;
+// Cluster merge (plan_cluster): one partial slot per CTA of the cluster, used
+// in the cluster's first CTA, then the mbarrier that counts the filled slots.
+constexpr int kMaxCluster = 16;
+constexpr int kClusterSmem = kMaxCluster * kCtaPartBytes + 16;
 constexpr int kWhereAppend = 0;
 constexpr int kWhereAttn = 1;
 constexpr int kWhereGather = 3;
@@ -57,7 +63,8 @@ constexpr int kWhereSplitWait = 5;
 
 static_assert(kWarpSmem % 16 == 0, "per-warp shared region must keep 16-byte alignment");
 static_assert(kBarBytes >= 8 * kAttnStages, "every stage needs its mbarrier inside the warp's region");
-static_assert(kAttnWarps * kWarpSmem + kCtaSmem <= 227 * 1024, "attention CTA exceeds shared memory");
+static_assert(kAttnWarps * kWarpSmem + kCtaSmem + kClusterSmem <= 227 * 1024,
+              "attention CTA exceeds shared memory");
 static_assert(kCtaPartBytes % 16 == 0, "CTA partial slots must keep 16-byte alignment");
 static_assert(kAttnWarps <= 8, "one run ticket per warp in 32 bytes");
 
@@ -118,6 +125,51 @@ __device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
 }
 __device__ __forceinline__ void st_shared_f32x2(uint32_t addr, float a, float b) {
     asm volatile("st.shared.v2.f32 [%0], {%1,%2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+
+// ------------------------------------------------ thread-block cluster
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f32x4(uint32_t addr, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void st_cluster_f32x2(uint32_t addr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1,%2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
+// Arrival on an mbarrier of another CTA of the cluster (release: this
+// thread's earlier cluster stores are visible to whoever completes the wait).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// True when the phase with `parity` completed within the budget.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            return false;
+        }
+    }
+    return true;
 }
 __device__ __forceinline__ void st_shared_f32x4(uint32_t addr, float4 v) {
     asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
@@ -530,10 +582,9 @@ __device__ __forceinline__ void merge_partials_wide(const float *part_o, const f
     }
 }
 
-// Merge of the m partials a run of warps left in shared memory (slot of warp
-// k: 1 for the run's first warp, 0 for the others), in warp order.
-__device__ __forceinline__ void merge_cta(const float *slots, int w0, int m, int lane, Merged &res) {
-    auto base = [&](int k) { return slots + (2 * (w0 + k) + (k == 0 ? 1 : 0)) * kCtaPartFloats; };
+// Merge of m partials in shared memory, partial k at base(k), in order k.
+template <class Base>
+__device__ __forceinline__ void merge_smem_partials(Base base, int m, int lane, Merged &res) {
     float mx[kGqa];
 #pragma unroll
     for (int j = 0; j < kGqa; ++j) {
@@ -566,6 +617,18 @@ __device__ __forceinline__ void merge_cta(const float *slots, int w0, int m, int
             res.o[j].w += w * ov.w;
         }
     }
+}
+
+// The m partials a run of warps left in its CTA's slots (slot of warp k: 1
+// for the run's first warp, 0 for the others), in warp order.
+__device__ __forceinline__ void merge_cta(const float *slots, int w0, int m, int lane, Merged &res) {
+    merge_smem_partials([&](int k) { return slots + (2 * (w0 + k) + (k == 0 ? 1 : 0)) * kCtaPartFloats; },
+                        m, lane, res);
+}
+
+// The C CTA partials of a cluster, slot k from the CTA of rank k, in rank order.
+__device__ __forceinline__ void merge_cluster(const float *slots, int m, int lane, Merged &res) {
+    merge_smem_partials([&](int k) { return slots + k * kCtaPartFloats; }, m, lane, res);
 }
 
 __device__ __forceinline__ float4 normalised(const Merged &r, int j) {
@@ -601,7 +664,9 @@ __device__ __forceinline__ void signal_arrival(const Exchange &x, int layer, int
     }
 }
 
-template <bool kAppend, bool kCtaMerge>
+// kCluster (with kCtaMerge): the launch is in clusters of batch.cluster CTAs,
+// one (slot, KV head) segment per cluster (plan_cluster).
+template <bool kAppend, bool kCtaMerge, bool kCluster>
 __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     attention_kernel(PoolView pool, RopeView rope, BatchView batch, int layer,
                      const float *__restrict__ q, const float *__restrict__ k_new,
@@ -614,13 +679,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
     const int gw = blockIdx.x * kAttnWarps + wid;
     const int G = pool.n_head_kv;
     const int W = batch.n_warps;
+    static_assert(kCtaMerge || !kCluster, "the cluster merge starts from the CTA merge");
     float *cta_slots = reinterpret_cast<float *>(smem + kAttnWarps * kWarpSmem);
     int *run_ticket = reinterpret_cast<int *>(smem + kAttnWarps * kWarpSmem + kAttnWarps * 2 * kCtaPartBytes);
+    float *cl_slots = reinterpret_cast<float *>(smem + kAttnWarps * kWarpSmem + kCtaSmem);
+    const uint32_t cl_bar = smem_u32(smem + kAttnWarps * kWarpSmem + kCtaSmem + kMaxCluster * kCtaPartBytes);
     if (kCtaMerge) {
         if (threadIdx.x < kAttnWarps) {
             run_ticket[threadIdx.x] = 0;
         }
+        if (kCluster && threadIdx.x == 0) {
+            mbar_init(cl_bar, static_cast<uint32_t>(batch.cluster));  // used in the first CTA
+            fence_barrier_init();
+        }
         __syncthreads();  // the only CTA barrier: before any warp can leave
+        if (kCluster) {
+            // Every thread arrives before it can leave; a CTA's last warp waits
+            // (barrier.cluster.wait) before its first store into another CTA,
+            // so that CTA's barrier is initialised by then.
+            cluster_arrive();
+        }
     }
     if (gw >= W) {
         return;
@@ -811,6 +889,49 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 #pragma unroll
                     for (int j = 0; j < kGqa; ++j) {
                         ob[j * (kHeadDim / 4) + lane] = normalised(cres, j);
+                    }
+                }
+                signal_arrival(xchg, layer, lane);
+                return;
+            }
+            if (kCluster) {
+                // The CTA's partial goes to slot `rank` in the cluster's first
+                // CTA, whose last warp merges the slots in rank order once all
+                // have arrived on its barrier, and writes the output.
+                const int rank = part - p_first;  // = the CTA's rank in its cluster
+                cluster_wait();
+                const uint32_t slot = cluster_map(smem_u32(cl_slots + rank * kCtaPartFloats), 0);
+#pragma unroll
+                for (int j = 0; j < kGqa; ++j) {
+                    st_cluster_f32x4(slot + (j * kHeadDim + 4 * lane) * 4, cres.o[j]);
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int j = 0; j < kGqa; ++j) {
+                        st_cluster_f32x2(slot + (kGqa * kHeadDim + 2 * j) * 4, cres.m[j], cres.l[j]);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                    mbar_arrive_remote(cluster_map(cl_bar, 0));
+                }
+                if (rank != 0) {
+                    return;
+                }
+                if (!__all_sync(0xffffffffu, mbar_wait_cluster_bounded(cl_bar, 0))) {
+                    if (lane == 0) {
+                        record_error(err, kErrTimeout, kWhereAttn, seg_h, blockIdx.x);
+                    }
+                    return;
+                }
+                Merged res;
+                merge_cluster(cl_slots, nparts, lane, res);
+                for (int r = 0; r < n_dst; ++r) {
+                    float4 *ob = reinterpret_cast<float4 *>(out_slice(out, xchg, r, layer, seg_e, seg_h, G));
+#pragma unroll
+                    for (int j = 0; j < kGqa; ++j) {
+                        ob[j * (kHeadDim / 4) + lane] = normalised(res, j);
                     }
                 }
                 signal_arrival(xchg, layer, lane);
@@ -1440,8 +1561,63 @@ __global__ void gather_kernel(PoolView pool, const int32_t *__restrict__ slot_pa
 
 }  // namespace
 
-size_t attention_smem_bytes(bool cta_merge) {
-    return static_cast<size_t>(kAttnWarps) * kWarpSmem + (cta_merge ? kCtaSmem : 0);
+size_t attention_smem_bytes(bool cta_merge, bool cluster) {
+    return static_cast<size_t>(kAttnWarps) * kWarpSmem + (cta_merge ? kCtaSmem : 0) +
+           (cluster ? kClusterSmem : 0);
+}
+
+// The shared-memory opt-in (and, for the cluster variant, sizes up to 16) of
+// one attention kernel, once per device.
+template <bool kAppend, bool kCtaMerge, bool kCluster>
+void configure_attention(int dev) {
+    static bool configured[64] = {};
+    if (dev >= 0 && dev < 64 && configured[dev]) {
+        return;
+    }
+    auto kern = attention_kernel<kAppend, kCtaMerge, kCluster>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(attention_smem_bytes(kCtaMerge, kCluster)));
+    if (kCluster) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    }
+    if (dev >= 0 && dev < 64) {
+        configured[dev] = true;
+    }
+}
+
+int attention_cluster_fit(int csize) {
+    static std::mutex mu;
+    static int cache[64][kMaxCluster + 1] = {};
+    if (csize < 2 || csize > kMaxCluster) {
+        return 0;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        return 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[dev][csize] != 0) {
+        return cache[dev][csize] > 0 ? cache[dev][csize] : 0;
+    }
+    configure_attention<true, true, true>(dev);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(csize));
+    cfg.blockDim = dim3(kAttnWarps * 32);
+    cfg.dynamicSmemBytes = attention_smem_bytes(true, true);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(csize);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attention_kernel<true, true, true>, &cfg) != cudaSuccess) {
+        n = 0;
+    }
+    (void)cudaGetLastError();
+    cache[dev][csize] = n > 0 ? n : -1;
+    return n > 0 ? n : 0;
 }
 
 void launch_append(const PoolView &pool, const RopeView &rope, const BatchView &batch, int layer,
@@ -1473,36 +1649,39 @@ void launch_append_range(const PoolView &pool, const RopeView &rope, const int32
     }
 }
 
-template <bool kAppend, bool kCtaMerge>
+template <bool kAppend, bool kCtaMerge, bool kCluster>
 void launch_attention_t(const PoolView &pool, const RopeView &rope, const BatchView &batch,
                         int layer, const float *q, const float *k_new, const float *v_new,
                         float *part_o, float *part_ml, int32_t *counters, float *out,
                         const Exchange &xchg, float scale_log2, DeviceError *err,
                         bool overlap_previous, cudaStream_t stream) {
-    // The dynamic shared-memory opt-in is per device and per kernel.
-    static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaFuncSetAttribute(attention_kernel<kAppend, kCtaMerge>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(attention_smem_bytes(kCtaMerge)));
-        if (dev >= 0 && dev < 64) {
-            configured[dev] = true;
-        }
-    }
+    configure_attention<kAppend, kCtaMerge, kCluster>(dev);
     const int grid = (batch.n_warps + kAttnWarps - 1) / kAttnWarps;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
     cfg.blockDim = dim3(kAttnWarps * 32);
-    cfg.dynamicSmemBytes = attention_smem_bytes(kCtaMerge);
+    cfg.dynamicSmemBytes = attention_smem_bytes(kCtaMerge, kCluster);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int n_attr = 0;
+    if (overlap_previous) {
+        attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+        ++n_attr;
+    }
+    if (kCluster) {
+        attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+        attr[n_attr].val.clusterDim.x = static_cast<unsigned>(batch.cluster);
+        attr[n_attr].val.clusterDim.y = 1;
+        attr[n_attr].val.clusterDim.z = 1;
+        ++n_attr;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = overlap_previous ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, attention_kernel<kAppend, kCtaMerge>, pool, rope, batch, layer, q, k_new,
-                       v_new, part_o, part_ml, counters, out, xchg, scale_log2, err);
+    cfg.numAttrs = static_cast<unsigned>(n_attr);
+    cudaLaunchKernelEx(&cfg, attention_kernel<kAppend, kCtaMerge, kCluster>, pool, rope, batch, layer, q,
+                       k_new, v_new, part_o, part_ml, counters, out, xchg, scale_log2, err);
     if (batch.combine && batch.split_segments > 0) {
         cudaLaunchConfig_t cc = {};
         cc.gridDim = dim3(static_cast<unsigned>(batch.n * pool.n_head_kv * kGqa));
@@ -1525,18 +1704,24 @@ void launch_attention(const PoolView &pool, const RopeView &rope, const BatchVie
     if (!append) {
         k_new = v_new = nullptr;
     }
-    if (append && batch.cta_merge) {
-        launch_attention_t<true, true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
-                                       counters, out, xchg, scale_log2, err, overlap_previous, stream);
+    if (append && batch.cluster > 0) {
+        launch_attention_t<true, true, true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                             counters, out, xchg, scale_log2, err, overlap_previous, stream);
+    } else if (append && batch.cta_merge) {
+        launch_attention_t<true, true, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                              counters, out, xchg, scale_log2, err, overlap_previous, stream);
     } else if (append) {
-        launch_attention_t<true, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
-                                        counters, out, xchg, scale_log2, err, overlap_previous, stream);
+        launch_attention_t<true, false, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                               counters, out, xchg, scale_log2, err, overlap_previous, stream);
+    } else if (batch.cluster > 0) {
+        launch_attention_t<false, true, true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                              counters, out, xchg, scale_log2, err, overlap_previous, stream);
     } else if (batch.cta_merge) {
-        launch_attention_t<false, true>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
-                                        counters, out, xchg, scale_log2, err, overlap_previous, stream);
+        launch_attention_t<false, true, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                               counters, out, xchg, scale_log2, err, overlap_previous, stream);
     } else {
-        launch_attention_t<false, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
-                                         counters, out, xchg, scale_log2, err, overlap_previous, stream);
+        launch_attention_t<false, false, false>(pool, rope, batch, layer, q, k_new, v_new, part_o, part_ml,
+                                                counters, out, xchg, scale_log2, err, overlap_previous, stream);
     }
 }
 

@@ -19,6 +19,12 @@
 // CTA (kAttnWarps consecutive warps) merge theirs in shared memory first and
 // the segment has one partial per CTA it spans.
 //
+// One long request (plan_cluster): each KV head's segment gets a cluster of C
+// thread-block CTAs (8C warps, the pages split evenly), the warps of a CTA
+// merge in shared memory, and the C CTA partials meet in the first CTA's
+// shared memory (distributed shared memory), which writes the output: no
+// combine launch and no global ticket.
+//
 // A segment with more than kMergeSingleMax partials is merged in two levels:
 // groups of merge_group_size() partials are merged by the last warp of each
 // group into one "group partial", and the last group merges those.
@@ -139,6 +145,32 @@ inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
                                (n * G + 1) + total_pages);
 }
 
+// Thread-block clusters for a batch of one entry (one long request, or the
+// batch-1 decode step): the largest C of 16, 8, 4, 2 CTAs per cluster such
+// that every KV head's cluster runs at once (fit[i] = clusters of 2^i CTAs
+// that can be resident together), every warp gets at least one page, and the
+// G * C CTAs are at least 3/4 of the warps the stream-K plan would use;
+// and only where that plan would pre-merge per CTA (long segments).  0: no
+// clusters (the stream-K plan).
+inline int32_t plan_cluster(int32_t n, int32_t G, int64_t npages, int64_t max_warps,
+                            const int32_t (&fit)[5]) {
+    if (n != 1 || G <= 0) {
+        return 0;
+    }
+    const int64_t w_default = plan_warps(npages * G, max_warps);
+    if (!plan_cta_merge(G, w_default)) {
+        return 0;
+    }
+    for (int i = 4; i >= 1; --i) {
+        const int64_t C = int64_t{1} << i;
+        const int64_t warps = G * C * kAttnWarps;
+        if (warps <= max_warps && fit[i] >= G && npages >= C * kAttnWarps && 4 * warps >= 3 * w_default) {
+            return static_cast<int32_t>(C);
+        }
+    }
+    return 0;
+}
+
 struct PlanSummary {
     int64_t total_pages = 0;
     int64_t total_units = 0;
@@ -150,77 +182,64 @@ struct PlanSummary {
     bool combine = false;        // split partials merged by the combine launch (plan_combine)
     int64_t budget = 0;    // the cost bound B of every share
     bool cta_merge = false;
+    int32_t cluster = 0;   // CTAs per cluster (plan_cluster), 0: none
 };
 
-// Fills `w` (plan_words(...) words, 16-byte aligned).  page_lists[e] points
-// at slot e's page ids, at least pos[e] / 16 + 1 of them.
-inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *pos_in,
-                              const int32_t *const *page_lists, int64_t total_pages, int32_t W) {
-    PlanSummary s;
-    s.total_pages = total_pages;
-    s.total_units = total_pages * G;
-    s.cta_merge = plan_cta_merge(static_cast<int64_t>(n) * G, W);
-    const int64_t U = s.total_units;
+
+// Descriptor arrays inside `w` (the layout at the top of this file).
+struct PlanArrays {
+    int32_t *warp_start, *seg, *pos, *ntok, *npg, *page_off, *unit_off, *part2_off, *pages;
+};
+
+// Lays the arrays out in `w` and fills the per-entry ones (positions, page
+// counts, prefix sums, page lists).
+inline PlanArrays plan_arrays(int32_t *w, int32_t n, int32_t G, const int32_t *pos_in,
+                              const int32_t *const *page_lists, int32_t W) {
     const int64_t S = static_cast<int64_t>(n) * G;
-    const int64_t span = s.cta_merge ? kAttnWarps : 1;  // warps per partial
-    int32_t *warp_start = w;
-    int32_t *seg = warp_start + kWarpStartWords * W;
-    int32_t *pos = seg + kSegWords * S;
-    int32_t *ntok = pos + n;
-    int32_t *npg = ntok + n;
-    int32_t *page_off = npg + n;
-    int32_t *unit_off = page_off + (n + 1);
-    int32_t *part2_off = unit_off + (n + 1);
-    int32_t *pages = part2_off + (S + 1);
-    page_off[0] = unit_off[0] = part2_off[0] = 0;
+    PlanArrays a;
+    a.warp_start = w;
+    a.seg = a.warp_start + kWarpStartWords * W;
+    a.pos = a.seg + kSegWords * S;
+    a.ntok = a.pos + n;
+    a.npg = a.ntok + n;
+    a.page_off = a.npg + n;
+    a.unit_off = a.page_off + (n + 1);
+    a.part2_off = a.unit_off + (n + 1);
+    a.pages = a.part2_off + (S + 1);
+    a.page_off[0] = a.unit_off[0] = a.part2_off[0] = 0;
     for (int32_t e = 0; e < n; ++e) {
         const int32_t np = pos_in[e] / kPageTokens + 1;
-        pos[e] = pos_in[e];
-        ntok[e] = pos_in[e] + 1;
-        npg[e] = np;
-        std::memcpy(pages + page_off[e], page_lists[e], static_cast<size_t>(np) * sizeof(int32_t));
-        page_off[e + 1] = page_off[e] + np;
-        unit_off[e + 1] = unit_off[e] + np * G;
+        a.pos[e] = pos_in[e];
+        a.ntok[e] = pos_in[e] + 1;
+        a.npg[e] = np;
+        std::memcpy(a.pages + a.page_off[e], page_lists[e], static_cast<size_t>(np) * sizeof(int32_t));
+        a.page_off[e + 1] = a.page_off[e] + np;
+        a.unit_off[e + 1] = a.unit_off[e] + np * G;
     }
+    return a;
+}
 
-    // ---- shares: the smallest budget that fits W warps (bisection)
-    const int64_t per = (U + W - 1) / W;
-    int64_t bad = kCostUnit * per - 1;  // W shares of fewer than per units cannot hold U
-    int64_t good = kCostUnit * per + kCostLeaveShared * (S + 1);
-    while (plan_cut(npg, G, S, good, W, nullptr) > W) {
-        good *= 2;
-    }
-    while (good - bad > 1) {
-        const int64_t mid = bad + (good - bad) / 2;
-        if (plan_cut(npg, G, S, mid, W, nullptr) > W) {
-            bad = mid;
-        } else {
-            good = mid;
-        }
-    }
-    s.budget = good;
-    // share starts go to word 8 of each record; the loop below fills the rest
-    std::vector<int32_t> starts(static_cast<size_t>(W) + 1);
-    s.shares = static_cast<int32_t>(plan_cut(npg, G, S, good, W, starts.data()));
-    for (int64_t k = s.shares; k <= W; ++k) {
-        starts[k] = static_cast<int32_t>(U);
-    }
-
+// The segment and per-warp records of a plan whose shares are known:
+// warp k holds units [starts[k], starts[k + 1]), starts[W] = U; span warps
+// share one partial.
+inline void fill_records(const PlanArrays &a, int32_t n, int32_t G, int32_t W,
+                         const int32_t *starts, int64_t span, PlanSummary &s) {
+    const int64_t S = static_cast<int64_t>(n) * G;
     // ---- segments: warps first .. last, partials
     int32_t parts = 0;
-    int32_t k = 0;  // the share holding unit a
+    int32_t k = 0;  // the share holding unit u
     for (int64_t sg = 0; sg < S; ++sg) {
         const int32_t e = static_cast<int32_t>(sg / G);
-        const int64_t a = unit_off[e] + (sg % G) * npg[e];
-        while (starts[k + 1] <= a) {
+        const int64_t u = a.unit_off[e] + (sg % G) * a.npg[e];
+        while (starts[k + 1] <= u) {
             ++k;
         }
         int32_t last = k;
-        while (starts[last + 1] <= a + npg[e] - 1) {
+        while (starts[last + 1] <= u + a.npg[e] - 1) {
             ++last;
         }
         const int32_t np_parts = static_cast<int32_t>(last / span - k / span + 1);
-        int32_t *rec = seg + kSegWords * sg;
+        int32_t *rec = a.seg + kSegWords * sg;
         rec[0] = parts;
         rec[1] = np_parts;
         rec[2] = k;
@@ -228,7 +247,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         parts += np_parts;
         s.split_segments += np_parts > 1 ? 1 : 0;
         s.max_parts = std::max(s.max_parts, np_parts);
-        part2_off[sg + 1] = part2_off[sg] + merge_groups(np_parts);
+        a.part2_off[sg + 1] = a.part2_off[sg] + merge_groups(np_parts);
     }
 
     // ---- per-warp records
@@ -236,7 +255,7 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
     for (int32_t kw = 0; kw < W; ++kw) {
         const int64_t ub = starts[kw];
         const int64_t ue = starts[kw + 1];
-        int32_t *ws = warp_start + kWarpStartWords * kw;
+        int32_t *ws = a.warp_start + kWarpStartWords * kw;
         ws[8] = static_cast<int32_t>(ub);
         ws[9] = static_cast<int32_t>(ue);
         ws[10] = ws[11] = 0;
@@ -246,22 +265,22 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
             }
             continue;
         }
-        while (e + 1 < n && unit_off[e + 1] <= ub) {
+        while (e + 1 < n && a.unit_off[e + 1] <= ub) {
             ++e;
         }
-        const int32_t np = npg[e];
-        const int32_t rem = static_cast<int32_t>(ub - unit_off[e]);
+        const int32_t np = a.npg[e];
+        const int32_t rem = static_cast<int32_t>(ub - a.unit_off[e]);
         ws[0] = e;
         ws[1] = rem / np;
         ws[2] = rem % np;
         ws[3] = np;
-        ws[4] = page_off[e];
+        ws[4] = a.page_off[e];
         // physical pages of the share's first three units
         int32_t ce = e, ch = ws[1], ci = ws[2];
         for (int j = 0; j < 3; ++j) {
             if (ub + j < ue) {
-                ws[5 + j] = pages[page_off[ce] + ci];
-                if (++ci == npg[ce]) {
+                ws[5 + j] = a.pages[a.page_off[ce] + ci];
+                if (++ci == a.npg[ce]) {
                     ci = 0;
                     if (++ch == G) {
                         ch = 0;
@@ -274,8 +293,73 @@ inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *p
         }
     }
     s.n_parts = parts;
-    s.n_groups = part2_off[S];
+    s.n_groups = a.part2_off[S];
+}
+
+// Fills `w` (plan_words(...) words, 16-byte aligned).  page_lists[e] points
+// at slot e's page ids, at least pos[e] / 16 + 1 of them.
+inline PlanSummary build_plan(int32_t *w, int32_t n, int32_t G, const int32_t *pos_in,
+                              const int32_t *const *page_lists, int64_t total_pages, int32_t W) {
+    PlanSummary s;
+    s.total_pages = total_pages;
+    s.total_units = total_pages * G;
+    s.cta_merge = plan_cta_merge(static_cast<int64_t>(n) * G, W);
+    const int64_t U = s.total_units;
+    const int64_t S = static_cast<int64_t>(n) * G;
+    const PlanArrays a = plan_arrays(w, n, G, pos_in, page_lists, W);
+
+    // ---- shares: the smallest budget that fits W warps (bisection)
+    const int64_t per = (U + W - 1) / W;
+    int64_t bad = kCostUnit * per - 1;  // W shares of fewer than per units cannot hold U
+    int64_t good = kCostUnit * per + kCostLeaveShared * (S + 1);
+    while (plan_cut(a.npg, G, S, good, W, nullptr) > W) {
+        good *= 2;
+    }
+    while (good - bad > 1) {
+        const int64_t mid = bad + (good - bad) / 2;
+        if (plan_cut(a.npg, G, S, mid, W, nullptr) > W) {
+            bad = mid;
+        } else {
+            good = mid;
+        }
+    }
+    s.budget = good;
+    std::vector<int32_t> starts(static_cast<size_t>(W) + 1);
+    s.shares = static_cast<int32_t>(plan_cut(a.npg, G, S, good, W, starts.data()));
+    for (int64_t k = s.shares; k <= W; ++k) {
+        starts[k] = static_cast<int32_t>(U);
+    }
+    fill_records(a, n, G, W, starts.data(), s.cta_merge ? kAttnWarps : 1, s);
     s.combine = plan_combine(s.cta_merge, s.max_parts);
+    return s;
+}
+
+// The cluster plan of a one-entry batch (plan_cluster returned C): KV head h
+// is segment h and cluster h, CTAs [h C, (h + 1) C), warps [8 h C, 8 (h + 1) C);
+// warp j of a segment of P pages holds pages [j P / 8C, (j + 1) P / 8C)
+// (at least one, as P >= 8C).  `w` holds plan_words(1, G, P, 8 G C) words.
+inline PlanSummary build_cluster_plan(int32_t *w, int32_t G, int32_t pos0,
+                                      const int32_t *page_list, int32_t C) {
+    const int32_t P = pos0 / kPageTokens + 1;
+    const int32_t per_seg = C * kAttnWarps;
+    const int32_t W = G * per_seg;
+    PlanSummary s;
+    s.total_pages = P;
+    s.total_units = static_cast<int64_t>(P) * G;
+    s.cta_merge = true;
+    s.cluster = C;
+    const PlanArrays a = plan_arrays(w, 1, G, &pos0, &page_list, W);
+    std::vector<int32_t> starts(static_cast<size_t>(W) + 1);
+    for (int32_t h = 0; h < G; ++h) {
+        for (int32_t j = 0; j < per_seg; ++j) {
+            starts[h * per_seg + j] = static_cast<int32_t>(static_cast<int64_t>(h) * P +
+                                                           static_cast<int64_t>(j) * P / per_seg);
+        }
+    }
+    starts[W] = static_cast<int32_t>(s.total_units);
+    s.shares = W;
+    fill_records(a, 1, G, W, starts.data(), kAttnWarps, s);
+    s.combine = false;
     return s;
 }
 
@@ -299,6 +383,7 @@ inline BatchView bind_plan(const int32_t *d, int32_t n, int32_t G, const PlanSum
     b.cta_merge = s.cta_merge ? 1 : 0;
     b.split_segments = s.split_segments;
     b.combine = s.combine ? 1 : 0;
+    b.cluster = s.cluster;
     return b;
 }
 

@@ -2,6 +2,9 @@
 // read from stdin, for tests/test_plan_invariants.py.
 //
 // Input, one batch per line:  G W pos_0 pos_1 ... pos_{n-1}
+//   or  cluster C G pos          (the cluster plan of one request, W = 8 G C)
+//   or  choose n G pages max_warps fit_2 fit_4 fit_8 fit_16
+//                                (prints "cluster <plan_cluster(...)>")
 // Output, per batch:
 //   plan <shares> <budget> <cta_merge> <n_parts> <n_groups> <combine>
 //   starts <u_begin of warp 0 .. W-1> <U>
@@ -20,8 +23,21 @@ int main() {
     std::string line;
     while (std::getline(std::cin, line)) {
         std::istringstream in(line);
-        int32_t G = 0, W = 0;
-        if (!(in >> G >> W)) {
+        int32_t G = 0, W = 0, C = 0;
+        if (line.rfind("choose", 0) == 0) {
+            std::string word;
+            int32_t n = 0;
+            long long pages = 0, max_warps = 0;
+            int32_t fit[5] = {0, 0, 0, 0, 0};
+            in >> word >> n >> G >> pages >> max_warps >> fit[1] >> fit[2] >> fit[3] >> fit[4];
+            std::printf("cluster %d\n", hkv::plan_cluster(n, G, pages, max_warps, fit));
+            continue;
+        }
+        if (line.rfind("cluster", 0) == 0) {
+            std::string word;
+            in >> word >> C >> G;
+            W = G * C * hkv::kAttnWarps;
+        } else if (!(in >> G >> W)) {
             continue;
         }
         std::vector<int32_t> pos;
@@ -42,7 +58,9 @@ int main() {
             total_pages += np;
         }
         std::vector<int32_t> w(hkv::plan_words(n, G, total_pages, W));
-        const hkv::PlanSummary s = hkv::build_plan(w.data(), n, G, pos.data(), ptrs.data(), total_pages, W);
+        const hkv::PlanSummary s =
+            C > 0 ? hkv::build_cluster_plan(w.data(), G, pos[0], ptrs[0], C)
+                  : hkv::build_plan(w.data(), n, G, pos.data(), ptrs.data(), total_pages, W);
         std::printf("plan %d %lld %d %d %d %d\n", s.shares, static_cast<long long>(s.budget),
                     s.cta_merge ? 1 : 0, s.n_parts, s.n_groups, s.combine ? 1 : 0);
         std::printf("starts");

@@ -261,6 +261,27 @@ def test_config1_single_slot_512_prefill_120_steps(harness):
     assert worst <= TOL
 
 
+@pytest.mark.parametrize("length", [260, 600, 1100, 16000])
+def test_single_slot_cluster_merge(harness, length):
+    """One slot alone (the batch-1 decode step, one long request): the plan
+    gives each KV head a thread-block cluster of 2, 4, 8 or 16 CTAs whose
+    partials meet in the first CTA's shared memory (plan_cluster).  Fused and
+    separate calls, four steps, against both oracle modes.  At 1,100
+    positions (69-72 pages: 8 clusters of 8 CTAs) each attention is one
+    launch: no combine launch follows."""
+    h = harness(n_layers=1, n_pages=length // 16 + 8)
+    s = h.new_slot(length + 8)
+    h.prefill(s, length, seed=31)
+    torch.cuda.synchronize()
+    before = h.eng.stats()["kernel_launches"]
+    for step in range(4):
+        check_outputs(h.decode([s], seed=600 + step, fused=step % 2 == 0))
+    launches = h.eng.stats()["kernel_launches"] - before
+    if length == 1100:
+        assert launches == 2 * 1 + 2 * 2  # fused: 1; separate: append + attention
+    h.check_cache(s)
+
+
 def test_batched_permuted_pages_many_slots(harness):
     """16 slots, contexts drawn in [256, 4096], permuted physical pages."""
     import synth

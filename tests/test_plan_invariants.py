@@ -12,7 +12,11 @@ prints its descriptor) and checked against a restatement here:
 
 The plan also chooses where the split partials are merged: by a combine
 launch after the attention grid for CTA-merged segments of at most 32
-partials, else inside the launch.
+partials, else inside the launch.  For one long request it may instead give
+every KV head a thread-block cluster of C CTAs (plan_cluster), whose CTA
+partials meet in the first CTA's shared memory: checked here are the choice
+of C and that cluster h covers exactly head h's pages, evenly, one CTA
+partial per cluster rank.
 
 Then every warp is walked the way attention_kernel does, with the two-level
 merge (a segment with more than 16 partials is merged in groups of
@@ -71,6 +75,7 @@ def plan_dump(tmp_path_factory):
                               n_groups=n_groups, starts=starts, segs=segs, part2=part2,
                               warps=[tuple(warps[k:k + 3]) for k in range(0, len(warps), 3)]))
         return plans
+    run.exe = exe
     return run
 
 
@@ -298,3 +303,49 @@ def test_cta_merge_rule():
     assert restate([2048], 1, 148 * WPC)["cta_merge"]
     assert not restate([100] * 16, 8, 148 * WPC)["cta_merge"]
     assert not restate([600] * 32, 8, 148 * WPC)["cta_merge"]
+
+
+def raw_lines(plan_dump, text):
+    return subprocess.run([str(plan_dump.exe)], input=text, capture_output=True, text=True,
+                          check=True, timeout=60).stdout.splitlines()
+
+
+@pytest.mark.parametrize("C,G,pos", [(16, 8, 32760), (8, 8, 1040), (8, 8, 1023), (2, 8, 300),
+                                     (16, 1, 5000), (4, 2, 16 * 32 - 1)])
+def test_cluster_plan_covers_each_head_with_one_cluster(plan_dump, C, G, pos):
+    out = raw_lines(plan_dump, f"cluster {C} {G} {pos}\n")
+    P = pos // 16 + 1
+    W = G * C * WPC
+    shares, budget, cta, n_parts, n_groups, combine = map(int, out[0].split()[1:])
+    assert (cta, combine, n_groups, n_parts, shares) == (1, 0, 0, G * C, W)
+    starts = list(map(int, out[1].split()[1:]))
+    assert len(starts) == W + 1 and starts[-1] == P * G
+    segs = [tuple(map(int, out[2 + h].split()[1:])) for h in range(G)]
+    for h in range(G):
+        # cluster h = CTAs [h C, (h + 1) C): its warps hold head h's pages, in order
+        assert segs[h] == (h * C, C, h * C * WPC, (h + 1) * C * WPC - 1)
+        sizes = [starts[k + 1] - starts[k] for k in range(h * C * WPC, (h + 1) * C * WPC)]
+        assert starts[h * C * WPC] == h * P and sum(sizes) == P
+        assert min(sizes) >= 1 and max(sizes) - min(sizes) <= 1
+    warps = list(map(int, out[3 + G].split()[1:]))
+    triples = [tuple(warps[k:k + 3]) for k in range(0, len(warps), 3)]
+    assert len(triples) == W
+    for k, (e, h, i) in enumerate(triples):
+        assert (e, h, i) == (0, k // (C * WPC), starts[k] - (k // (C * WPC)) * P)
+
+
+def test_cluster_choice(plan_dump):
+    # fit = clusters of 2, 4, 8, 16 CTAs resident at once (B200: one CTA per SM)
+    cases = [
+        ((1, 8, 2048, 1184, 74, 37, 18, 8), 16),  # one request near 32k: 8 x 16 CTAs
+        ((1, 8, 2048, 1184, 74, 37, 18, 7), 0),   # 16-CTA clusters in two waves: stream-K plan
+        ((1, 8, 66, 1184, 74, 37, 18, 8), 8),     # the batch-1 step at 1,040 positions: 8 x 8
+        ((1, 8, 63, 1184, 74, 37, 18, 8), 0),     # 63 pages: 4-CTA clusters would use 256 of
+                                                  # the 504 warps the stream-K plan uses
+        ((1, 4, 2048, 1184, 74, 37, 18, 8), 0),   # 64 CTAs for 4 heads: under 3/4 of the grid
+        ((2, 8, 2048, 1184, 74, 37, 18, 8), 0),   # two requests: stream-K plan
+        ((1, 8, 10, 1184, 74, 37, 18, 8), 0),     # short: one partial per warp, no CTA merge
+    ]
+    text = "".join("choose " + " ".join(map(str, a)) + "\n" for a, _ in cases)
+    got = [int(line.split()[1]) for line in raw_lines(plan_dump, text)]
+    assert got == [want for _, want in cases]
