@@ -107,8 +107,9 @@ typedef struct hkv_pool_stats {
 typedef enum hkv_kernel_id {
     HKV_KERNEL_APPEND = 0,  /* hkv_append, hkv_rope_append, hkv_rope_append_range */
     HKV_KERNEL_ATTN = 1,    /* hkv_decode_attn                                    */
-    HKV_KERNEL_COMBINE = 2, /* reserved: the split merge runs inside the attention
-                               kernels, so nothing is recorded under this id    */
+    HKV_KERNEL_COMBINE = 2, /* reserved: nothing is recorded under this id; the
+                               combine launch that follows some attention launches
+                               is timed with them (ATTN or STEP)              */
     HKV_KERNEL_GATHER = 3,  /* hkv_gather                                         */
     HKV_KERNEL_STEP = 4,    /* hkv_decode_step (append + attention, one launch)   */
     HKV_KERNEL_GEMV = 5,    /* Q4_K projections (hkv_q4k_*, hkv_backbone_decode)  */
