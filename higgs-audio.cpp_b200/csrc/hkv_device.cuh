@@ -64,8 +64,8 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // --------------------------------------------------------------- bulk copy
-// 1-D bulk copy global -> this CTA's shared memory (no tensor map, no
-// multicast); completion is counted in transaction bytes on `bar`.
+// 1-D bulk copy global -> this CTA's shared memory only (no tensor map);
+// completion is counted in transaction bytes on `bar`.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
                                           uint64_t policy) {
     asm volatile(
