@@ -772,8 +772,27 @@ __device__ __forceinline__ void store_row(const GemvParams &p, float *res, int r
 // whose partial sums are added in a fixed order after one consumer barrier.
 template <int MODE, int NB>
 __global__ void __launch_bounds__(consumer_warps(MODE, NB) * 32 + 32, NB > 1 && MODE != kQkv ? 1 : 2)
-    gemv_kernel(GemvParams p) {
+    gemv_kernel(GemvParams pin) {
     extern __shared__ __align__(128) unsigned char smem[];
+    // Several vectors: one launch covers ceil(n / NB) groups of NB vectors,
+    // grid_ctas CTAs per group; a CTA computes for its group exactly what a
+    // launch of those vectors alone computes (the same rows, tiles and sums).
+    GemvParams p = pin;
+    int cta = static_cast<int>(blockIdx.x);
+    if (NB > 1) {
+        const int grp = cta / pin.grid_ctas;
+        cta -= grp * pin.grid_ctas;
+        const int e0 = grp * NB;
+        p.n = min(NB, pin.n - e0);
+        p.x = pin.x + static_cast<size_t>(e0) * pin.cols;
+        if (pin.residual != nullptr) p.residual = pin.residual + static_cast<size_t>(e0) * pin.rows;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            if (pin.y[k] != nullptr) {
+                p.y[k] = pin.y[k] + static_cast<size_t>(e0) * (MODE == kQkv ? pin.y_rows[k] : pin.rows);
+            }
+        }
+    }
     constexpr int kMats = MODE == kSwiglu ? 2 : 1;
     constexpr int NT = NB > 1 ? NB / 8 : 1;  // mma n-tiles of 8 vectors
     static_assert(NB == 1 || NB % 8 == 0, "the tensor-core kernel takes 8 vectors per n-tile");
@@ -783,7 +802,7 @@ __global__ void __launch_bounds__(consumer_warps(MODE, NB) * 32 + 32, NB > 1 && 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int kW = consumer_warps(MODE, NB);  // consumer warps; warp kW is the producer
     const bool producer = warp == kW;
-    const int row0 = blockIdx.x * p.rows_per_cta;
+    const int row0 = cta * p.rows_per_cta;
     const int nrows = max(0, min(p.rows, row0 + p.rows_per_cta) - row0);
     const int R = p.chunk_rows;
     const int n_stages = p.n_stages;
@@ -800,7 +819,7 @@ __global__ void __launch_bounds__(consumer_warps(MODE, NB) * 32 + 32, NB > 1 && 
     int m = 0, mrow0 = row0;
     if (MODE == kQkv) {
         m = row0 < p.row_end[0] ? 0 : (row0 < p.row_end[1] ? 1 : 2);
-        mrow0 = row0 - (m == 0 ? 0 : p.row_end[m - 1]);
+        mrow0 = row0 - (m == 0 ? 0 : (m == 1 ? p.row_end[0] : p.row_end[1]));
     }
     if (tid == 0) {
         for (int c = 0; c < (NB > 1 ? n_chunks : n_stages); ++c) mbar_init(full_of(c), 1);
@@ -828,7 +847,8 @@ __global__ void __launch_bounds__(consumer_warps(MODE, NB) * 32 + 32, NB > 1 && 
         const uint8_t *wbase[kMats];
 #pragma unroll
         for (int k = 0; k < kMats; ++k) {
-            wbase[k] = p.w[MODE == kSwiglu ? k : m] + static_cast<size_t>(mrow0) * row_bytes;
+            const int wm = MODE == kSwiglu ? k : m;  // selected, not indexed: p stays in registers
+            wbase[k] = (wm == 0 ? p.w[0] : (wm == 1 ? p.w[1] : p.w[2])) + static_cast<size_t>(mrow0) * row_bytes;
         }
         int issued = 0;
         // chunk c into its stage (lane 0)
@@ -1195,12 +1215,17 @@ __global__ void __launch_bounds__(consumer_warps(MODE, NB) * 32 + 32, NB > 1 && 
         __syncthreads();
         if (!bad) {
             const int dim0 = static_cast<int>(cl.block_rank()) * kQkvRows;
+            // matrix m's output and norm, selected without indexing p's arrays
+            // by a runtime value (which would move p to local memory)
+            float *const ym = m == 0 ? p.y[0] : (m == 1 ? p.y[1] : p.y[2]);
+            const int yrows = m == 0 ? p.y_rows[0] : (m == 1 ? p.y_rows[1] : p.y_rows[2]);
+            const float *const hn = m == 0 ? p.head_norm[0] : p.head_norm[1];
             for (int i = tid; i < p.n * kQkvRows; i += static_cast<int>(blockDim.x)) {
                 const int e = i / kQkvRows, r = i % kQkvRows;
                 if (r < nrows) {
                     float v = res[e * kQkvRows + r];
-                    if (normed) v = __fmul_rn(__fmul_rn(v, scale_s[e]), p.head_norm[m][dim0 + r]);
-                    p.y[m][static_cast<size_t>(e) * p.y_rows[m] + mrow0 + r] = v;
+                    if (normed) v = __fmul_rn(__fmul_rn(v, scale_s[e]), hn[dim0 + r]);
+                    ym[static_cast<size_t>(e) * yrows + mrow0 + r] = v;
                 }
             }
         }
@@ -1423,7 +1448,9 @@ cudaError_t launch_one(const GemvParams &p, cudaStream_t stream) {
         }
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(NB > 1 ? p.grid_ctas : (p.rows + p.rows_per_cta - 1) / p.rows_per_cta));
+    // several vectors: grid_ctas CTAs per group of NB vectors, all groups in one grid
+    cfg.gridDim = dim3(static_cast<unsigned>(NB > 1 ? p.grid_ctas * ((p.n + NB - 1) / NB)
+                                                    : (p.rows + p.rows_per_cta - 1) / p.rows_per_cta));
     cfg.blockDim = dim3(consumer_warps(MODE, NB) * 32 + 32);  // consumer warps + one producer warp
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -1628,23 +1655,18 @@ cudaError_t launch_gemv(GemvParams p, cudaStream_t stream, int64_t *launches = n
     if (p.n > 1 || p.tensor != 0) {
         // 16 vectors per launch where their image fits beside the weights
         // (the same tiles, slices and sums as 8 per launch: bit-identical)
+        // (all groups of 16 or 8 vectors in one grid: gemv_kernel)
         GemvParams t2 = p;
         if (p.n > kMaxVec && plan_tiles(t2, MODE, dev, kMaxVec2)) {
-            for (int e0 = 0; e0 < p.n; e0 += kMaxVec2) {
-                st = launch_one<MODE, kMaxVec2>(vector_slice(t2, MODE, e0, std::min(kMaxVec2, p.n - e0)), stream);
-                if (st != cudaSuccess) return st;
-                if (launches != nullptr) ++*launches;
-            }
-            return cudaSuccess;
+            st = launch_one<MODE, kMaxVec2>(t2, stream);
+            if (st == cudaSuccess && launches != nullptr) ++*launches;
+            return st;
         }
         GemvParams t = p;
         if (plan_tiles(t, MODE, dev, kMaxVec)) {
-            for (int e0 = 0; e0 < p.n; e0 += kMaxVec) {
-                st = launch_one<MODE, kMaxVec>(vector_slice(t, MODE, e0, std::min(kMaxVec, p.n - e0)), stream);
-                if (st != cudaSuccess) return st;
-                if (launches != nullptr) ++*launches;
-            }
-            return cudaSuccess;
+            st = launch_one<MODE, kMaxVec>(t, stream);
+            if (st == cudaSuccess && launches != nullptr) ++*launches;
+            return st;
         }
     }
     GemvParams one = p;  // one vector per launch

@@ -61,7 +61,7 @@ def test_encoder_round_trip(hkv_lib, oracle):
     (2560, 9728, 1, False, True, False),    # ffn_down + residual
     (8208, 2560, 1, True, False, False),    # output head after output_norm
     (4096, 2560, 3, True, False, False),    # several vectors: tensor cores
-    (300, 2560, 9, False, True, False),     # rows not a multiple of 16, n > 8 (two launches)
+    (300, 2560, 9, False, True, False),     # rows not a multiple of 16, n > 8 (two vector groups)
     (2560, 4096, 1, False, True, True),     # o_proj, one vector on the tensor cores
     (2560, 9728, 1, False, True, True),     # ffn_down (rows in flight beside a 9728-wide image)
     (8208, 2560, 16, True, False, False),   # the output head at batch 16
@@ -69,7 +69,7 @@ def test_encoder_round_trip(hkv_lib, oracle):
     (40, 256, 3, True, True, False),        # one block per row, one partial tile
     (1000, 512, 16, False, True, False),    # 16 vectors in one launch, residual
     (130, 16384, 5, False, False, False),   # the widest rows, CTAs without rows
-    (2560, 9728, 13, False, True, False),   # down: 8 + 5 vectors (two launches)
+    (2560, 9728, 13, False, True, False),   # down: 8 + 5 vectors (two groups, one launch)
     (2560, 4096, 17, False, True, False),   # o_proj: 16 + 1 vectors
     (2560, 9728, 17, False, True, False),   # down: 8 + 8 + 1 vectors
 ])
@@ -152,7 +152,7 @@ def test_qkv_head_norm_matches_oracle(hkv_lib, oracle, n, tc):
                                              (2560, 9728, False)])
 def test_tensor_core_results_do_not_depend_on_batch(hkv_lib, rows, cols, swiglu):
     """On the tensor cores a vector's result is the same bits alone (n = 1)
-    or among 4 or 11 others (one and two launches): the tiles, block slices
+    or among 4 or 11 others (one and two vector groups): the tiles, block slices
     and summation order depend on the matrix shape only."""
     import hkv
     _, b = q4k_matrix(hkv, rows, cols, 70 + rows)
