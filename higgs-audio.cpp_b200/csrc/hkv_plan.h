@@ -149,9 +149,10 @@ inline size_t plan_words(int64_t n, int64_t G, int64_t total_pages, int64_t W) {
 // batch-1 decode step): the largest C of 16, 8, 4, 2 CTAs per cluster such
 // that every KV head's cluster runs at once (fit[i] = clusters of 2^i CTAs
 // that can be resident together), every warp gets at least one page, and the
-// G * C CTAs are at least 3/4 of the warps the stream-K plan would use;
-// and only where that plan would pre-merge per CTA (long segments).  0: no
-// clusters (the stream-K plan).
+// cluster plan's G * C * kAttnWarps warps are at least 3/4 of the warps the
+// stream-K plan would use (fewer SMs would cost bandwidth); and only where
+// that plan would pre-merge per CTA (long segments).  0: no clusters (the
+// stream-K plan).
 inline int32_t plan_cluster(int32_t n, int32_t G, int64_t npages, int64_t max_warps,
                             const int32_t (&fit)[5]) {
     if (n != 1 || G <= 0) {
